@@ -1,0 +1,341 @@
+#!/usr/bin/env python
+"""Benchmark of the PISA hot path: pyramid -> block selection -> selected attention.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload prefill32k] [--impl ours|reference]
+
+One step = one causal prefill of one synthetic sequence per GPU (BASELINE
+configs[1] by default: B=1, N=32768, Hq=32, Hkv=8, D=128, block 64, branching
+4, top-K 32, forced first + current block, LSE scoring, bf16): key pyramid,
+coarse-to-fine routing with leaf scoring and top-K, then attention over the
+selected blocks.  Multi-GPU runs (torchrun) give each rank its own sequence
+(weak scaling, no collective on the data path).  Prints one JSON line on rank 0.
+
+The reference arm (--impl reference) times the CPU restatement of the
+reference algorithm on a bounded sample of query rows on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--workload", default="prefill32k")
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-rows", type=int, default=12, help="sampled rows per CPU worker")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.index), "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as fh:
+            for line in fh:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace('.', '').isdigit())}
+
+
+# ---------------------------------------------------------------------------
+# the reference arm: CPU restatement on a bounded sample
+# ---------------------------------------------------------------------------
+def run_reference(args, workload):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    sys.path.insert(0, str(ROOT / "oracle"))
+    from cpu_sample import time_sample
+
+    samples = []
+    for _ in range(args.warmup):
+        time_sample(workload, rows_per_worker=2)
+    for _ in range(max(1, min(args.steps, 3))):
+        samples.append(time_sample(workload, rows_per_worker=args.cpu_rows))
+    value = statistics.median(s["value"] for s in samples)
+    base = samples[0]
+    line = {
+        "impl": "reference",
+        "metric": "prefill tokens/s (select+attend)",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": args.gpus,
+        "steps": len(samples),
+        "warmup": args.warmup,
+        "ms_per_step": 1000.0 * workload.tokens / value,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": workload.dtype,
+        "data": "synthetic",
+        "config": {"workload": workload.name, **workload.as_dict()},
+        "cpu_baseline": {k: base[k] for k in ("unit", "cores", "kind", "sample")} | {"value": value},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def main():
+    args = parse_args()
+    from nlogn_pisa_b200.workloads import WORKLOADS
+
+    workload = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return run_reference(args, workload)
+
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    import nlogn_pisa_b200 as P
+    from nlogn_pisa_b200 import _lib
+    from nlogn_pisa_b200.selection import _c_array, level_sizes, routing_geometry
+    from nlogn_pisa_b200.workloads import make_inputs
+
+    w = workload
+    q, k, v = make_inputs(w, device, seed=w.seed + rank)
+    B, N, Hq, H, D = w.batch, w.tokens, w.q_heads, w.kv_heads, w.head_dim
+    G, C, K, br = Hq // H, w.block_size, w.topk, w.branching
+    code = _lib.dtype_code(q)
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream(device)
+    sptr = _lib.stream_of(device)
+    leaves = -(-N // C)
+    top, first_width = routing_geometry(leaves, K, br)
+    sizes = level_sizes(leaves, br, top + 1)
+    offsets = [sum(sizes[:i]) for i in range(len(sizes))]
+    storage = torch.empty((B, sum(sizes), H, D), dtype=q.dtype, device=device)
+    ids = torch.empty((B, N, H, K), dtype=torch.int64, device=device)
+    out = torch.empty((B, N, Hq, D), dtype=q.dtype, device=device)
+    lse = torch.empty((B, N, Hq), dtype=torch.float32, device=device)
+    method = _lib.METHODS[w.method]
+    scale = D ** -0.5
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    launches_per_step = len(sizes) + 1 + 1
+
+    def pyramid():
+        _lib.check(lib.pisa_build_pyramid(
+            _lib.ptr(k), code, B, N, H, D, *k.stride()[:3], C, br, len(sizes), _lib.ptr(storage),
+            storage.stride(0), _c_array(offsets), sptr))
+
+    def select():
+        _lib.check(lib.pisa_select_blocks(
+            _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3], _lib.ptr(storage),
+            storage.stride(0), _c_array(offsets), _c_array(sizes), len(sizes), None, 0, code, B, N,
+            Hq, H, D, N, method, C, br, K, int(w.force_first), w.force_recent, top, first_width,
+            _lib.SCHEDULES["grouped"], _lib.ptr(ids), None, 0, sptr))
+
+    def attend():
+        _lib.check(lib.pisa_sparse_attn_fwd(
+            _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3], _lib.ptr(v), *v.stride()[:3],
+            _lib.ptr(ids), 8, None, 0, code, B, N, Hq, H, D, D, N, K, C, float(scale), 1,
+            _lib.ptr(out), _lib.ptr(lse), sptr))
+
+    stages = (("pyramid", pyramid), ("select", select), ("attention", attend))
+    for _ in range(max(args.warmup, 3)):
+        for _, fn in stages:
+            fn()
+    torch.cuda.synchronize()
+
+    # algorithmic work of one step (outside the timed region)
+    pos = torch.arange(N, device=device)
+    valid_ids = (ids >= 0) & (ids * C <= pos[None, :, None, None])
+    key_count = torch.clamp(torch.minimum(pos[None, :, None, None] + 1, torch.full_like(ids, N)) - ids * C, 0, C)
+    attn_keys = torch.where(valid_ids, key_count, 0).sum().item()
+    attn_flops = attn_keys * G * (2 * D + 2 * D)
+    leaf = pos // C
+    valid_leaves = leaf + 1
+    cand = torch.full_like(leaf, br * K)
+    forced = 1 + (leaf > 0).long()          # first block + current block (force_recent = 1)
+    invalid = (br - 1) - (leaf % br)        # siblings of the current leaf past the causal edge
+    scored = torch.where(valid_leaves > K, cand - forced - invalid, 0)
+    leaf_flops = scored.sum().item() * H * B * 2 * D * G * C
+    pyramid_bytes = (B * N * H * D + B * sum(sizes) * H * D) * q.element_size()
+
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)] for _ in range(args.steps)]
+    for step in range(args.steps):
+        flush.zero_()
+        ev = events[step]
+        ev[0].record(stream)
+        for i, (_, fn) in enumerate(stages):
+            fn()
+            ev[i + 1].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clock_info = clocks.stop()
+    stage_ms = [sum(ev[i].elapsed_time(ev[i + 1]) for ev in events) / args.steps for i in range(len(stages))]
+    step_ms = sum(ev[0].elapsed_time(ev[-1]) for ev in events) / args.steps
+    times = torch.tensor([step_ms] + stage_ms, device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    step_ms = times[0].item()
+    stage_ms = times[1:].tolist()
+    value = world * B * N / (step_ms / 1000.0)
+
+    # end to end through the public API with pinned host buffers
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+
+    def e2e_step():
+        dq, dk, dv = (x.to(device, non_blocking=True) for x in (hq, hk, hv))
+        sel = P.select_blocks(dq, dk, method=w.method, block_size=C, topk=K, force_first=w.force_first,
+                              force_recent=w.force_recent, branching=br)
+        o = P.sparse_attention(dq, dk, dv, sel, block_size=C)
+        hout.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e_start.elapsed_time(e_end) / args.steps], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = e2e_ms.item()
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
+    d2h = hout.numel() * hout.element_size()
+
+    peaks = {}
+    peaks_file = ROOT / "MEASURED_PEAKS.json"
+    if peaks_file.exists():
+        peaks = json.loads(peaks_file.read_text())
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    tensor = peaks.get("bf16_tflops", 1590.0)
+    src = "measured" if peaks else "fallback"
+    stage_work = {
+        "pyramid": ("hbm", pyramid_bytes / 1e9, hbm, "GB/s"),
+        "select": ("tensor", leaf_flops / 1e12, tensor, "TFLOP/s"),
+        "attention": ("tensor", attn_flops / 1e12, tensor, "TFLOP/s"),
+    }
+    stage_report = {}
+    for (name, _), ms in zip(stages, stage_ms):
+        bound, amount, peak, unit = stage_work[name]
+        achieved = amount / (ms / 1000.0)
+        stage_report[name] = {"ms": ms, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                              "frac": achieved / peak}
+    dominant = max(stage_report, key=lambda n: stage_report[n]["ms"])
+    dom = stage_report[dominant]
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            sys.path.insert(0, str(ROOT / "oracle"))
+            from cpu_sample import time_sample
+
+            cpu = time_sample(w, rows_per_worker=args.cpu_rows)
+            cpu.pop("seconds", None)
+        line = {
+            "metric": "prefill tokens/s (select+attend)",
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(args.warmup, 3),
+            "ms_per_step": step_ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": w.dtype,
+            "data": "synthetic",
+            "config": {
+                "workload": w.name, "batch_per_gpu": B, "tokens": N, "q_heads": Hq, "kv_heads": H,
+                "head_dim": D, "block_size": C, "branching": br, "topk": K, "method": w.method,
+                "forced": "first + current block", "schedule": "grouped",
+                "l2": "flushed between timed steps (256 MiB write outside the events)",
+                "parallelism": f"dp{world} (one sequence per GPU, no collective)",
+            },
+            "roofline": {"kernel": dominant, "bound": dom["bound"], "achieved": dom["achieved"],
+                         "peak": dom["peak"], "unit": dom["unit"], "frac": dom["frac"], "traffic": None,
+                         "peak_source": src},
+            "stages": stage_report,
+            "cpu_baseline": cpu,
+            "e2e": {"value": world * B * N / (e2e_ms / 1000.0), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clock_info,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,179 @@
+/*
+ * pisa_b200.h -- C ABI of the B200 (sm_100a) PISA hot path.
+ *
+ * PISA's hot path is hierarchical log-sum-exp block selection over a
+ * mean-pooled key pyramid followed by attention over the selected key blocks.
+ * Each entry point below replaces one operator of the reference Python
+ * package `pisa` (Aphelios-Tang/NlogN_PISA; paths relative to that project).
+ *
+ * Conventions
+ *  - Tensors are [batch, tokens, heads, dim] with a contiguous last dim and
+ *    16-byte aligned rows; strides are in ELEMENTS.  Key/value tensors may be
+ *    strided in batch and tokens (the reference's PyramidCache views).
+ *  - All pointers are device pointers unless marked "host".
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call is
+ *    asynchronous on that stream and never synchronises the host.
+ *  - The return value is a status code (PISA_OK or a PISA_ERR_*); nothing
+ *    throws across the ABI.  pisa_last_error() describes the last failure of
+ *    the calling thread.
+ *  - Workspaces are caller-allocated; the *_workspace_bytes functions give the
+ *    size.  The library allocates no device memory of its own.
+ */
+#ifndef PISA_B200_H
+#define PISA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define PISA_OK 0
+#define PISA_ERR_INVALID 1     /* argument violates the operator contract (Python: ValueError) */
+#define PISA_ERR_UNSUPPORTED 2 /* outside the GPU kernels' envelope (Python: ValueError) */
+#define PISA_ERR_CUDA 3        /* CUDA launch or runtime error (Python: RuntimeError) */
+#define PISA_ERR_TIMEOUT 4     /* a bounded device-side wait expired (Python: RuntimeError) */
+
+/* ---- element types (the reference's GPU path accepts fp16, bf16 and fp32) ---- */
+#define PISA_F32 0
+#define PISA_BF16 1
+#define PISA_F16 2
+
+/* ---- scoring methods (pisa1 = first order, pisa2 = second order, pisa = LSE) ---- */
+#define PISA_METHOD_PISA1 0
+#define PISA_METHOD_PISA2 1
+#define PISA_METHOD_PISA 2
+
+/* ---- routing schedules (top_k_pyramid.py:16-24 `routing_schedule`) ---- */
+#define PISA_SCHEDULE_GROUPED 0 /* coarse router -> grouped leaf scoring -> final top-K */
+#define PISA_SCHEDULE_FUSED 1   /* one kernel: coarse levels, leaf scoring and top-K */
+
+typedef void *pisa_stream_t; /* cudaStream_t */
+
+#if defined(__GNUC__)
+#define PISA_API __attribute__((visibility("default")))
+#else
+#define PISA_API
+#endif
+
+/* Library version (major*10000 + minor*100 + patch). */
+PISA_API int pisa_version(void);
+
+/* Text of the last error raised on the calling host thread ("" if none). */
+PISA_API const char *pisa_last_error(void);
+
+/*
+ * Mean of the valid tokens of every `size`-token block; a partial tail block
+ * divides by its real count.  Accumulates in fp32 and rounds to `dtype`.
+ * Replaces mean_pool / torch_mean_pool / pool_kernel
+ *   (pisa/pisa/ops/compress/mean_pooling/mean_pooling.py:8-42,
+ *    mean_pooling_torch.py:7-14, mean_pooling_triton.py:8-51).
+ * out: [B, ceil(N/size), H, D] contiguous.
+ */
+PISA_API int pisa_mean_pool(const void *keys, int dtype, int64_t B, int64_t N, int64_t H, int64_t D,
+                   int64_t key_sb, int64_t key_st, int64_t key_sh, int64_t size, void *out,
+                   pisa_stream_t stream);
+
+/*
+ * Key pyramid: level 0 = mean_pool(keys, block_size), level l+1 =
+ * mean_pool(level l, branching), for levels 0..num_levels-1.  All levels go
+ * to one storage [B, total, H, D] (node stride H*D, batch stride storage_sb)
+ * at node offsets level_offsets[l] (host array) -- the PyramidCache layout
+ * (xmixers/xmixers/utils/attention_cache.py:102-118).
+ * Replaces build_pyramid (mean_pooling.py:45-52) and the level concatenation
+ * of select_cuda (top_k_pyramid_triton.py:348-359).  branching 2 is the
+ * reference; 4 is this library's extension.
+ */
+PISA_API int pisa_build_pyramid(const void *keys, int dtype, int64_t B, int64_t N, int64_t H, int64_t D,
+                       int64_t key_sb, int64_t key_st, int64_t key_sh, int64_t block_size,
+                       int64_t branching, int64_t num_levels, void *storage, int64_t storage_sb,
+                       const int64_t *level_offsets, pisa_stream_t stream);
+
+/*
+ * Recompute the pyramid nodes that depend on key tokens [first_token, N):
+ * the leaves they touch and those leaves' ancestors, as
+ * PyramidCache.append (attention_cache.py:120-140) does after appending keys.
+ * Levels 0..num_levels-1 must already hold the pyramid of keys[:, :first_token].
+ */
+PISA_API int pisa_pyramid_update(const void *keys, int dtype, int64_t B, int64_t N, int64_t H, int64_t D,
+                        int64_t key_sb, int64_t key_st, int64_t key_sh, int64_t block_size,
+                        int64_t branching, int64_t num_levels, void *storage, int64_t storage_sb,
+                        const int64_t *level_offsets, int64_t first_token, pisa_stream_t stream);
+
+/*
+ * Block selection: ids [B, Tq, H, topk] int64 in network-rank order, -1
+ * padded.  Replaces select_blocks/_select_unpacked -> select_cuda
+ *   (pisa/pisa/ops/flash_sparse_attn/top_k_pyramid/top_k_pyramid.py:11-122,
+ *    top_k_pyramid_triton.py:311-447) with the equations of the torch
+ *    reference (top_k_pyramid_torch.py:6-177).
+ * q: [B,Tq,Hq,D]; keys: [B,N,H,D]; Hq = G*H.
+ * summary: pyramid storage as written by pisa_build_pyramid with levels
+ *   0..top (level_offsets/level_sizes: host arrays of num_levels >= top+1
+ *   entries), or NULL to build it inside `workspace`.
+ * positions: device int64 [B,Tq] absolute query positions, or NULL for
+ *   position = position_offset + token (validation.py:38-47).
+ * top, first_width: routing geometry (top_k_pyramid_torch.py:124-133).
+ * schedule: PISA_SCHEDULE_GROUPED or PISA_SCHEDULE_FUSED.
+ * Constraints (as the reference's GPU path, top_k_pyramid_triton.py:327-335):
+ *   block_size a power of two >= 16, topk in {8,16,32,64}, D % 8 == 0,
+ *   D <= 256, branching in {2,4}, G <= 32.
+ */
+PISA_API int pisa_select_blocks(const void *q, int64_t q_sb, int64_t q_st, int64_t q_sh, const void *keys,
+                       int64_t key_sb, int64_t key_st, int64_t key_sh, const void *summary,
+                       int64_t summary_sb, const int64_t *level_offsets,
+                       const int64_t *level_sizes, int64_t num_levels, const int64_t *positions,
+                       int64_t position_offset, int dtype, int64_t B, int64_t Tq, int64_t Hq,
+                       int64_t H, int64_t D, int64_t N, int method, int64_t block_size,
+                       int64_t branching, int64_t topk, int force_first, int64_t force_recent,
+                       int64_t top, int64_t first_width, int schedule, int64_t *out_ids,
+                       void *workspace, int64_t workspace_bytes, pisa_stream_t stream);
+
+/* Workspace bytes for pisa_select_blocks (with summary == NULL when build_summary != 0). */
+PISA_API int64_t pisa_select_workspace_bytes(int64_t B, int64_t Tq, int64_t H, int64_t D, int64_t N,
+                                    int dtype, int64_t block_size, int64_t branching,
+                                    int64_t topk, int64_t top, int64_t first_width, int schedule,
+                                    int build_summary);
+
+/*
+ * Attention over selected key blocks with one softmax over their union
+ * (causal inside blocks), forward.  Replaces sparse_attention's CUDA branch
+ * (pisa/pisa/ops/flash_sparse_attn/sparse_attn/sparse_attn.py:10-61 ->
+ * sparse_attn_fla.py:22-71 / decode_triton.py:82-115) with the semantics of
+ * sparse_attn_torch.py:6-35.
+ * indices: [B,Tq,H,S] int32 (index_bytes 4) or int64 (8), contiguous; ids < 0
+ *   or past the keys are skipped; duplicates count once per occurrence.
+ * out: [B,Tq,Hq,Dv] in dtype (contiguous); lse: [B,Tq,Hq] fp32 natural-log
+ *   log-sum-exp of the scaled logits (-inf for rows without a visible key,
+ *   whose output is 0).  lse may be NULL.
+ */
+PISA_API int pisa_sparse_attn_fwd(const void *q, int64_t q_sb, int64_t q_st, int64_t q_sh, const void *k,
+                         int64_t k_sb, int64_t k_st, int64_t k_sh, const void *v, int64_t v_sb,
+                         int64_t v_st, int64_t v_sh, const void *indices, int index_bytes,
+                         const int64_t *positions, int64_t position_offset, int dtype, int64_t B,
+                         int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t Dv, int64_t N,
+                         int64_t S, int64_t block_size, float scale, int causal, void *out,
+                         float *lse, pisa_stream_t stream);
+
+/*
+ * Backward of pisa_sparse_attn_fwd: dq [B,Tq,Hq,D], dk/dv [B,N,H,D|Dv] in
+ * dtype, contiguous.  Gradient of the reference's autograd through
+ * sparse_attn_torch.py:6-35.  q/k/v/out/dout/dq/dk/dv contiguous.
+ * workspace: pisa_sparse_attn_bwd_workspace_bytes(...) bytes.
+ */
+PISA_API int pisa_sparse_attn_bwd(const void *q, const void *k, const void *v, const void *out,
+                         const void *dout, const float *lse, const void *indices, int index_bytes,
+                         const int64_t *positions, int64_t position_offset, int dtype, int64_t B,
+                         int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t Dv, int64_t N,
+                         int64_t S, int64_t block_size, float scale, int causal, void *dq,
+                         void *dk, void *dv, void *workspace, int64_t workspace_bytes,
+                         pisa_stream_t stream);
+
+PISA_API int64_t pisa_sparse_attn_bwd_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H,
+                                             int64_t D, int64_t Dv, int64_t N);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PISA_B200_H */

@@ -1,0 +1,87 @@
+"""ctypes binding of libpisa_b200.so (the C ABI declared in include/pisa_b200.h).
+
+The CUDA library is the only compute path: importing an operator without the
+built library raises ImportError, and every call on a CPU tensor raises
+ValueError.  There is no CPU or Triton fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().with_name("libpisa_b200.so")
+
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT = 0, 1, 2, 3, 4
+F32, BF16, F16 = 0, 1, 2
+METHODS = {"pisa1": 0, "pisa2": 1, "pisa": 2}
+SCHEDULES = {"grouped": 0, "fused": 1}
+DTYPES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_L = ctypes.c_int64
+_F = ctypes.c_float
+
+# name -> (restype, argtypes); one entry per function of include/pisa_b200.h
+SIGNATURES = {
+    "pisa_version": (_I, []),
+    "pisa_last_error": (ctypes.c_char_p, []),
+    "pisa_mean_pool": (_I, [_P, _I, _L, _L, _L, _L, _L, _L, _L, _L, _P, _P]),
+    "pisa_build_pyramid": (_I, [_P, _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _L, _P, _L, _P, _P]),
+    "pisa_pyramid_update": (_I, [_P, _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _L, _P, _L, _P, _L, _P]),
+    "pisa_select_blocks": (_I, [_P, _L, _L, _L, _P, _L, _L, _L, _P, _L, _P, _P, _L, _P, _L, _I,
+                                _L, _L, _L, _L, _L, _L, _I, _L, _L, _L, _I, _L, _L, _L, _I, _P,
+                                _P, _L, _P]),
+    "pisa_select_workspace_bytes": (_L, [_L, _L, _L, _L, _L, _I, _L, _L, _L, _L, _L, _I, _I]),
+    "pisa_sparse_attn_fwd": (_I, [_P, _L, _L, _L, _P, _L, _L, _L, _P, _L, _L, _L, _P, _I, _P, _L,
+                                  _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _F, _I, _P, _P, _P]),
+    "pisa_sparse_attn_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _L, _I, _L, _L, _L, _L, _L,
+                                  _L, _L, _L, _L, _F, _I, _P, _P, _P, _P, _L, _P]),
+    "pisa_sparse_attn_bwd_workspace_bytes": (_L, [_L, _L, _L, _L, _L, _L, _L]),
+}
+
+_lib = None
+
+
+def lib():
+    """Load and type the library once (ImportError when it was never built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH.name} is not built; run `python -m nlogn_pisa_b200.build` "
+                "(there is no CPU fallback)")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = handle
+    return _lib
+
+
+def check(status):
+    """Map a status code to the reference's exception types."""
+    if status == OK:
+        return
+    message = lib().pisa_last_error().decode(errors="replace")
+    if status in (ERR_INVALID, ERR_UNSUPPORTED):
+        raise ValueError(message)
+    raise RuntimeError(f"libpisa_b200: {message}")
+
+
+def ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def dtype_code(t):
+    try:
+        return DTYPES[t.dtype]
+    except KeyError:
+        raise ValueError("the CUDA kernels support FP16, BF16 and FP32") from None

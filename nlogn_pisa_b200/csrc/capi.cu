@@ -1,0 +1,273 @@
+// extern "C" entry points of libpisa_b200: argument checks, workspace layout
+// and dispatch.  Each function documents the reference operator it replaces
+// in include/pisa_b200.h.
+#include <cmath>
+#include <cstdio>
+#include <string>
+
+#include "internal.h"
+
+namespace pisa {
+
+static thread_local std::string g_last_error;
+
+int fail(int code, const char* msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int fail_cuda(cudaError_t err, const char* where) {
+  g_last_error = std::string(where) + ": " + cudaGetErrorString(err);
+  return PISA_ERR_CUDA;
+}
+
+static bool is_pow2(int64_t x) { return x > 0 && (x & (x - 1)) == 0; }
+
+static int elem_size(int dtype) { return dtype == PISA_F32 ? 4 : 2; }
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Rows of a [B, T, H, D] view are 16-byte aligned when the base is and every
+// stride is a multiple of the 16-byte vector.
+static bool rows_aligned(const void* p, int dtype, int64_t sb, int64_t st, int64_t sh) {
+  const int64_t v = 16 / elem_size(dtype);
+  return aligned16(p) && sb % v == 0 && st % v == 0 && sh % v == 0;
+}
+
+static int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+struct Geometry {
+  int64_t sizes[kMaxLevels];
+  int64_t offsets[kMaxLevels];
+  int64_t total;
+};
+
+// Node counts of levels 0..levels-1 for N keys: ceil(N/C), then ceil(n/br).
+static Geometry level_geometry(int64_t N, int64_t C, int64_t br, int64_t levels) {
+  Geometry g{};
+  int64_t n = (N + C - 1) / C, off = 0;
+  for (int64_t l = 0; l < levels && l < kMaxLevels; ++l) {
+    g.sizes[l] = n;
+    g.offsets[l] = off;
+    off += n;
+    n = (n + br - 1) / br;
+  }
+  g.total = off;
+  return g;
+}
+
+}  // namespace pisa
+
+using namespace pisa;
+
+extern "C" {
+
+int pisa_version(void) { return 100; }
+
+const char* pisa_last_error(void) { return g_last_error.c_str(); }
+
+int pisa_mean_pool(const void* keys, int dtype, int64_t B, int64_t N, int64_t H, int64_t D,
+                   int64_t key_sb, int64_t key_st, int64_t key_sh, int64_t size, void* out,
+                   pisa_stream_t stream) {
+  if (dtype < PISA_F32 || dtype > PISA_F16) return fail(PISA_ERR_UNSUPPORTED, "dtype must be fp32, bf16 or fp16");
+  if (size < 1) return fail(PISA_ERR_INVALID, "pool size must be positive");
+  if (B <= 0 || N <= 0 || H <= 0 || D <= 0) return fail(PISA_ERR_INVALID, "pooling requires nonempty [B,N,H,D] input");
+  if (D % (16 / elem_size(dtype)) != 0) return fail(PISA_ERR_UNSUPPORTED, "head_dim must fill whole 16-byte vectors");
+  if (!rows_aligned(keys, dtype, key_sb, key_st, key_sh) || !aligned16(out))
+    return fail(PISA_ERR_UNSUPPORTED, "rows must be 16-byte aligned");
+  const int64_t blocks = (N + size - 1) / size;
+  const int64_t off = 0;
+  return build_pyramid(keys, dtype, B, N, H, D, key_sb, key_st, key_sh, size, 2, 1, out,
+                       blocks * H * D, &off, 0, static_cast<cudaStream_t>(stream));
+}
+
+static int pyramid_checks(const void* keys, int dtype, int64_t B, int64_t N, int64_t H, int64_t D,
+                          int64_t sb, int64_t st, int64_t sh, int64_t C, int64_t br, int64_t levels,
+                          void* storage, int64_t ssb, const int64_t* offs) {
+  if (dtype < PISA_F32 || dtype > PISA_F16) return fail(PISA_ERR_UNSUPPORTED, "dtype must be fp32, bf16 or fp16");
+  if (B <= 0 || N <= 0 || H <= 0 || D <= 0) return fail(PISA_ERR_INVALID, "pyramid requires nonempty [B,N,H,D] keys");
+  if (C < 1) return fail(PISA_ERR_INVALID, "block_size must be positive");
+  if (br < 2) return fail(PISA_ERR_INVALID, "branching must be at least 2");
+  if (levels < 1 || levels > kMaxLevels) return fail(PISA_ERR_INVALID, "level count out of range");
+  if (!offs) return fail(PISA_ERR_INVALID, "level_offsets is required");
+  if (D % (16 / elem_size(dtype)) != 0) return fail(PISA_ERR_UNSUPPORTED, "head_dim must fill whole 16-byte vectors");
+  if (!rows_aligned(keys, dtype, sb, st, sh) || !rows_aligned(storage, dtype, ssb, H * D, D))
+    return fail(PISA_ERR_UNSUPPORTED, "rows must be 16-byte aligned");
+  return PISA_OK;
+}
+
+int pisa_build_pyramid(const void* keys, int dtype, int64_t B, int64_t N, int64_t H, int64_t D,
+                       int64_t key_sb, int64_t key_st, int64_t key_sh, int64_t block_size,
+                       int64_t branching, int64_t num_levels, void* storage, int64_t storage_sb,
+                       const int64_t* level_offsets, pisa_stream_t stream) {
+  int rc = pyramid_checks(keys, dtype, B, N, H, D, key_sb, key_st, key_sh, block_size, branching,
+                          num_levels, storage, storage_sb, level_offsets);
+  if (rc) return rc;
+  return build_pyramid(keys, dtype, B, N, H, D, key_sb, key_st, key_sh, block_size, branching,
+                       num_levels, storage, storage_sb, level_offsets, 0,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int pisa_pyramid_update(const void* keys, int dtype, int64_t B, int64_t N, int64_t H, int64_t D,
+                        int64_t key_sb, int64_t key_st, int64_t key_sh, int64_t block_size,
+                        int64_t branching, int64_t num_levels, void* storage, int64_t storage_sb,
+                        const int64_t* level_offsets, int64_t first_token, pisa_stream_t stream) {
+  int rc = pyramid_checks(keys, dtype, B, N, H, D, key_sb, key_st, key_sh, block_size, branching,
+                          num_levels, storage, storage_sb, level_offsets);
+  if (rc) return rc;
+  if (first_token < 0 || first_token > N) return fail(PISA_ERR_INVALID, "first_token out of range");
+  return build_pyramid(keys, dtype, B, N, H, D, key_sb, key_st, key_sh, block_size, branching,
+                       num_levels, storage, storage_sb, level_offsets, first_token,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int64_t pisa_select_workspace_bytes(int64_t B, int64_t Tq, int64_t H, int64_t D, int64_t N,
+                                    int dtype, int64_t block_size, int64_t branching,
+                                    int64_t topk, int64_t top, int64_t first_width, int schedule,
+                                    int build_summary) {
+  (void)Tq; (void)topk; (void)first_width; (void)schedule;
+  if (!build_summary || block_size < 1 || branching < 2 || top < 0) return 0;
+  Geometry g = level_geometry(N, block_size, branching, top + 1);
+  return align_up(B * g.total * H * D * elem_size(dtype), 256);
+}
+
+int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, const void* keys,
+                       int64_t key_sb, int64_t key_st, int64_t key_sh, const void* summary,
+                       int64_t summary_sb, const int64_t* level_offsets,
+                       const int64_t* level_sizes, int64_t num_levels, const int64_t* positions,
+                       int64_t position_offset, int dtype, int64_t B, int64_t Tq, int64_t Hq,
+                       int64_t H, int64_t D, int64_t N, int method, int64_t block_size,
+                       int64_t branching, int64_t topk, int force_first, int64_t force_recent,
+                       int64_t top, int64_t first_width, int schedule, int64_t* out_ids,
+                       void* workspace, int64_t workspace_bytes, pisa_stream_t stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype < PISA_F32 || dtype > PISA_F16) return fail(PISA_ERR_UNSUPPORTED, "GPU routing supports FP16, BF16 and FP32");
+  if (method < PISA_METHOD_PISA1 || method > PISA_METHOD_PISA) return fail(PISA_ERR_INVALID, "method must be pisa1, pisa2 or pisa");
+  if (schedule != PISA_SCHEDULE_GROUPED && schedule != PISA_SCHEDULE_FUSED) return fail(PISA_ERR_INVALID, "routing_schedule must be grouped or fused");
+  if (B <= 0 || Tq <= 0 || Hq <= 0 || H <= 0 || D <= 0 || N <= 0) return fail(PISA_ERR_INVALID, "nonempty tensors are required");
+  if (Hq % H) return fail(PISA_ERR_INVALID, "a whole number of query heads per KV head is required");
+  if (Hq / H > 32) return fail(PISA_ERR_UNSUPPORTED, "at most 32 query heads per KV head");
+  if (D % 8 || D > 256) return fail(PISA_ERR_UNSUPPORTED, "head_dim must be a multiple of 8 and at most 256");
+  if (!is_pow2(topk) || topk < 8 || topk > 64 || !is_pow2(block_size) || block_size < 16)
+    return fail(PISA_ERR_UNSUPPORTED, "GPU routing requires power-of-two block_size >= 16 and topk in {8,16,32,64}");
+  if (branching != 2 && branching != 4) return fail(PISA_ERR_UNSUPPORTED, "branching must be 2 or 4");
+  if (force_recent < 1) return fail(PISA_ERR_INVALID, "causal pyramid routing requires force_recent >= 1");
+  const int64_t blocks = (N + block_size - 1) / block_size;
+  if (topk < std::min<int64_t>(blocks, force_recent + (force_first ? 1 : 0)))
+    return fail(PISA_ERR_INVALID, "topk cannot hold all required blocks");
+  if (top < 0 || top >= kMaxLevels) return fail(PISA_ERR_INVALID, "routing depth out of range");
+  if (!is_pow2(first_width) || first_width < 16 || first_width > 256)
+    return fail(PISA_ERR_UNSUPPORTED, "first network width must be a power of two in [16, 256]");
+  if (topk * branching > 256) return fail(PISA_ERR_UNSUPPORTED, "topk * branching must be at most 256");
+  if (!out_ids) return fail(PISA_ERR_INVALID, "out_ids is required");
+  if (!rows_aligned(q, dtype, q_sb, q_st, q_sh) || !rows_aligned(keys, dtype, key_sb, key_st, key_sh))
+    return fail(PISA_ERR_UNSUPPORTED, "q and key rows must be 16-byte aligned");
+
+  RouteArgs a{};
+  if (summary == nullptr) {
+    Geometry g = level_geometry(N, block_size, branching, top + 1);
+    const int64_t need = align_up(B * g.total * H * D * elem_size(dtype), 256);
+    if (!workspace || workspace_bytes < need) return fail(PISA_ERR_INVALID, "workspace too small");
+    int rc = build_pyramid(keys, dtype, B, N, H, D, key_sb, key_st, key_sh, block_size, branching,
+                           top + 1, workspace, g.total * H * D, g.offsets, 0, s);
+    if (rc) return rc;
+    a.summary = workspace;
+    a.s_sb = g.total * H * D;
+    for (int l = 0; l <= top; ++l) { a.levels.offset[l] = g.offsets[l]; a.levels.size[l] = int32_t(g.sizes[l]); }
+  } else {
+    if (!level_offsets || !level_sizes || num_levels < 1) return fail(PISA_ERR_INVALID, "pyramid level tables are required");
+    if (!rows_aligned(summary, dtype, summary_sb, H * D, D)) return fail(PISA_ERR_UNSUPPORTED, "summary rows must be 16-byte aligned");
+    a.summary = summary;
+    a.s_sb = summary_sb;
+    // A one-node local pyramid remains that node at additional common levels
+    // (top_k_pyramid_torch.py:145-147).
+    for (int l = 0; l <= top; ++l) {
+      const int64_t src = std::min<int64_t>(l, num_levels - 1);
+      a.levels.offset[l] = level_offsets[src];
+      a.levels.size[l] = int32_t(level_sizes[src]);
+    }
+  }
+  a.q = q; a.q_sb = q_sb; a.q_st = q_st; a.q_sh = q_sh;
+  a.keys = keys; a.k_sb = key_sb; a.k_st = key_st; a.k_sh = key_sh;
+  a.positions = positions; a.pos_offset = position_offset;
+  a.B = int(B); a.T = int(Tq); a.H = int(H); a.G = int(Hq / H); a.D = int(D); a.N = int(N);
+  a.C = int(block_size); a.K = int(topk); a.br = int(branching); a.method = method;
+  a.top = int(top); a.first_width = int(first_width);
+  a.force_first = force_first ? 1 : 0; a.force_recent = int(force_recent);
+  const double scale = 1.0 / std::sqrt(double(D));
+  a.scale = float(scale);
+  a.c2 = float(0.5 * scale * scale);
+  a.out_ids = out_ids;
+  a.coarse_only = 0;
+  return route(a, dtype, s);
+}
+
+int pisa_sparse_attn_fwd(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, const void* k,
+                         int64_t k_sb, int64_t k_st, int64_t k_sh, const void* v, int64_t v_sb,
+                         int64_t v_st, int64_t v_sh, const void* indices, int index_bytes,
+                         const int64_t* positions, int64_t position_offset, int dtype, int64_t B,
+                         int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t Dv, int64_t N,
+                         int64_t S, int64_t block_size, float scale, int causal, void* out,
+                         float* lse, pisa_stream_t stream) {
+  if (dtype < PISA_F32 || dtype > PISA_F16) return fail(PISA_ERR_UNSUPPORTED, "CUDA attention supports FP16, BF16 and FP32");
+  if (B <= 0 || Tq <= 0 || Hq <= 0 || H <= 0 || D <= 0 || Dv <= 0 || N <= 0) return fail(PISA_ERR_INVALID, "nonempty tensors are required");
+  if (Hq % H) return fail(PISA_ERR_INVALID, "a whole number of query heads per KV head is required");
+  if (S < 0) return fail(PISA_ERR_INVALID, "negative slot count");
+  if (block_size < 1) return fail(PISA_ERR_INVALID, "invalid block_size");
+  if (index_bytes != 4 && index_bytes != 8) return fail(PISA_ERR_INVALID, "indices must be int32 or int64");
+  if (D % 8 || D > 256 || Dv > 256) return fail(PISA_ERR_UNSUPPORTED, "head_dim must be a multiple of 8 and at most 256");
+  if (!rows_aligned(q, dtype, q_sb, q_st, q_sh) || !rows_aligned(k, dtype, k_sb, k_st, k_sh))
+    return fail(PISA_ERR_UNSUPPORTED, "q and key rows must be 16-byte aligned");
+  if (!out) return fail(PISA_ERR_INVALID, "out is required");
+  AttnArgs a{};
+  a.q = q; a.q_sb = q_sb; a.q_st = q_st; a.q_sh = q_sh;
+  a.k = k; a.k_sb = k_sb; a.k_st = k_st; a.k_sh = k_sh;
+  a.v = v; a.v_sb = v_sb; a.v_st = v_st; a.v_sh = v_sh;
+  a.indices = indices; a.index_bytes = index_bytes;
+  a.positions = positions; a.pos_offset = position_offset;
+  a.B = int(B); a.T = int(Tq); a.Hq = int(Hq); a.H = int(H); a.G = int(Hq / H);
+  a.D = int(D); a.Dv = int(Dv); a.N = int(N); a.S = int(S); a.C = int(block_size);
+  a.scale = scale; a.causal = causal ? 1 : 0;
+  a.out = out; a.lse = lse;
+  return attn_fwd(a, dtype, static_cast<cudaStream_t>(stream));
+}
+
+int64_t pisa_sparse_attn_bwd_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H,
+                                             int64_t D, int64_t Dv, int64_t N) {
+  (void)Tq; (void)Hq;
+  return align_up(B * N * H * D * 4, 256) + align_up(B * N * H * Dv * 4, 256);
+}
+
+int pisa_sparse_attn_bwd(const void* q, const void* k, const void* v, const void* out,
+                         const void* dout, const float* lse, const void* indices, int index_bytes,
+                         const int64_t* positions, int64_t position_offset, int dtype, int64_t B,
+                         int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t Dv, int64_t N,
+                         int64_t S, int64_t block_size, float scale, int causal, void* dq,
+                         void* dk, void* dv, void* workspace, int64_t workspace_bytes,
+                         pisa_stream_t stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype < PISA_F32 || dtype > PISA_F16) return fail(PISA_ERR_UNSUPPORTED, "CUDA attention supports FP16, BF16 and FP32");
+  if (B <= 0 || Tq <= 0 || Hq <= 0 || H <= 0 || D <= 0 || Dv <= 0 || N <= 0) return fail(PISA_ERR_INVALID, "nonempty tensors are required");
+  if (Hq % H) return fail(PISA_ERR_INVALID, "a whole number of query heads per KV head is required");
+  if (index_bytes != 4 && index_bytes != 8) return fail(PISA_ERR_INVALID, "indices must be int32 or int64");
+  if (D % 8 || Dv % 8 || D > 256 || Dv > 256) return fail(PISA_ERR_UNSUPPORTED, "head_dim must be a multiple of 8 and at most 256");
+  if (!lse || !dq || !dk || !dv) return fail(PISA_ERR_INVALID, "lse, dq, dk and dv are required");
+  const int64_t need = pisa_sparse_attn_bwd_workspace_bytes(B, Tq, Hq, H, D, Dv, N);
+  if (!workspace || workspace_bytes < need) return fail(PISA_ERR_INVALID, "workspace too small");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dout)) return fail(PISA_ERR_UNSUPPORTED, "rows must be 16-byte aligned");
+  AttnArgs a{};
+  a.q = q; a.k = k; a.v = v; a.o = out; a.dout = dout; a.lse_in = lse;
+  a.indices = indices; a.index_bytes = index_bytes;
+  a.positions = positions; a.pos_offset = position_offset;
+  a.B = int(B); a.T = int(Tq); a.Hq = int(Hq); a.H = int(H); a.G = int(Hq / H);
+  a.D = int(D); a.Dv = int(Dv); a.N = int(N); a.S = int(S); a.C = int(block_size);
+  a.scale = scale; a.causal = causal ? 1 : 0;
+  a.dq = dq;
+  a.dk_acc = static_cast<float*>(workspace);
+  a.dv_acc = reinterpret_cast<float*>(static_cast<char*>(workspace) + align_up(B * N * H * D * 4, 256));
+  cudaError_t e = cudaMemsetAsync(workspace, 0, need, s);
+  if (e != cudaSuccess) return fail_cuda(e, "workspace clear");
+  return attn_bwd(a, dtype, dk, dv, s);
+}
+
+}  // extern "C"

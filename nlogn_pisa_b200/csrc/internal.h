@@ -1,0 +1,81 @@
+// Internal declarations shared by the translation units of libpisa_b200.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "pisa_b200.h"
+
+namespace pisa {
+
+// Records `msg` as the calling thread's last error and returns `code`.
+int fail(int code, const char* msg);
+int fail_cuda(cudaError_t err, const char* where);
+
+#define PISA_CHECK_LAUNCH()                                        \
+  do {                                                             \
+    cudaError_t _e = cudaGetLastError();                           \
+    if (_e != cudaSuccess) return ::pisa::fail_cuda(_e, __func__); \
+  } while (0)
+
+struct LevelTable {
+  int64_t offset[kMaxLevels];
+  int32_t size[kMaxLevels];
+};
+
+int build_pyramid(const void* keys, int dtype, int64_t B, int64_t N, int64_t H, int64_t D,
+                  int64_t sb, int64_t st, int64_t sh, int64_t C, int64_t br, int64_t levels,
+                  void* storage, int64_t ssb, const int64_t* offs, int64_t first_token,
+                  cudaStream_t stream);
+
+struct RouteArgs {
+  const void* q;
+  int64_t q_sb, q_st, q_sh;
+  const void* keys;
+  int64_t k_sb, k_st, k_sh;
+  const void* summary;
+  int64_t s_sb;
+  LevelTable levels;
+  const int64_t* positions;
+  int64_t pos_offset;
+  int B, T, H, G, D, N;
+  int C, K, br, method, top, first_width, force_first, force_recent;
+  float scale, c2;
+  int64_t* out_ids;     // [B,T,H,K] when the leaf level is scored here
+  int32_t* candidates;  // [B,T,H,W0] when only the coarse levels run here
+  int W0;
+  int coarse_only;
+};
+
+int route(const RouteArgs& a, int dtype, cudaStream_t stream);
+
+struct AttnArgs {
+  const void* q;
+  int64_t q_sb, q_st, q_sh;
+  const void* k;
+  int64_t k_sb, k_st, k_sh;
+  const void* v;
+  int64_t v_sb, v_st, v_sh;
+  const void* indices;
+  int index_bytes;
+  const int64_t* positions;
+  int64_t pos_offset;
+  int B, T, Hq, H, G, D, Dv, N, S, C;
+  float scale;
+  int causal;
+  void* out;
+  float* lse;
+  // backward
+  const void* o;
+  const void* dout;
+  const float* lse_in;
+  void* dq;
+  float* dk_acc;
+  float* dv_acc;
+};
+
+int attn_fwd(const AttnArgs& a, int dtype, cudaStream_t stream);
+int attn_bwd(const AttnArgs& a, int dtype, void* dk, void* dv, cudaStream_t stream);
+
+}  // namespace pisa

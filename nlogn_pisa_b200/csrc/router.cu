@@ -1,0 +1,354 @@
+// K2: coarse-to-fine router (and, in the fused schedule, leaf scoring + top-K).
+//
+// One CTA of four warps routes one (batch, query token, KV head) item through
+// levels top..0, as pyramid_select (pisa/pisa/ops/flash_sparse_attn/
+// top_k_pyramid/top_k_pyramid_torch.py:137-177):
+//   masks      valid = id>=0 & id*(C*b^l) <= pos; forced = first block or an
+//              ancestor of leaf pos//C - r (r < force_recent); scoreable =
+//              valid & !forced & (#valid > K) (pisa1: no identity shortcut)
+//              (:6-14, :114-120; triton score_masks :105-122)
+//   scores     LSE / second-order over the b child summaries (levels >= 1),
+//              over the C raw keys (level 0), or q . node mean (pisa1),
+//              fp32, summed over the G query heads of the KV head (:48-80)
+//   fill       unscoreable 0, invalid -1e9, forced +1e9 (:169-171)
+//   top-K      the descending bitonic network with its tie order (:84-110)
+//   expand     children b*id + {0..b-1} (:173-175)
+// Scoring threads own one candidate each at coarse levels and one warp per
+// candidate block at the leaf level (lanes own keys; warp shuffles combine the
+// per-lane running max / sum of exponentials).  Warp 0 runs the network in
+// registers (element i in lane i%32, slot i/32).
+#include "internal.h"
+
+namespace pisa {
+
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int kMaxWidth = 256;
+
+template <typename T, int GMAX>
+__device__ __forceinline__ void row_dots(const T* __restrict__ row, const float* __restrict__ qs,
+                                         int G, int D, float (&acc)[GMAX]) {
+  constexpr int V = Vec<T>::N;
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) acc[g] = 0.f;
+  for (int d = 0; d < D; d += V) {
+    float x[V];
+    load_vec<T>(row + d, x);
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      if (g < G) {
+        const float* qg = qs + g * D + d;
+#pragma unroll
+        for (int i = 0; i < V; i += 4) {
+          const float4 qv = *reinterpret_cast<const float4*>(qg + i);
+          acc[g] = fmaf(qv.x, x[i + 0], acc[g]);
+          acc[g] = fmaf(qv.y, x[i + 1], acc[g]);
+          acc[g] = fmaf(qv.z, x[i + 2], acc[g]);
+          acc[g] = fmaf(qv.w, x[i + 3], acc[g]);
+        }
+      }
+    }
+  }
+}
+
+// Score of one coarse candidate (level >= 1) from its `br` child summaries,
+// or of one node (pisa1, support 1).  Thread-local.
+template <typename T, int GMAX>
+__device__ float coarse_score(const RouteArgs& a, const T* level_base, int child_len, int id,
+                              const float* qs) {
+  const int64_t node_stride = int64_t(a.H) * a.D;
+  float acc[GMAX];
+  if (a.method == PISA_METHOD_PISA1) {
+    row_dots<T, GMAX>(level_base + int64_t(id) * node_stride, qs, a.G, a.D, acc);
+    float score = 0.f;
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g)
+      if (g < a.G) score += acc[g];
+    return score;
+  }
+  // pisa: running max m / scaled sum s; pisa2 binary: z0, z1; pisa2 general:
+  // sum of products s1 and of squares s2.
+  float m[GMAX], s[GMAX], z0[GMAX], z1[GMAX], s1[GMAX], s2[GMAX];
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+    m[g] = -INFINITY; s[g] = 0.f; z0[g] = 0.f; z1[g] = 0.f; s1[g] = 0.f; s2[g] = 0.f;
+  }
+  int count = 0;
+  const bool binary = a.br == 2;
+  float score = 0.f;
+  for (int j = 0; j < a.br; ++j) {
+    const int c = id * a.br + j;
+    if (c >= child_len) break;
+    row_dots<T, GMAX>(level_base + int64_t(c) * node_stride, qs, a.G, a.D, acc);
+    ++count;
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      if (g >= a.G) continue;
+      if (a.method == PISA_METHOD_PISA) {
+        const float z = acc[g] * a.scale;
+        if (z > m[g]) { s[g] = s[g] * expf(m[g] - z) + 1.f; m[g] = z; }
+        else { s[g] += expf(z - m[g]); }
+      } else if (binary) {
+        const float z = acc[g] * a.scale;
+        if (j == 0) z0[g] = z; else z1[g] = z;
+      } else {
+        s1[g] += acc[g];
+        s2[g] += acc[g] * acc[g];
+      }
+    }
+  }
+  const float cnt = float(count > 0 ? count : 1);
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+    if (g >= a.G) continue;
+    if (a.method == PISA_METHOD_PISA) {
+      score += m[g] + logf(s[g]);
+    } else if (binary) {
+      const float total = z0[g] + z1[g];
+      const float diff = z0[g] - z1[g];
+      score += count == 2 ? 0.5f * total + 0.125f * diff * diff : total;
+    } else {
+      const float mean = s1[g] / cnt;
+      const float second = s2[g] / cnt;
+      const float var = fmaxf(second - mean * mean, 0.f);
+      score += a.scale * mean + a.c2 * var;
+    }
+  }
+  return score;
+}
+
+// Score of one leaf candidate from its C raw keys; executed by a whole warp.
+template <typename T, int GMAX>
+__device__ float leaf_score_warp(const RouteArgs& a, const T* key_base, int id, const float* qs,
+                                 int lane) {
+  float m[GMAX], s[GMAX], s2[GMAX], acc[GMAX];
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) { m[g] = -INFINITY; s[g] = 0.f; s2[g] = 0.f; }
+  int count = 0;
+  const int64_t first = int64_t(id) * a.C;
+  for (int kk = lane; kk < a.C; kk += 32) {
+    const int64_t tok = first + kk;
+    if (tok >= a.N) break;
+    row_dots<T, GMAX>(key_base + tok * a.k_st, qs, a.G, a.D, acc);
+    ++count;
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      if (g >= a.G) continue;
+      if (a.method == PISA_METHOD_PISA) {
+        const float z = acc[g] * a.scale;
+        if (z > m[g]) { s[g] = s[g] * expf(m[g] - z) + 1.f; m[g] = z; }
+        else { s[g] += expf(z - m[g]); }
+      } else {
+        s[g] += acc[g];
+        s2[g] += acc[g] * acc[g];
+      }
+    }
+  }
+  float score = 0.f;
+  if (a.method == PISA_METHOD_PISA) {
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      if (g >= a.G) continue;
+      const float M = warp_max(m[g]);
+      const float part = m[g] == -INFINITY ? 0.f : s[g] * expf(m[g] - M);
+      const float S = warp_sum(part);
+      score += M + logf(S);
+    }
+  } else {
+    int total = count;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(kFull, total, o);
+    const float cnt = float(total > 0 ? total : 1);
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      if (g >= a.G) continue;
+      const float mean = warp_sum(s[g]) / cnt;
+      const float second = warp_sum(s2[g]) / cnt;
+      const float var = fmaxf(second - mean * mean, 0.f);
+      score += a.scale * mean + a.c2 * var;
+    }
+  }
+  return score;
+}
+
+template <int WP>
+__device__ __forceinline__ void network_step(float* sc, int* ids, int width, int K, int br,
+                                             int level, int64_t pos, int C, int lane,
+                                             int64_t* out, int* next_ids) {
+  constexpr int E = Network<WP>::E;
+  float s[E];
+  int id[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = e * 32 + lane;
+    const bool in = i < width;
+    s[e] = in ? sc[i] : kNegFill;
+    id[e] = in ? ids[i] : -1;
+  }
+  __syncwarp();
+  Network<WP>::sort(s, id, lane);
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = e * 32 + lane;
+    if (i < K) {
+      const int v = id[e];
+      if (level > 0) {
+        for (int j = 0; j < br; ++j) next_ids[i * br + j] = v < 0 ? -1 : v * br + j;
+      } else if (out) {
+        out[i] = (v < 0 || int64_t(v) * C > pos) ? -1 : v;
+      }
+    }
+  }
+}
+
+template <typename T, int GMAX>
+__global__ void __launch_bounds__(kThreads) route_kernel(const RouteArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  float* qs = smem;                                    // [G][D]
+  int* ids = reinterpret_cast<int*>(qs + a.G * a.D);   // [kMaxWidth]
+  float* sc = reinterpret_cast<float*>(ids + kMaxWidth);
+  unsigned char* fl = reinterpret_cast<unsigned char*>(sc + kMaxWidth);
+  __shared__ int s_valid;
+
+  const int item = blockIdx.x;
+  const int h = item % a.H;
+  const int t = (item / a.H) % a.T;
+  const int b = item / (a.H * a.T);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t pos = a.positions ? a.positions[int64_t(b) * a.T + t] : a.pos_offset + t;
+
+  const T* qp = static_cast<const T*>(a.q) + b * a.q_sb + t * a.q_st + int64_t(h) * a.G * a.q_sh;
+  for (int e = tid; e < a.G * a.D; e += kThreads) {
+    const int g = e / a.D, d = e % a.D;
+    qs[e] = to_f32<T>(qp[g * a.q_sh + d]);
+  }
+  int width = a.first_width;
+  for (int w = tid; w < width; w += kThreads) ids[w] = w;
+  const T* summary = static_cast<const T*>(a.summary) + b * a.s_sb + int64_t(h) * a.D;
+  const T* key_base = static_cast<const T*>(a.keys) + b * a.k_sb + int64_t(h) * a.k_sh;
+  const int64_t node_stride = int64_t(a.H) * a.D;
+  __syncthreads();
+
+  int64_t span = a.C;  // C * br^level
+  int64_t div = 1;     // br^level
+  for (int l = 0; l < a.top; ++l) { span *= a.br; div *= a.br; }
+  const int64_t leaf = pos / a.C;
+
+  for (int level = a.top; level >= 0; --level) {
+    const int len = a.levels.size[level];
+    for (int w = tid; w < width; w += kThreads) {
+      int id = ids[w];
+      if (id >= len) id = -1;
+      ids[w] = id;
+      const bool valid = id >= 0 && int64_t(id) * span <= pos;
+      bool forced = false;
+      if (valid) {
+        if (a.force_first && id == 0) forced = true;
+        for (int r = 0; r < a.force_recent; ++r) {
+          const int64_t target = leaf - r;
+          if (target >= 0 && id == target / div) forced = true;
+        }
+      }
+      fl[w] = (valid ? 1 : 0) | (forced ? 2 : 0);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int cnt = 0;
+      for (int w = lane; w < width; w += 32) cnt += fl[w] & 1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(kFull, cnt, o);
+      if (lane == 0) s_valid = cnt;
+    }
+    __syncthreads();
+    const bool identity = a.method != PISA_METHOD_PISA1 && s_valid <= a.K;
+
+    if (level == 0 && a.coarse_only) {
+      int32_t* dst = a.candidates + int64_t(item) * a.W0;
+      for (int w = tid; w < width; w += kThreads) dst[w] = ids[w];
+      return;
+    }
+
+    // fill values and thread-per-candidate scoring
+    const bool warp_leaf = level == 0 && a.method != PISA_METHOD_PISA1;
+    for (int w = tid; w < width; w += kThreads) {
+      const int f = fl[w];
+      const bool valid = f & 1, forced = f & 2;
+      const bool scoreable = valid && !forced && !identity;
+      float v = 0.f;
+      if (scoreable && !warp_leaf) {
+        if (a.method == PISA_METHOD_PISA1) {
+          v = coarse_score<T, GMAX>(a, summary + a.levels.offset[level] * node_stride, len, ids[w], qs);
+        } else {
+          v = coarse_score<T, GMAX>(a, summary + a.levels.offset[level - 1] * node_stride,
+                                    a.levels.size[level - 1], ids[w], qs);
+        }
+      }
+      sc[w] = !valid ? kNegFill : (forced ? kPosFill : v);
+    }
+    if (warp_leaf) {
+      __syncthreads();
+      for (int w = warp; w < width; w += kThreads / 32) {
+        const int f = fl[w];
+        const bool scoreable = (f & 1) && !(f & 2) && !identity;
+        if (scoreable) {
+          const float v = leaf_score_warp<T, GMAX>(a, key_base, ids[w], qs, lane);
+          if (lane == 0) sc[w] = v;
+        }
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int64_t* out = level == 0 ? a.out_ids + int64_t(item) * a.K : nullptr;
+      switch (width) {
+        case 16: network_step<16>(sc, ids, width, a.K, a.br, level, pos, a.C, lane, out, ids); break;
+        case 32: network_step<32>(sc, ids, width, a.K, a.br, level, pos, a.C, lane, out, ids); break;
+        case 64: network_step<64>(sc, ids, width, a.K, a.br, level, pos, a.C, lane, out, ids); break;
+        case 128: network_step<128>(sc, ids, width, a.K, a.br, level, pos, a.C, lane, out, ids); break;
+        default: network_step<256>(sc, ids, width, a.K, a.br, level, pos, a.C, lane, out, ids); break;
+      }
+    }
+    __syncthreads();
+    width = a.K * a.br;
+    span /= a.br;
+    div /= a.br;
+  }
+}
+
+template <typename T, int GMAX>
+int launch_route(const RouteArgs& a, cudaStream_t stream) {
+  const size_t smem = size_t(a.G) * a.D * sizeof(float) + kMaxWidth * (2 * sizeof(int) + 1);
+  auto kernel = route_kernel<T, GMAX>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return fail_cuda(e, "route smem attribute");
+  }
+  const int64_t items = int64_t(a.B) * a.T * a.H;
+  if (items == 0) return PISA_OK;
+  kernel<<<unsigned(items), kThreads, smem, stream>>>(a);
+  PISA_CHECK_LAUNCH();
+  return PISA_OK;
+}
+
+template <typename T>
+int route_t(const RouteArgs& a, cudaStream_t stream) {
+  if (a.G <= 1) return launch_route<T, 1>(a, stream);
+  if (a.G <= 2) return launch_route<T, 2>(a, stream);
+  if (a.G <= 4) return launch_route<T, 4>(a, stream);
+  if (a.G <= 8) return launch_route<T, 8>(a, stream);
+  if (a.G <= 16) return launch_route<T, 16>(a, stream);
+  return launch_route<T, 32>(a, stream);
+}
+
+}  // namespace
+
+int route(const RouteArgs& a, int dtype, cudaStream_t stream) {
+  switch (dtype) {
+    case PISA_F32: return route_t<float>(a, stream);
+    case PISA_BF16: return route_t<__nv_bfloat16>(a, stream);
+    case PISA_F16: return route_t<__half>(a, stream);
+  }
+  return fail(PISA_ERR_UNSUPPORTED, "unsupported dtype");
+}
+
+}  // namespace pisa

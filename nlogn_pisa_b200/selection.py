@@ -1,0 +1,229 @@
+"""Block selection, mean pooling and pyramids on the CUDA library.
+
+Drop-in mirrors of the reference operators (paths relative to the
+Aphelios-Tang/NlogN_PISA project):
+  select_blocks / top_k_pyramid_fn -> pisa/pisa/ops/flash_sparse_attn/top_k_pyramid/top_k_pyramid.py:11-122
+  routing_geometry                 -> top_k_pyramid_torch.py:124-133
+  mean_pool / build_pyramid        -> pisa/pisa/ops/compress/mean_pooling/mean_pooling.py:8-52
+Same argument names, defaults and ValueError contract; every computation runs
+in libpisa_b200 (no Triton, no CPU fallback).  ``branching`` (default 2, the
+reference's only value) additionally allows a 4-ary pyramid.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .validation import packed_queries, query_positions, require_cuda, validate_qkv
+
+_INT64_ARRAY = ctypes.c_int64 * 32
+
+
+def routing_geometry(blocks, topk, branching=2):
+    """(top, first_width): levels descended and the first network width."""
+    top = 0
+    while blocks > topk:
+        parent = -(-blocks // branching)
+        if parent < topk or parent == blocks:
+            break
+        blocks = parent
+        top += 1
+    return top, max(16, 1 << (max(blocks, topk) - 1).bit_length())
+
+
+def level_sizes(leaves, branching, levels):
+    sizes, n = [], leaves
+    for _ in range(levels):
+        sizes.append(n)
+        n = -(-n // branching)
+    return sizes
+
+
+def _rows16(t):
+    """t itself when its rows are 16-byte aligned with a unit last stride, else a contiguous copy."""
+    vec = 16 // t.element_size()
+    ok = (t.stride(-1) == 1 and t.data_ptr() % 16 == 0
+          and all(s % vec == 0 for s in t.stride()[:-1]) and t.shape[-1] % vec == 0)
+    return t if ok else t.contiguous()
+
+
+def _c_array(values):
+    arr = _INT64_ARRAY()
+    for i, v in enumerate(values):
+        arr[i] = int(v)
+    return arr
+
+
+def mean_pool(keys, size, *, backend="auto", fp32_accumulation=False):
+    """Mean over the valid tokens of each ``size`` block (tail divides by its count).
+
+    Accumulates in fp32 for every input (the reference's torch path does; its
+    Triton path does so when ``fp32_accumulation``), forward only.
+    """
+    if size < 1:
+        raise ValueError("pool size must be positive")
+    if backend not in ("auto", "torch", "triton", "cuda"):
+        raise ValueError("pooling backend must be auto, torch, or triton")
+    require_cuda(keys)
+    if keys.ndim != 4 or not keys.numel():
+        raise ValueError("pooling requires a positive size and nonempty [B,N,H,D] input")
+    if torch.is_grad_enabled() and keys.requires_grad:
+        raise ValueError("CUDA pooling does not support gradients")
+    code = _lib.dtype_code(keys)
+    keys = _rows16(keys)
+    batch, length, heads, dim = keys.shape
+    blocks = -(-length // size)
+    out = torch.empty((batch, blocks, heads, dim), device=keys.device, dtype=keys.dtype)
+    with torch.cuda.device(keys.device):
+        _lib.check(_lib.lib().pisa_mean_pool(
+            _lib.ptr(keys), code, batch, length, heads, dim, *keys.stride()[:3], size,
+            _lib.ptr(out), _lib.stream_of(keys.device)))
+    return out
+
+
+def build_pyramid(keys, block_size, *, backend="auto", max_level=None, branching=2):
+    """Leaf means first, then pools of ``branching`` up to the root or ``max_level``.
+
+    All levels share one storage allocation; the returned tensors are views.
+    """
+    if max_level is not None and (type(max_level) is not int or max_level < 0):
+        raise ValueError("max_level must be a nonnegative integer or None")
+    if block_size < 1:
+        raise ValueError("pool size must be positive")
+    if backend not in ("auto", "torch", "triton", "cuda"):
+        raise ValueError("pooling backend must be auto, torch, or triton")
+    require_cuda(keys)
+    if keys.ndim != 4 or not keys.numel():
+        raise ValueError("pooling requires a positive size and nonempty [B,N,H,D] input")
+    if torch.is_grad_enabled() and keys.requires_grad:
+        raise ValueError("CUDA pooling does not support gradients")
+    code = _lib.dtype_code(keys)
+    keys = _rows16(keys)
+    batch, length, heads, dim = keys.shape
+    sizes = [-(-length // block_size)]
+    while sizes[-1] > 1 and (max_level is None or len(sizes) <= max_level):
+        sizes.append(-(-sizes[-1] // branching))
+    offsets = [0]
+    for s in sizes[:-1]:
+        offsets.append(offsets[-1] + s)
+    total = offsets[-1] + sizes[-1]
+    storage = torch.empty((batch, total, heads, dim), device=keys.device, dtype=keys.dtype)
+    with torch.cuda.device(keys.device):
+        _lib.check(_lib.lib().pisa_build_pyramid(
+            _lib.ptr(keys), code, batch, length, heads, dim, *keys.stride()[:3], block_size,
+            branching, len(sizes), _lib.ptr(storage), storage.stride(0), _c_array(offsets),
+            _lib.stream_of(keys.device)))
+    return [storage[:, o:o + s] for o, s in zip(offsets, sizes)]
+
+
+@torch.no_grad()
+def select_blocks(q, k, method="pisa", block_size=64, topk=8, cu_seqlens=None, query_offset=None,
+                  force_first=True, force_recent=2, backend="auto", pyramid=None, leaf_tile=4,
+                  routing_schedule="auto", branching=2):
+    """Return block ids [B,Tq,Hkv,K] int64 in network-rank order, padded by -1.
+
+    Arguments as the reference's select_blocks.  Ids are document-relative
+    under ``cu_seqlens``; slot order follows the comparison network; required
+    blocks (first, and the ``force_recent`` most recent) count toward K.
+    """
+    validate_qkv(q, k)
+    if method not in ("bsa", "pisa1", "pisa2", "pisa"):
+        raise ValueError("method must be bsa, pisa1, pisa2 or pisa")
+    if backend not in ("torch", "triton", "auto", "cuda"):
+        raise ValueError("backend must be torch, triton or auto")
+    if leaf_tile not in (1, 2, 4):
+        raise ValueError("leaf_tile must be 1, 2 or 4")
+    if routing_schedule not in ("auto", "grouped", "fused"):
+        raise ValueError("routing_schedule must be auto, grouped or fused")
+    if block_size < 1 or topk < 1 or force_recent < 0:
+        raise ValueError("positive block_size/topk and nonnegative force_recent required")
+    if method != "bsa" and force_recent == 0:
+        raise ValueError("causal pyramid routing requires force_recent >= 1")
+    if method == "bsa":
+        raise ValueError("the flat BSA baseline selection is not part of nlogn_pisa_b200")
+    if branching not in (2, 4):
+        raise ValueError("branching must be 2 or 4")
+    if routing_schedule == "auto":
+        grouped = method != "pisa1" and (q.shape[1] == k.shape[1] or (cu_seqlens is None and q.shape[1] > 1))
+        routing_schedule = "grouped" if grouped else "fused"
+        if grouped:
+            leaf_tile = 4
+    if cu_seqlens is not None:
+        segments = list(packed_queries(q, k, cu_seqlens, query_offset))
+        blocks = max((ke - ks + block_size - 1) // block_size for _, _, ks, ke, _ in segments)
+        geometry = routing_geometry(blocks, topk, branching) if routing_schedule == "fused" else None
+        pieces = [
+            _select_unpacked(q[:, qs:qe], k[:, ks:ke], method, block_size, topk, offset, force_first,
+                             force_recent, None, leaf_tile, routing_schedule, geometry, branching)
+            for qs, qe, ks, ke, offset in segments
+        ]
+        return torch.cat(pieces, 1)
+    return _select_unpacked(q, k, method, block_size, topk, query_offset, force_first, force_recent,
+                            pyramid, leaf_tile, routing_schedule, None, branching)
+
+
+def _pyramid_tables(pyramid, k, block_size, top, branching):
+    """(storage, batch_stride, offsets, sizes) for a caller-supplied pyramid, or Nones."""
+    if pyramid is None:
+        return None, 0, None, None
+    if hasattr(pyramid, "storage"):
+        storage = pyramid.storage
+        sizes = list(pyramid.level_sizes)
+        starts = getattr(pyramid, "starts", None)
+        offsets = list(starts) if starts is not None else [int(x) for x in pyramid.offsets.tolist()]
+        return _rows16_storage(storage), storage.stride(0), offsets[:len(sizes)], sizes
+    levels = list(pyramid.levels if hasattr(pyramid, "levels") else pyramid)
+    levels = levels + [levels[-1]] * max(0, top + 1 - len(levels))
+    summary = torch.cat(levels, dim=1).contiguous()
+    sizes = [x.shape[1] for x in levels]
+    offsets = [0]
+    for s in sizes[:-1]:
+        offsets.append(offsets[-1] + s)
+    return summary, summary.stride(0), offsets, sizes
+
+
+def _rows16_storage(storage):
+    if storage.stride(-1) != 1 or storage.stride(-2) != storage.shape[-1] or storage.stride(1) != storage.shape[-1] * storage.shape[-2]:
+        raise ValueError("pyramid storage must be contiguous per node ([B, total, H, D])")
+    return storage
+
+
+def _select_unpacked(q, k, method, block_size, topk, query_offset, force_first, force_recent,
+                     pyramid, leaf_tile, routing_schedule, geometry, branching):
+    require_cuda(q, k)
+    code = _lib.dtype_code(q)
+    if topk & (topk - 1) or block_size & (block_size - 1) or not 8 <= topk <= 64 or block_size < 16:
+        raise ValueError("GPU routing requires power-of-two block_size >= 16 and topk in {8,16,32,64}")
+    blocks = -(-k.shape[1] // block_size)
+    if topk < min(blocks, force_recent + int(force_first)):
+        raise ValueError("topk cannot hold all required blocks")
+    positions, offset = query_positions(q, k, query_offset)
+    top, first_width = geometry or routing_geometry(blocks, topk, branching)
+    q = _rows16(q)
+    k = _rows16(k)
+    batch, tokens, q_heads, dim = q.shape
+    heads, length = k.shape[2], k.shape[1]
+    summary, summary_sb, offsets, sizes = _pyramid_tables(pyramid, k, block_size, top, branching)
+    schedule = _lib.SCHEDULES[routing_schedule]
+    library = _lib.lib()
+    ws_bytes = library.pisa_select_workspace_bytes(
+        batch, tokens, heads, dim, length, code, block_size, branching, topk, top, first_width,
+        schedule, 1 if summary is None else 0)
+    workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+    out = torch.empty((batch, tokens, heads, topk), dtype=torch.int64, device=q.device)
+    with torch.cuda.device(q.device):
+        _lib.check(library.pisa_select_blocks(
+            _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3],
+            _lib.ptr(summary), summary_sb,
+            _c_array(offsets) if offsets else None, _c_array(sizes) if sizes else None,
+            len(sizes) if sizes else 0, _lib.ptr(positions), offset, code, batch, tokens, q_heads,
+            heads, dim, length, _lib.METHODS[method], block_size, branching, topk,
+            int(bool(force_first)), force_recent, top, first_width, schedule, _lib.ptr(out),
+            _lib.ptr(workspace), ws_bytes, _lib.stream_of(q.device)))
+    return out
+
+
+top_k_pyramid_fn = select_blocks

@@ -1,0 +1,104 @@
+"""CPU-side checks of the C ABI and the host logic (no compute calls)."""
+
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import pisa_oracle as O
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def header_symbols():
+    text = (ROOT / "include" / "pisa_b200.h").read_text()
+    return sorted(set(re.findall(r"PISA_API\s+[\w\s\*]+?\b(pisa_\w+)\(", text)))
+
+
+def test_library_exports_every_header_symbol():
+    from nlogn_pisa_b200 import _lib
+
+    lib = _lib.lib()
+    symbols = header_symbols()
+    assert len(symbols) >= 10
+    for name in symbols:
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert set(_lib.SIGNATURES) == set(symbols)
+    assert lib.pisa_version() >= 100
+
+
+def test_workspace_sizes_are_pure_host_functions():
+    from nlogn_pisa_b200 import _lib
+
+    lib = _lib.lib()
+    n = lib.pisa_select_workspace_bytes(1, 32768, 8, 128, 32768, 1, 64, 2, 32, 4, 32, 0, 1)
+    assert n >= 1 * (512 + 256 + 128 + 64 + 32) * 8 * 128 * 2
+    assert lib.pisa_select_workspace_bytes(1, 1, 8, 128, 4096, 1, 64, 2, 32, 1, 32, 1, 0) == 0
+    assert lib.pisa_sparse_attn_bwd_workspace_bytes(1, 4, 4, 2, 64, 64, 100) >= 2 * 100 * 2 * 64 * 4
+
+
+def test_invalid_arguments_report_status_without_gpu():
+    """Argument checks run before any device work and map to ValueError."""
+    from nlogn_pisa_b200 import _lib
+
+    lib = _lib.lib()
+    # topk 12 is outside {8,16,32,64}
+    rc = lib.pisa_select_blocks(None, 0, 0, 0, None, 0, 0, 0, None, 0, None, None, 0, None, 0, 1, 1, 64,
+                                4, 1, 64, 4096, 2, 64, 2, 12, 1, 1, 0, 16, 0, None, None, 0, None)
+    assert rc == _lib.ERR_UNSUPPORTED
+    assert "topk" in _lib.lib().pisa_last_error().decode()
+    with pytest.raises(ValueError):
+        _lib.check(rc)
+
+
+@pytest.mark.parametrize("blocks,topk,branching", [(64, 16, 2), (512, 32, 2), (4096, 32, 2), (20, 16, 2),
+                                                   (512, 32, 4), (4096, 32, 4), (1000, 64, 2), (7, 8, 2)])
+def test_routing_geometry_matches_oracle(blocks, topk, branching):
+    from nlogn_pisa_b200.selection import routing_geometry
+
+    assert routing_geometry(blocks, topk, branching) == O.routing_geometry(blocks, topk, branching)
+
+
+def test_operators_reject_cpu_tensors():
+    import nlogn_pisa_b200 as P
+
+    q = torch.randn(1, 64, 4, 64)
+    k = torch.randn(1, 64, 2, 64)
+    with pytest.raises(ValueError, match="CUDA"):
+        P.select_blocks(q, k, topk=8, block_size=16, force_recent=1)
+    with pytest.raises(ValueError, match="CUDA"):
+        P.sparse_attention(q, k, k, torch.zeros(1, 64, 2, 8, dtype=torch.long), block_size=16)
+    with pytest.raises(ValueError, match="CUDA"):
+        P.build_pyramid(k, 16)
+
+
+def test_validation_contract():
+    import nlogn_pisa_b200 as P
+
+    q = torch.randn(1, 64, 3, 64)
+    k = torch.randn(1, 64, 2, 64)
+    with pytest.raises(ValueError, match="whole number"):
+        P.select_blocks(q, k)
+    q = torch.randn(1, 64, 4, 64)
+    with pytest.raises(ValueError, match="method"):
+        P.select_blocks(q, k, method="nope")
+    with pytest.raises(ValueError, match="force_recent"):
+        P.select_blocks(q, k, force_recent=0)
+    with pytest.raises(ValueError, match="leaf_tile"):
+        P.select_blocks(q, k, leaf_tile=3)
+    with pytest.raises(ValueError, match="indices"):
+        P.sparse_attention(q, k, k, torch.zeros(1, 64, 2, dtype=torch.long))
+
+
+def test_cu_seqlens_contract():
+    from nlogn_pisa_b200.validation import packed_queries, sequence_slices
+
+    assert sequence_slices(torch.tensor([0, 5, 9]), 9) == [(0, 5), (5, 9)]
+    with pytest.raises(ValueError):
+        sequence_slices(torch.tensor([0, 5, 5, 9]), 9)
+    q = torch.zeros(1, 2, 4, 8)
+    k = torch.zeros(1, 9, 2, 8)
+    assert list(packed_queries(q, k, torch.tensor([0, 5, 9]))) == [(0, 1, 0, 5, 4), (1, 2, 5, 9, 3)]
