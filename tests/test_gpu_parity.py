@@ -10,6 +10,8 @@ from golden_cases import CASES, load, np_inputs, offset_arg
 pytestmark = pytest.mark.gpu
 
 GPU_CASES = [n for n, c in CASES.items() if c["dtype"] != "f64"]
+# the GPU routing envelope (top_k_pyramid_triton.py:329-332): topk in {8,16,32,64}
+SELECT_CASES = [n for n in GPU_CASES if CASES[n]["K"] >= 8]
 
 
 def _cuda(*tensors):
@@ -36,7 +38,7 @@ def _check_ids(got, want, trace, min_exact=1.0):
 
 
 @pytest.mark.parametrize("schedule", ["grouped", "fused"])
-@pytest.mark.parametrize("name", GPU_CASES)
+@pytest.mark.parametrize("name", SELECT_CASES)
 def test_selection_matches_reference(cuda_device, name, schedule):
     import nlogn_pisa_b200 as P
 
@@ -52,7 +54,19 @@ def test_selection_matches_reference(cuda_device, name, schedule):
         _check_ids(got.cpu().numpy(), rec[f"ids_{method}"].astype(np.int64), trace, min_exact)
 
 
-@pytest.mark.parametrize("name", GPU_CASES)
+def test_selection_outside_gpu_envelope_raises(cuda_device):
+    """topk 4 / f64 are outside the GPU routing envelope: ValueError, as the reference's GPU path."""
+    import nlogn_pisa_b200 as P
+
+    case, rec, (q, k, v, dout), _ = np_inputs("tail_f32")
+    qc, kc = _cuda(q, k)
+    with pytest.raises(ValueError, match="topk"):
+        P.select_blocks(qc, kc, block_size=case["C"], topk=case["K"], force_recent=1)
+    with pytest.raises(ValueError):
+        P.select_blocks(qc.double(), kc.double(), block_size=16, topk=8, force_recent=1)
+
+
+@pytest.mark.parametrize("name", SELECT_CASES)
 def test_network_order_matches_reference(cuda_device, name):
     """Slot order (network rank) is reproduced, not only the id sets."""
     import nlogn_pisa_b200 as P
