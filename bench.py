@@ -175,19 +175,24 @@ def main():
     method = _lib.METHODS[w.method]
     scale = D ** -0.5
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
-    launches_per_step = len(sizes) + 1 + 1
+    # pyramid levels + router + bucket count/scan/scatter + leaf tiles + final top-K + attention
+    launches_per_step = len(sizes) + 7
 
     def pyramid():
         _lib.check(lib.pisa_build_pyramid(
             _lib.ptr(k), code, B, N, H, D, *k.stride()[:3], C, br, len(sizes), _lib.ptr(storage),
             storage.stride(0), _c_array(offsets), sptr))
 
+    sel_ws_bytes = lib.pisa_select_workspace_bytes(B, N, Hq, H, D, N, code, method, C, br, K, top,
+                                                   first_width, _lib.SCHEDULES["grouped"], 0)
+    sel_ws = torch.empty(max(sel_ws_bytes, 1), dtype=torch.uint8, device=device)
+
     def select():
         _lib.check(lib.pisa_select_blocks(
             _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3], _lib.ptr(storage),
             storage.stride(0), _c_array(offsets), _c_array(sizes), len(sizes), None, 0, code, B, N,
             Hq, H, D, N, method, C, br, K, int(w.force_first), w.force_recent, top, first_width,
-            _lib.SCHEDULES["grouped"], _lib.ptr(ids), None, 0, sptr))
+            _lib.SCHEDULES["grouped"], _lib.ptr(ids), _lib.ptr(sel_ws), sel_ws_bytes, sptr))
 
     def attend():
         _lib.check(lib.pisa_sparse_attn_fwd(

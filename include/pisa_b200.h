@@ -129,11 +129,14 @@ PISA_API int pisa_select_blocks(const void *q, int64_t q_sb, int64_t q_st, int64
                        int64_t top, int64_t first_width, int schedule, int64_t *out_ids,
                        void *workspace, int64_t workspace_bytes, pisa_stream_t stream);
 
-/* Workspace bytes for pisa_select_blocks (with summary == NULL when build_summary != 0). */
-PISA_API int64_t pisa_select_workspace_bytes(int64_t B, int64_t Tq, int64_t H, int64_t D, int64_t N,
-                                    int dtype, int64_t block_size, int64_t branching,
-                                    int64_t topk, int64_t top, int64_t first_width, int schedule,
-                                    int build_summary);
+/*
+ * Workspace bytes for pisa_select_blocks with the same shapes and options
+ * (build_summary != 0 when it will be called with summary == NULL).
+ */
+PISA_API int64_t pisa_select_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D,
+                                             int64_t N, int dtype, int method, int64_t block_size,
+                                             int64_t branching, int64_t topk, int64_t top,
+                                             int64_t first_width, int schedule, int build_summary);
 
 /*
  * Attention over selected key blocks with one softmax over their union

@@ -121,14 +121,80 @@ int pisa_pyramid_update(const void* keys, int dtype, int64_t B, int64_t N, int64
                        static_cast<cudaStream_t>(stream));
 }
 
-int64_t pisa_select_workspace_bytes(int64_t B, int64_t Tq, int64_t H, int64_t D, int64_t N,
-                                    int dtype, int64_t block_size, int64_t branching,
-                                    int64_t topk, int64_t top, int64_t first_width, int schedule,
-                                    int build_summary) {
-  (void)Tq; (void)topk; (void)first_width; (void)schedule;
-  if (!build_summary || block_size < 1 || branching < 2 || top < 0) return 0;
-  Geometry g = level_geometry(N, block_size, branching, top + 1);
-  return align_up(B * g.total * H * D * elem_size(dtype), 256);
+}  // extern "C"
+
+namespace pisa {
+
+// Workspace layout of pisa_select_blocks.  The grouped tensor-core path needs
+// the leaf candidates, their masks and scores, the bucket counters and the
+// tile list; the fused path needs only the pyramid (when built here).
+struct SelectPlan {
+  bool grouped_tc = false;
+  Geometry geo{};
+  int64_t W0 = 0, NF = 0, NP = 0, nwin = 0, TW = 4096, RT = 0, rows = 0, num_buckets = 0, capacity = 0;
+  int64_t pyramid_off = 0, cand_off = 0, flags_off = 0, scores_off = 0, counts_off = 0,
+          cursors_off = 0, offsets_off = 0, misc_off = 0, owner_off = 0, req_off = 0, total = 0;
+};
+
+static bool grouped_tc_eligible(int64_t Hq, int64_t H, int64_t D, int dtype, int method,
+                                int64_t C, int64_t br, int schedule) {
+  const int64_t G = Hq / H;
+  return schedule == PISA_SCHEDULE_GROUPED && (dtype == PISA_BF16 || dtype == PISA_F16) &&
+         (method == PISA_METHOD_PISA || method == PISA_METHOD_PISA2) && is_pow2(G) && G <= 32 &&
+         D % 8 == 0 && D <= 256 && br * C <= 512;
+}
+
+static SelectPlan plan_select(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t N,
+                              int dtype, int method, int64_t C, int64_t br, int64_t K, int64_t top,
+                              int64_t fw, int schedule, int build_summary) {
+  SelectPlan p;
+  p.geo = level_geometry(N, C, br, top + 1);
+  int64_t off = 0;
+  if (build_summary) {
+    p.pyramid_off = off;
+    off += align_up(B * p.geo.total * H * D * elem_size(dtype), 256);
+  }
+  p.grouped_tc = grouped_tc_eligible(Hq, H, D, dtype, method, C, br, schedule);
+  if (p.grouped_tc) {
+    p.W0 = top == 0 ? fw : K * br;
+    p.NF = p.W0 / br;
+    p.NP = top == 0 ? fw / br : p.geo.sizes[1];
+    p.nwin = (Tq + p.TW - 1) / p.TW;
+    p.RT = 128 / (Hq / H);
+    p.rows = B * Tq * H;
+    p.num_buckets = B * p.nwin * H * p.NP;
+    p.capacity = (p.rows * p.NF + p.RT - 1) / p.RT + p.num_buckets;
+    if (p.rows * p.NF >= (int64_t(1) << 31)) p.grouped_tc = false;
+  }
+  if (p.grouped_tc) {
+    const int64_t slots = p.rows * p.W0;
+    p.cand_off = off; off += align_up(slots * 4, 256);
+    p.flags_off = off; off += align_up(slots, 256);
+    p.scores_off = off; off += align_up(slots * 4, 256);
+    p.counts_off = off; off += align_up(p.num_buckets * 4, 256);
+    p.cursors_off = off; off += align_up(p.num_buckets * 4, 256);
+    p.offsets_off = off; off += align_up(p.num_buckets * 4, 256);
+    p.misc_off = off; off += 256;
+    p.owner_off = off; off += align_up(p.capacity * 4, 256);
+    p.req_off = off; off += align_up(p.capacity * p.RT * 4, 256);
+  }
+  p.total = off;
+  return p;
+}
+
+}  // namespace pisa
+
+extern "C" {
+
+int64_t pisa_select_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D,
+                                    int64_t N, int dtype, int method, int64_t block_size,
+                                    int64_t branching, int64_t topk, int64_t top,
+                                    int64_t first_width, int schedule, int build_summary) {
+  if (B <= 0 || Tq <= 0 || Hq <= 0 || H <= 0 || D <= 0 || N <= 0 || block_size < 1 ||
+      branching < 2 || top < 0 || top >= kMaxLevels || Hq % H)
+    return 0;
+  return plan_select(B, Tq, Hq, H, D, N, dtype, method, block_size, branching, topk, top,
+                     first_width, schedule, build_summary).total;
 }
 
 int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, const void* keys,
@@ -163,15 +229,19 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
   if (!rows_aligned(q, dtype, q_sb, q_st, q_sh) || !rows_aligned(keys, dtype, key_sb, key_st, key_sh))
     return fail(PISA_ERR_UNSUPPORTED, "q and key rows must be 16-byte aligned");
 
+  const SelectPlan plan = plan_select(B, Tq, Hq, H, D, N, dtype, method, block_size, branching,
+                                      topk, top, first_width, schedule, summary == nullptr);
+  if (plan.total > 0 && (!workspace || workspace_bytes < plan.total))
+    return fail(PISA_ERR_INVALID, "workspace too small");
+  char* ws = static_cast<char*>(workspace);
+
   RouteArgs a{};
   if (summary == nullptr) {
-    Geometry g = level_geometry(N, block_size, branching, top + 1);
-    const int64_t need = align_up(B * g.total * H * D * elem_size(dtype), 256);
-    if (!workspace || workspace_bytes < need) return fail(PISA_ERR_INVALID, "workspace too small");
+    const Geometry& g = plan.geo;
     int rc = build_pyramid(keys, dtype, B, N, H, D, key_sb, key_st, key_sh, block_size, branching,
-                           top + 1, workspace, g.total * H * D, g.offsets, 0, s);
+                           top + 1, ws + plan.pyramid_off, g.total * H * D, g.offsets, 0, s);
     if (rc) return rc;
-    a.summary = workspace;
+    a.summary = ws + plan.pyramid_off;
     a.s_sb = g.total * H * D;
     for (int l = 0; l <= top; ++l) { a.levels.offset[l] = g.offsets[l]; a.levels.size[l] = int32_t(g.sizes[l]); }
   } else {
@@ -198,8 +268,46 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
   a.scale = float(scale);
   a.c2 = float(0.5 * scale * scale);
   a.out_ids = out_ids;
-  a.coarse_only = 0;
-  return route(a, dtype, s);
+  if (!plan.grouped_tc) {
+    a.coarse_only = 0;
+    return route(a, dtype, s);
+  }
+  // grouped: coarse levels -> leaf candidates + masks, then tensor-core leaf scoring
+  a.coarse_only = 1;
+  a.W0 = int(plan.W0);
+  a.candidates = reinterpret_cast<int32_t*>(ws + plan.cand_off);
+  a.flags = reinterpret_cast<uint8_t*>(ws + plan.flags_off);
+  int rc = route(a, dtype, s);
+  if (rc) return rc;
+  GroupArgs g{};
+  g.q = q; g.q_sb = q_sb; g.q_st = q_st; g.q_sh = q_sh;
+  g.keys = keys; g.k_sb = key_sb; g.k_st = key_st; g.k_sh = key_sh;
+  g.positions = positions; g.pos_offset = position_offset;
+  g.B = int(B); g.T = int(Tq); g.H = int(H); g.G = int(Hq / H); g.D = int(D);
+  g.Dp = int((D + 63) / 64 * 64); g.N = int(N); g.C = int(block_size); g.K = int(topk);
+  g.br = int(branching); g.W0 = int(plan.W0); g.NF = int(plan.NF); g.NP = int(plan.NP);
+  g.nwin = int(plan.nwin); g.TW = int(plan.TW); g.RT = int(plan.RT);
+  g.method = method; g.bf16 = dtype == PISA_BF16 ? 1 : 0;
+  g.scale = a.scale; g.c2 = a.c2;
+  g.cand = a.candidates; g.flags = a.flags;
+  g.scores = reinterpret_cast<float*>(ws + plan.scores_off);
+  g.counts = reinterpret_cast<int32_t*>(ws + plan.counts_off);
+  g.cursors = reinterpret_cast<int32_t*>(ws + plan.cursors_off);
+  g.offsets = reinterpret_cast<int32_t*>(ws + plan.offsets_off);
+  g.num_buckets = plan.num_buckets;
+  g.total_tiles_w = reinterpret_cast<int32_t*>(ws + plan.misc_off);
+  g.total_tiles = g.total_tiles_w;
+  g.status = reinterpret_cast<int*>(ws + plan.misc_off + 4);
+  g.tile_owner_w = reinterpret_cast<int32_t*>(ws + plan.owner_off);
+  g.tile_owner = g.tile_owner_w;
+  g.tile_req_w = reinterpret_cast<int32_t*>(ws + plan.req_off);
+  g.tile_req = g.tile_req_w;
+  g.tile_capacity = plan.capacity;
+  g.tiles_per_cta = 8;
+  const int64_t nk = branching * block_size;
+  g.tmem_cols = nk <= 32 ? 32 : nk <= 64 ? 64 : nk <= 128 ? 128 : nk <= 256 ? 256 : 512;
+  g.out_ids = out_ids;
+  return grouped_leaf(g, dtype, s);
 }
 
 int pisa_sparse_attn_fwd(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, const void* k,

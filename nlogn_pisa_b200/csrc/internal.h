@@ -44,11 +44,47 @@ struct RouteArgs {
   float scale, c2;
   int64_t* out_ids;     // [B,T,H,K] when the leaf level is scored here
   int32_t* candidates;  // [B,T,H,W0] when only the coarse levels run here
+  uint8_t* flags;       // [B,T,H,W0] leaf masks: bit0 valid, bit1 forced, bit2 scoreable
   int W0;
   int coarse_only;
 };
 
 int route(const RouteArgs& a, int dtype, cudaStream_t stream);
+
+// Grouped leaf scoring: requests (row, family) bucketed by (batch, token
+// window, KV head, level-1 survivor), scored on the tensor cores, then the
+// final top-K.  Arrays are workspace slices laid out by the C entry point.
+struct GroupArgs {
+  const void* q;
+  int64_t q_sb, q_st, q_sh;
+  const void* keys;
+  int64_t k_sb, k_st, k_sh;
+  const int64_t* positions;
+  int64_t pos_offset;
+  int B, T, H, G, D, Dp, N, C, K, br, W0, NF, NP, nwin, TW, RT;
+  int method, bf16;
+  float scale, c2;
+  const int32_t* cand;
+  const uint8_t* flags;
+  float* scores;
+  int32_t* counts;
+  int32_t* cursors;
+  int32_t* offsets;
+  int64_t num_buckets;
+  const int32_t* tile_owner;
+  const int32_t* tile_req;
+  const int32_t* total_tiles;
+  int32_t* tile_owner_w;
+  int32_t* tile_req_w;
+  int32_t* total_tiles_w;
+  int64_t tile_capacity;
+  int tiles_per_cta;
+  int tmem_cols;
+  int64_t* out_ids;
+  int* status;
+};
+
+int grouped_leaf(const GroupArgs& g, int dtype, cudaStream_t stream);
 
 struct AttnArgs {
   const void* q;

@@ -264,8 +264,15 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const RouteArgs a) {
     const bool identity = a.method != PISA_METHOD_PISA1 && s_valid <= a.K;
 
     if (level == 0 && a.coarse_only) {
+      // Leaf candidates with their masks: bit0 valid, bit1 forced, bit2 scoreable.
       int32_t* dst = a.candidates + int64_t(item) * a.W0;
-      for (int w = tid; w < width; w += kThreads) dst[w] = ids[w];
+      uint8_t* fdst = a.flags + int64_t(item) * a.W0;
+      for (int w = tid; w < width; w += kThreads) {
+        const int f = fl[w];
+        const bool scoreable = (f & 1) && !(f & 2) && !identity;
+        dst[w] = ids[w];
+        fdst[w] = uint8_t(f | (scoreable ? 4 : 0));
+      }
       return;
     }
 

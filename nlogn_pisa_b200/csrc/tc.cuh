@@ -1,0 +1,166 @@
+// Blackwell (sm_100a) tensor-core building blocks written as inline PTX:
+// tensor memory (TMEM) allocation, tcgen05.mma with shared-memory operand
+// descriptors, commit to an mbarrier, tcgen05.ld of the accumulator, and the
+// bounded mbarrier wait used everywhere a thread waits on asynchronous work.
+//
+// Operand layout used throughout: K-major bf16/fp16 tiles whose rows are
+// 128 bytes (64 elements) wide, stored with the 128-byte swizzle -- within
+// each 1024-byte atom of 8 rows, the 16-byte chunk c of row r lives at chunk
+// position (c ^ r).  A tile of R rows x 64 elements occupies R*128 bytes and
+// must be 1024-byte aligned; wider K is a sequence of such tiles.
+#pragma once
+
+#include <stdint.h>
+
+namespace pisa {
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Byte offset of 16-byte chunk `c` (0..7) of row `r` inside a 128B-swizzled tile.
+__device__ __forceinline__ uint32_t swizzle128(int r, int c) {
+  return uint32_t(r) * 128u + (uint32_t((c ^ (r & 7)) & 7) << 4);
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row core
+// groups 1024 bytes apart (stride byte offset), descriptor version 1.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr & 0x3FFFFu) >> 4);      // start address
+  d |= uint64_t(1) << 16;                       // leading byte offset (unused when swizzled)
+  d |= uint64_t(1024 >> 4) << 32;               // stride byte offset
+  d |= uint64_t(1) << 46;                       // version
+  d |= uint64_t(2) << 61;                       // 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with fp32 accumulation.
+// ab_bf16: 1 for bf16 operands, 0 for fp16.  Both operands K-major unless
+// b_mn_major (B stored with N contiguous, e.g. V in [keys][dims] order).
+__host__ __device__ __forceinline__ uint32_t idesc_f16(int M, int N, int ab_bf16, int b_mn_major = 0) {
+  uint32_t d = 0;
+  d |= 1u << 4;                          // D format: f32
+  d |= uint32_t(ab_bf16) << 7;           // A format
+  d |= uint32_t(ab_bf16) << 10;          // B format
+  d |= uint32_t(b_mn_major) << 16;       // B major-ness
+  d |= uint32_t(N >> 3) << 17;
+  d |= uint32_t(M >> 4) << 24;
+  return d;
+}
+
+__device__ __forceinline__ void fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Make generic-proxy shared-memory writes visible to the tensor core.
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Warp-collective: allocate `ncols` TMEM columns (power of two >= 32); the
+// base address is written to *slot (shared memory).
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+               :: "r"(smem_u32(slot)), "r"(ncols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_free(uint32_t base, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(base), "r"(ncols) : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+// Arrive on `mbar` once every MMA issued so far by this thread has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               :: "r"(smem_u32(mbar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(mbar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* mbar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(mbar)), "r"(phase) : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with parity `phase` to complete.  Returns false
+// (and the caller records a timeout status) instead of spinning forever.
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t phase, uint32_t max_tries = 1u << 22) {
+  for (uint32_t i = 0; i < max_tries; ++i)
+    if (mbar_try_wait(mbar, phase)) return true;
+  return false;
+}
+
+// 32 lanes x 32 consecutive 32-bit TMEM columns -> 32 registers per thread
+// (thread i of warp w reads lane 32*(w%4) + i), waiting for completion inside
+// the same asm statement so no consumer can be scheduled before the data lands.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Store 16 consecutive 32-bit columns of this thread's TMEM lane and wait.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n\t"
+      "tcgen05.wait::st.sync.aligned;"
+      :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+         "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]),
+         "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]; A is K-major in TMEM (lane = row).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      :: "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+// Generic descriptor with explicit byte offsets (for layout experiments and
+// MN-major operands): leading/stride byte offsets and swizzle code.
+__device__ __forceinline__ uint64_t desc_make(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t swizzle) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr & 0x3FFFFu) >> 4);
+  d |= uint64_t((lbo >> 4) & 0x3FFFu) << 16;
+  d |= uint64_t((sbo >> 4) & 0x3FFFu) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(swizzle & 7u) << 61;
+  return d;
+}
+
+}  // namespace tc
+}  // namespace pisa

@@ -210,8 +210,8 @@ def _select_unpacked(q, k, method, block_size, topk, query_offset, force_first, 
     schedule = _lib.SCHEDULES[routing_schedule]
     library = _lib.lib()
     ws_bytes = library.pisa_select_workspace_bytes(
-        batch, tokens, heads, dim, length, code, block_size, branching, topk, top, first_width,
-        schedule, 1 if summary is None else 0)
+        batch, tokens, q_heads, heads, dim, length, code, _lib.METHODS[method], block_size, branching,
+        topk, top, first_width, schedule, 1 if summary is None else 0)
     workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
     out = torch.empty((batch, tokens, heads, topk), dtype=torch.int64, device=q.device)
     with torch.cuda.device(q.device):
