@@ -194,11 +194,14 @@ def main():
             Hq, H, D, N, method, C, br, K, int(w.force_first), w.force_recent, top, first_width,
             _lib.SCHEDULES["grouped"], _lib.ptr(ids), _lib.ptr(sel_ws), sel_ws_bytes, sptr))
 
+    attn_ws_bytes = lib.pisa_sparse_attn_fwd_workspace_bytes(B, N, Hq, H, D, D, N, K, C, code)
+    attn_ws = torch.empty(max(attn_ws_bytes, 1), dtype=torch.uint8, device=device)
+
     def attend():
         _lib.check(lib.pisa_sparse_attn_fwd(
             _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3], _lib.ptr(v), *v.stride()[:3],
             _lib.ptr(ids), 8, None, 0, code, B, N, Hq, H, D, D, N, K, C, float(scale), 1,
-            _lib.ptr(out), _lib.ptr(lse), sptr))
+            _lib.ptr(out), _lib.ptr(lse), _lib.ptr(attn_ws), attn_ws_bytes, sptr))
 
     stages = (("pyramid", pyramid), ("select", select), ("attention", attend))
     for _ in range(max(args.warmup, 3)):

@@ -149,6 +149,9 @@ PISA_API int64_t pisa_select_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, 
  * out: [B,Tq,Hq,Dv] in dtype (contiguous); lse: [B,Tq,Hq] fp32 natural-log
  *   log-sum-exp of the scaled logits (-inf for rows without a visible key,
  *   whose output is 0).  lse may be NULL.
+ * workspace: pisa_sparse_attn_fwd_workspace_bytes(...) bytes enable the
+ *   block-bucketed tensor-core path for fp16/bf16 prefill; with NULL (or when
+ *   that size is 0) the per-query gather kernels run.
  */
 PISA_API int pisa_sparse_attn_fwd(const void *q, int64_t q_sb, int64_t q_st, int64_t q_sh, const void *k,
                          int64_t k_sb, int64_t k_st, int64_t k_sh, const void *v, int64_t v_sb,
@@ -156,7 +159,13 @@ PISA_API int pisa_sparse_attn_fwd(const void *q, int64_t q_sb, int64_t q_st, int
                          const int64_t *positions, int64_t position_offset, int dtype, int64_t B,
                          int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t Dv, int64_t N,
                          int64_t S, int64_t block_size, float scale, int causal, void *out,
-                         float *lse, pisa_stream_t stream);
+                         float *lse, void *workspace, int64_t workspace_bytes,
+                         pisa_stream_t stream);
+
+/* Workspace bytes of pisa_sparse_attn_fwd for these shapes (0: none needed). */
+PISA_API int64_t pisa_sparse_attn_fwd_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H,
+                                                      int64_t D, int64_t Dv, int64_t N, int64_t S,
+                                                      int64_t block_size, int dtype);
 
 /*
  * Backward of pisa_sparse_attn_fwd: dq [B,Tq,Hq,D], dk/dv [B,N,H,D|Dv] in

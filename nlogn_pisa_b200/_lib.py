@@ -37,7 +37,9 @@ SIGNATURES = {
                                 _P, _L, _P]),
     "pisa_select_workspace_bytes": (_L, [_L, _L, _L, _L, _L, _L, _I, _I, _L, _L, _L, _L, _L, _I, _I]),
     "pisa_sparse_attn_fwd": (_I, [_P, _L, _L, _L, _P, _L, _L, _L, _P, _L, _L, _L, _P, _I, _P, _L,
-                                  _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _F, _I, _P, _P, _P]),
+                                  _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _F, _I, _P, _P, _P, _L,
+                                  _P]),
+    "pisa_sparse_attn_fwd_workspace_bytes": (_L, [_L, _L, _L, _L, _L, _L, _L, _L, _L, _I]),
     "pisa_sparse_attn_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _L, _I, _L, _L, _L, _L, _L,
                                   _L, _L, _L, _L, _F, _I, _P, _P, _P, _P, _L, _P]),
     "pisa_sparse_attn_bwd_workspace_bytes": (_L, [_L, _L, _L, _L, _L, _L, _L]),

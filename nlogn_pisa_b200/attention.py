@@ -32,12 +32,17 @@ def attention_forward(q, k, v, indices, block_size, scale, positions, offset, ca
     heads, length, dim_v = k.shape[2], k.shape[1], v.shape[-1]
     out = torch.empty((batch, tokens, q_heads, dim_v), dtype=q.dtype, device=q.device)
     lse = torch.empty((batch, tokens, q_heads), dtype=torch.float32, device=q.device)
+    library = _lib.lib()
+    ws_bytes = library.pisa_sparse_attn_fwd_workspace_bytes(
+        batch, tokens, q_heads, heads, dim, dim_v, length, indices.shape[-1], block_size, code)
+    workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
     with torch.cuda.device(q.device):
-        _lib.check(_lib.lib().pisa_sparse_attn_fwd(
+        _lib.check(library.pisa_sparse_attn_fwd(
             _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3], _lib.ptr(v), *v.stride()[:3],
             _lib.ptr(indices), indices.element_size(), _lib.ptr(positions), offset, code, batch,
             tokens, q_heads, heads, dim, dim_v, length, indices.shape[-1], block_size, float(scale),
-            int(bool(causal)), _lib.ptr(out), _lib.ptr(lse), _lib.stream_of(q.device)))
+            int(bool(causal)), _lib.ptr(out), _lib.ptr(lse), _lib.ptr(workspace), ws_bytes,
+            _lib.stream_of(q.device)))
     return out, lse
 
 

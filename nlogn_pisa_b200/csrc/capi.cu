@@ -310,23 +310,113 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
   return grouped_leaf(g, dtype, s);
 }
 
+}  // extern "C"
+
+namespace pisa {
+
+// Workspace layout of the bucketed tensor-core attention forward (one token
+// chunk at a time; the partials of a chunk are bounded to about 2 GiB).
+struct AttnPlan {
+  bool tc = false;
+  int64_t TW = 4096, chunk = 0, NB = 0, RT = 0, num_buckets = 0, capacity = 0;
+  int64_t p_col = 0, o_col = 0, tmem_cols = 0;
+  int64_t counts_off = 0, cursors_off = 0, offsets_off = 0, misc_off = 0, owner_off = 0,
+          req_off = 0, po_off = 0, pml_off = 0, total = 0;
+};
+
+static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t Dv,
+                          int64_t N, int64_t S, int64_t C, int dtype) {
+  AttnPlan p;
+  const int64_t G = Hq / H;
+  p.p_col = C;
+  p.o_col = (C + C / 2 + 31) / 32 * 32;
+  const int64_t cols = p.o_col + Dv;
+  p.tmem_cols = cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
+  p.tc = (dtype == PISA_BF16 || dtype == PISA_F16) && is_pow2(G) && G <= 32 && D % 16 == 0 &&
+         Dv % 16 == 0 && D <= 256 && Dv <= 256 && is_pow2(C) && C >= 16 && C <= 256 &&
+         cols <= 512 && S > 0 && B * Tq * H * S >= 4096;
+  if (!p.tc) return p;
+  const int64_t per_token = H * S * G * (Dv * elem_size(dtype) + 8);
+  const int64_t fit = ((int64_t(1) << 31) / per_token) / p.TW * p.TW;
+  p.chunk = std::min<int64_t>(Tq, std::max<int64_t>(p.TW, fit));
+  p.NB = (N + C - 1) / C;
+  p.RT = 128 / G;
+  const int64_t nwin = (p.chunk + p.TW - 1) / p.TW;
+  p.num_buckets = B * nwin * H * p.NB;
+  const int64_t reqs = B * p.chunk * H * S;
+  if (reqs >= (int64_t(1) << 31)) { p.tc = false; return p; }
+  p.capacity = (reqs + p.RT - 1) / p.RT + p.num_buckets;
+  int64_t off = 0;
+  p.counts_off = off; off += align_up(p.num_buckets * 4, 256);
+  p.cursors_off = off; off += align_up(p.num_buckets * 4, 256);
+  p.offsets_off = off; off += align_up(p.num_buckets * 4, 256);
+  p.misc_off = off; off += 256;
+  p.owner_off = off; off += align_up(p.capacity * 4, 256);
+  p.req_off = off; off += align_up(p.capacity * p.RT * 4, 256);
+  p.po_off = off; off += align_up(reqs * G * Dv * elem_size(dtype), 256);
+  p.pml_off = off; off += align_up(reqs * G * 8, 256);
+  p.total = off;
+  return p;
+}
+
+}  // namespace pisa
+
+extern "C" {
+
+int64_t pisa_sparse_attn_fwd_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H,
+                                             int64_t D, int64_t Dv, int64_t N, int64_t S,
+                                             int64_t block_size, int dtype) {
+  if (B <= 0 || Tq <= 0 || Hq <= 0 || H <= 0 || Hq % H || block_size < 1) return 0;
+  return plan_attn(B, Tq, Hq, H, D, Dv, N, S, block_size, dtype).total;
+}
+
 int pisa_sparse_attn_fwd(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, const void* k,
                          int64_t k_sb, int64_t k_st, int64_t k_sh, const void* v, int64_t v_sb,
                          int64_t v_st, int64_t v_sh, const void* indices, int index_bytes,
                          const int64_t* positions, int64_t position_offset, int dtype, int64_t B,
                          int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t Dv, int64_t N,
                          int64_t S, int64_t block_size, float scale, int causal, void* out,
-                         float* lse, pisa_stream_t stream) {
+                         float* lse, void* workspace, int64_t workspace_bytes,
+                         pisa_stream_t stream) {
   if (dtype < PISA_F32 || dtype > PISA_F16) return fail(PISA_ERR_UNSUPPORTED, "CUDA attention supports FP16, BF16 and FP32");
   if (B <= 0 || Tq <= 0 || Hq <= 0 || H <= 0 || D <= 0 || Dv <= 0 || N <= 0) return fail(PISA_ERR_INVALID, "nonempty tensors are required");
   if (Hq % H) return fail(PISA_ERR_INVALID, "a whole number of query heads per KV head is required");
   if (S < 0) return fail(PISA_ERR_INVALID, "negative slot count");
   if (block_size < 1) return fail(PISA_ERR_INVALID, "invalid block_size");
   if (index_bytes != 4 && index_bytes != 8) return fail(PISA_ERR_INVALID, "indices must be int32 or int64");
-  if (D % 8 || D > 256 || Dv > 256) return fail(PISA_ERR_UNSUPPORTED, "head_dim must be a multiple of 8 and at most 256");
-  if (!rows_aligned(q, dtype, q_sb, q_st, q_sh) || !rows_aligned(k, dtype, k_sb, k_st, k_sh))
-    return fail(PISA_ERR_UNSUPPORTED, "q and key rows must be 16-byte aligned");
+  if (D % 8 || Dv % 8 || D > 256 || Dv > 256) return fail(PISA_ERR_UNSUPPORTED, "head_dim must be a multiple of 8 and at most 256");
+  if (!rows_aligned(q, dtype, q_sb, q_st, q_sh) || !rows_aligned(k, dtype, k_sb, k_st, k_sh) ||
+      !rows_aligned(v, dtype, v_sb, v_st, v_sh))
+    return fail(PISA_ERR_UNSUPPORTED, "q, key and value rows must be 16-byte aligned");
   if (!out) return fail(PISA_ERR_INVALID, "out is required");
+  const AttnPlan plan = plan_attn(B, Tq, Hq, H, D, Dv, N, S, block_size, dtype);
+  if (plan.tc && workspace && workspace_bytes >= plan.total) {
+    char* ws = static_cast<char*>(workspace);
+    AttnTcArgs a{};
+    a.q = q; a.q_sb = q_sb; a.q_st = q_st; a.q_sh = q_sh;
+    a.k = k; a.k_sb = k_sb; a.k_st = k_st; a.k_sh = k_sh;
+    a.v = v; a.v_sb = v_sb; a.v_st = v_st; a.v_sh = v_sh;
+    a.indices = indices; a.index_bytes = index_bytes;
+    a.positions = positions; a.pos_offset = position_offset;
+    a.B = int(B); a.T = int(Tq); a.Hq = int(Hq); a.H = int(H); a.G = int(Hq / H);
+    a.D = int(D); a.Dp = int((D + 63) / 64 * 64); a.Dv = int(Dv); a.Dvp = int((Dv + 63) / 64 * 64);
+    a.N = int(N); a.S = int(S); a.C = int(block_size); a.NB = int(plan.NB); a.TW = int(plan.TW);
+    a.RT = int(plan.RT); a.chunk = int(plan.chunk);
+    a.scale = scale; a.causal = causal ? 1 : 0; a.bf16 = dtype == PISA_BF16 ? 1 : 0;
+    a.counts = reinterpret_cast<int32_t*>(ws + plan.counts_off);
+    a.cursors = reinterpret_cast<int32_t*>(ws + plan.cursors_off);
+    a.offsets = reinterpret_cast<int32_t*>(ws + plan.offsets_off);
+    a.total_tiles = reinterpret_cast<int32_t*>(ws + plan.misc_off);
+    a.status = reinterpret_cast<int*>(ws + plan.misc_off + 4);
+    a.tile_owner = reinterpret_cast<int32_t*>(ws + plan.owner_off);
+    a.tile_req = reinterpret_cast<int32_t*>(ws + plan.req_off);
+    a.part_o = ws + plan.po_off;
+    a.part_ml = reinterpret_cast<float*>(ws + plan.pml_off);
+    a.tiles_per_cta = 8;
+    a.tmem_cols = int(plan.tmem_cols); a.p_col = int(plan.p_col); a.o_col = int(plan.o_col);
+    a.out = out; a.lse = lse;
+    return attn_fwd_tc(a, dtype, static_cast<cudaStream_t>(stream));
+  }
   AttnArgs a{};
   a.q = q; a.q_sb = q_sb; a.q_st = q_st; a.q_sh = q_sh;
   a.k = k; a.k_sb = k_sb; a.k_st = k_st; a.k_sh = k_sh;

@@ -112,6 +112,40 @@ struct AttnArgs {
 };
 
 int attn_fwd(const AttnArgs& a, int dtype, cudaStream_t stream);
+
+// Bucketed tensor-core attention forward (prefill): see attn_tc.cu.
+struct AttnTcArgs {
+  const void* q;
+  int64_t q_sb, q_st, q_sh;
+  const void* k;
+  int64_t k_sb, k_st, k_sh;
+  const void* v;
+  int64_t v_sb, v_st, v_sh;
+  const void* indices;
+  int index_bytes;
+  const int64_t* positions;
+  int64_t pos_offset;
+  int B, T, Hq, H, G, D, Dp, Dv, Dvp, N, S, C, NB, TW, RT;
+  int chunk, t0, tlen, nwin;
+  float scale;
+  int causal, bf16;
+  int32_t* counts;
+  int32_t* cursors;
+  int32_t* offsets;
+  int64_t num_buckets;
+  int32_t* tile_owner;
+  int32_t* tile_req;
+  int32_t* total_tiles;
+  int64_t capacity;
+  int tiles_per_cta, tmem_cols, p_col, o_col;
+  void* part_o;
+  float* part_ml;
+  void* out;
+  float* lse;
+  int* status;
+};
+
+int attn_fwd_tc(const AttnTcArgs& a, int dtype, cudaStream_t stream);
 int attn_bwd(const AttnArgs& a, int dtype, void* dk, void* dv, cudaStream_t stream);
 
 }  // namespace pisa

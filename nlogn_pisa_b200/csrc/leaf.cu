@@ -21,6 +21,7 @@
 // the tile list has a fixed capacity and the kernels read the real count.
 #include <algorithm>
 
+#include "bucket.cuh"
 #include "internal.h"
 #include "tc.cuh"
 
@@ -29,7 +30,6 @@ namespace pisa {
 namespace {
 
 constexpr int kLeafThreads = 128;
-constexpr int kScanThreads = 1024;
 
 __device__ __forceinline__ void decode_row(int64_t row, int T, int H, int& b, int& t, int& h) {
   h = int(row % H);
@@ -55,42 +55,6 @@ __global__ void family_count_kernel(const GroupArgs g, int32_t* __restrict__ cou
   atomicAdd(counts + bucket, 1);
 }
 
-// Exclusive scan of ceil(count / RT) over all buckets in one CTA: each warp
-// owns a contiguous segment (coalesced 32-wide chunks), warp totals are
-// scanned in shared memory, then offsets are written in a second pass.
-__global__ void __launch_bounds__(kScanThreads)
-tile_scan_kernel(const int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
-                 int32_t* __restrict__ total_tiles, int64_t nb, int RT) {
-  __shared__ int64_t warp_base[kScanThreads / 32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int warps = kScanThreads / 32;
-  const int64_t seg = (nb + warps - 1) / warps;
-  const int64_t s0 = min64(int64_t(warp) * seg, nb), s1 = min64(s0 + seg, nb);
-  int64_t sum = 0;
-  for (int64_t i = s0 + lane; i < s1; i += 32) sum += (counts[i] + RT - 1) / RT;
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(kFull, sum, o);
-  if (lane == 0) warp_base[warp] = sum;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int64_t acc = 0;
-    for (int w = 0; w < warps; ++w) { const int64_t v = warp_base[w]; warp_base[w] = acc; acc += v; }
-    *total_tiles = int32_t(acc);
-  }
-  __syncthreads();
-  int64_t carry = warp_base[warp];
-  for (int64_t base = s0; base < s1; base += 32) {
-    const int64_t i = base + lane;
-    const int v = i < s1 ? (counts[i] + RT - 1) / RT : 0;
-    int incl = v;
-    for (int o = 1; o < 32; o <<= 1) {
-      const int n = __shfl_up_sync(kFull, incl, o);
-      if (lane >= o) incl += n;
-    }
-    if (i < s1) offsets[i] = int32_t(carry + incl - v);
-    carry += __shfl_sync(kFull, incl, 31);
-  }
-}
-
 __global__ void family_scatter_kernel(const GroupArgs g, const int32_t* __restrict__ offsets,
                                       int32_t* __restrict__ cursors, int32_t* __restrict__ tile_owner,
                                       int32_t* __restrict__ tile_req) {
@@ -111,16 +75,6 @@ __global__ void family_scatter_kernel(const GroupArgs g, const int32_t* __restri
   const int64_t tile = offsets[bucket] + pos / g.RT;
   tile_req[tile * g.RT + pos % g.RT] = int32_t(idx);
   if (pos % g.RT == 0) tile_owner[tile] = int32_t(bucket);
-}
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.wait_all;" ::: "memory");
-}
-__device__ __forceinline__ void st_zero16(uint32_t dst) {
-  asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" :: "r"(dst), "r"(0) : "memory");
 }
 
 // One CTA walks `tiles_per_cta` consecutive tiles, restaging the family keys
@@ -223,36 +177,24 @@ __global__ void __launch_bounds__(kLeafThreads) leaf_tc_kernel(const GroupArgs g
     for (int j = 0; j < g.br; ++j) {
       const int64_t key0 = (int64_t(p) * g.br + j) * g.C;
       const int col0 = j * g.C;
+      const int valid_keys = int(min64(g.C, max(int64_t(0), g.N - key0)));
       float score;
       if (g.method == PISA_METHOD_PISA) {
         float mx = -INFINITY;
-        for (int cc = 0; cc < g.C; cc += 32) {
-          float v[32];
-          tc::tmem_ld32(tmem + lane_base + col0 + cc, v);
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (key0 + cc + i < g.N) mx = fmaxf(mx, v[i] * g.scale);
-        }
+        for_columns(tmem + lane_base + col0, g.C, [&](int c, float x) {
+          if (c < valid_keys) mx = fmaxf(mx, x * g.scale);
+        });
         float sum = 0.f;
-        for (int cc = 0; cc < g.C; cc += 32) {
-          float v[32];
-          tc::tmem_ld32(tmem + lane_base + col0 + cc, v);
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (key0 + cc + i < g.N) sum += expf(v[i] * g.scale - mx);
-        }
+        for_columns(tmem + lane_base + col0, g.C, [&](int c, float x) {
+          if (c < valid_keys) sum += expf(x * g.scale - mx);
+        });
         score = mx + logf(sum);
       } else {
         float s1 = 0.f, s2 = 0.f;
-        int cnt = 0;
-        for (int cc = 0; cc < g.C; cc += 32) {
-          float v[32];
-          tc::tmem_ld32(tmem + lane_base + col0 + cc, v);
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (key0 + cc + i < g.N) { s1 += v[i]; s2 += v[i] * v[i]; ++cnt; }
-        }
-        const float n = float(cnt > 0 ? cnt : 1);
+        for_columns(tmem + lane_base + col0, g.C, [&](int c, float x) {
+          if (c < valid_keys) { s1 += x; s2 += x * x; }
+        });
+        const float n = float(valid_keys > 0 ? valid_keys : 1);
         const float mean = s1 / n, var = fmaxf(s2 / n - mean * mean, 0.f);
         score = g.scale * mean + g.c2 * var;
       }

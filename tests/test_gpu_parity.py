@@ -218,3 +218,35 @@ def test_sampled_rows_at_32k(cuda_device):
     _check_ids(got, want, trace, min_exact=0.95)
     ref_out, _ = O.sparse_attention(qn[:, rows], kn, vn, got, C, positions=pos)
     np.testing.assert_allclose(out.float().cpu().numpy()[:, rows], ref_out, rtol=0, atol=2e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [
+    # B, T, N, Hq, H, D, C, S, causal, offset
+    (1, 1500, 1500, 8, 2, 64, 64, 8, True, None),
+    (2, 700, 1000, 4, 1, 128, 32, 12, True, 300),
+    (1, 900, 900, 16, 1, 64, 16, 16, False, None),
+    (1, 1200, 1337, 2, 2, 128, 128, 6, True, 137),
+])
+def test_tensor_core_attention_matches_oracle(cuda_device, dtype, shape):
+    """Bucketed tensor-core attention on arbitrary indices: -1, duplicates, blocks past
+    the causal edge, tails (N % C != 0), query offsets, non-causal."""
+    import nlogn_pisa_b200 as P
+    from nlogn_pisa_b200 import _lib
+
+    B, T, N, Hq, H, D, C, S, causal, offset = shape
+    g = torch.Generator().manual_seed(sum(shape[:8]))
+    q = torch.randn(B, T, Hq, D, generator=g).to(dtype)
+    k = torch.randn(B, N, H, D, generator=g).to(dtype)
+    v = torch.randn(B, N, H, D, generator=g).to(dtype)
+    blocks = -(-N // C)
+    ids = torch.randint(-1, blocks + 1, (B, T, H, S), generator=g)
+    ids[..., 1] = ids[..., 0]                     # duplicates count twice
+    code = _lib.DTYPES[dtype]
+    assert _lib.lib().pisa_sparse_attn_fwd_workspace_bytes(B, T, Hq, H, D, D, N, S, C, code) > 0
+    out = P.sparse_attention(q.cuda(), k.cuda(), v.cuda(), ids.cuda(), block_size=C,
+                             query_offset=offset, causal=causal)
+    pos = O.query_positions(B, T, N, offset)
+    want, _ = O.sparse_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), ids.numpy(), C,
+                                 positions=pos, causal=causal)
+    np.testing.assert_allclose(out.float().cpu().numpy(), want, rtol=0, atol=2e-2)
