@@ -30,8 +30,6 @@ namespace pisa {
 
 namespace {
 
-constexpr int kThreads = 128;
-
 __device__ __forceinline__ int64_t index_at(const void* p, int bytes, int64_t i) {
   return bytes == 4 ? int64_t(static_cast<const int32_t*>(p)[i]) : static_cast<const int64_t*>(p)[i];
 }
@@ -100,198 +98,292 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
+// Warp roles (one persistent CTA per SM):
+//   warps 0-3 / 4-7  epilogue groups: group (tile % 2) turns S into P (softmax
+//                    in registers, P back to TMEM) and then O into the partial;
+//                    thread = TMEM lane = query-head row
+//   warps 8-11       producers: query rows into a 2-stage ring; block K/V
+//   warp 12          MMA issue: S(i+1) = Q K^T is issued before O(i) = P V
+// mbarriers per stage/buffer: q_full/q_empty (query stages), s_full, p_full,
+// o_full, acc_empty (TMEM buffer of S, P and O).  All waits are bounded.
+constexpr int kEpiWarps = 8, kLoadWarps = 4, kMmaWarp = 12;
+constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
+
 template <typename T>
-__global__ void __launch_bounds__(kThreads) attn_tc_kernel(const AttnTcArgs a) {
+__global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int qch = a.Dp / 64, vch = a.Dvp / 64;
-  uint8_t* Qs = smem;                        // [qch][128 rows][128 B]
-  uint8_t* Ks = Qs + qch * 128 * 128;        // [qch][C keys][128 B]
-  uint8_t* Vs = Ks + qch * a.C * 128;        // [vch][C keys][128 B] (value dims contiguous)
-  __shared__ uint64_t mbar;
+  const int q_stage_bytes = qch * 128 * 128;
+  // two K/V buffers, each [qch][C keys][128 B] of keys then [vch][C keys][128 B]
+  // of values (value dims contiguous); a block change switches buffers
+  const int kv_bytes = (qch + vch) * a.C * 128;
+  uint8_t* KV = smem + 2 * q_stage_bytes;
+  __shared__ uint64_t q_full[2], q_empty[2], s_full[2], p_full[2], o_full[2], acc_empty[2];
   __shared__ uint32_t tmem_slot;
-  __shared__ int32_t s_req[128];
+  __shared__ int64_t s_qoff[2][128];
+  __shared__ int s_kvb[2];
+  __shared__ int s_fail;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int total = *a.total_tiles;
-  const int first = blockIdx.x * a.tiles_per_cta;
-  if (first >= total) return;
-  const int last = min(first + a.tiles_per_cta, total);
+  const int per = (total + gridDim.x - 1) / gridDim.x;
+  const int first = blockIdx.x * per;
+  const int last = min(first + per, total);
+  if (first >= last) return;
+  const int ntiles = last - first;
+  const int nacc = a.nacc;
 
-  if (tid == 0) tc::mbar_init(&mbar, 1);
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&q_full[i], kLoadWarps * 32);
+      tc::mbar_init(&q_empty[i], 1);
+      tc::mbar_init(&s_full[i], 1);
+      tc::mbar_init(&p_full[i], 128);
+      tc::mbar_init(&o_full[i], 1);
+      tc::mbar_init(&acc_empty[i], 128);
+    }
+    s_fail = 0;
+    tc::fence_barrier_init();
+  }
   if (warp == 0) tc::tmem_alloc(&tmem_slot, a.tmem_cols);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_slot;
-  const uint32_t lane_base = (uint32_t(warp) * 32) << 16;
-  const uint32_t qs_addr = tc::smem_u32(Qs), ks_addr = tc::smem_u32(Ks), vs_addr = tc::smem_u32(Vs);
-  const T* qbase = static_cast<const T*>(a.q);
-  const T* kbase = static_cast<const T*>(a.k);
-  const T* vbase = static_cast<const T*>(a.v);
-  T* part_o = static_cast<T*>(a.part_o);
-  const uint32_t idesc_s = tc::idesc_f16(128, a.C, a.bf16);
-  const uint32_t idesc_o = tc::idesc_f16(128, a.Dv, a.bf16, 1);
-  uint32_t phase = 0;
-  int64_t cur_kv = -1;
-  bool ok = true;
+  const uint32_t qs_addr = tc::smem_u32(smem), kv_addr = tc::smem_u32(KV);
+  const int lgG = 31 - __clz(a.G);
+  // round of tile `it` on its TMEM buffer
+  auto acc_of = [&](int it) { return nacc == 2 ? (it & 1) : 0; };
+  auto round_of = [&](int it) { return nacc == 2 ? (it >> 1) : it; };
 
-  for (int tile = first; tile < last; ++tile) {
-    const int owner = a.tile_owner[tile];
-    const int blk = owner % a.NB;
-    const int h = (owner / a.NB) % a.H;
-    const int b = owner / (a.NB * a.H * a.nwin);
-    if (tid < a.RT) s_req[tid] = a.tile_req[int64_t(tile) * a.RT + tid];
-    const int64_t kv_key = (int64_t(b) * a.H + h) * a.NB + blk;
-    if (kv_key != cur_kv) {
-      const int64_t tok0 = int64_t(blk) * a.C;
-      const T* kb = kbase + b * a.k_sb + int64_t(h) * a.k_sh;
-      const T* vb = vbase + b * a.v_sb + int64_t(h) * a.v_sh;
-      const int kvec = a.Dp / 8, vvec = a.Dvp / 8;
-      for (int idx = tid; idx < a.C * kvec; idx += kThreads) {
-        const int r = idx / kvec, c = idx % kvec;
-        const uint32_t dst = ks_addr + (c >> 3) * a.C * 128 + tc::swizzle128(r, c & 7);
-        const int64_t tok = tok0 + r;
-        if (tok < a.N && c < a.D / 8) cp_async16(dst, kb + tok * a.k_st + c * 8);
-        else st_zero16(dst);
-      }
-      for (int idx = tid; idx < a.C * vvec; idx += kThreads) {
-        const int r = idx / vvec, c = idx % vvec;
-        const uint32_t dst = vs_addr + (c >> 3) * a.C * 128 + tc::swizzle128(r, c & 7);
-        const int64_t tok = tok0 + r;
-        if (tok < a.N && c < a.Dv / 8) cp_async16(dst, vb + tok * a.v_st + c * 8);
-        else st_zero16(dst);
-      }
-      cur_kv = kv_key;
-    }
-    __syncthreads();  // s_req visible
-    {
-      const int qvec = a.Dp / 8;
-      for (int idx = tid; idx < 128 * qvec; idx += kThreads) {
-        const int row = idx / qvec, c = idx % qvec;
-        const int r = row / a.G, g = row % a.G;
-        const uint32_t dst = qs_addr + (c >> 3) * 128 * 128 + tc::swizzle128(row, c & 7);
-        const int req = r < a.RT ? s_req[r] : -1;
-        if (req >= 0 && c < a.D / 8) {
-          const Req q = decode_req(req, a);
-          cp_async16(dst, qbase + q.b * a.q_sb + int64_t(a.t0 + q.tl) * a.q_st +
-                              int64_t(q.h * a.G + g) * a.q_sh + c * 8);
-        } else {
-          st_zero16(dst);
+  if (warp >= kEpiWarps && warp < kMmaWarp) {
+    // ---------------- producers ----------------
+    const int ptid = tid - kEpiWarps * 32;
+    const int vpr = a.Dp / 8, vvpr = a.Dvp / 8;
+    const T* qbase = static_cast<const T*>(a.q);
+    const T* kbase = static_cast<const T*>(a.k);
+    const T* vbase = static_cast<const T*>(a.v);
+    int64_t cur_kv = -1;
+    int kvb = 1, used[2] = {0, 0};
+    for (int it = 0; it < ntiles; ++it) {
+      const int tile = first + it, s = it & 1;
+      if (!tc::mbar_wait(&q_empty[s], ((it >> 1) & 1) ^ 1)) { s_fail = 1; break; }
+      const int owner = a.tile_owner[tile];
+      const int blk = owner % a.NB;
+      const int h = (owner / a.NB) % a.H;
+      const int b = owner / (a.NB * a.H * a.nwin);
+      const int64_t kv_key = (int64_t(b) * a.H + h) * a.NB + blk;
+      if (kv_key != cur_kv) {
+        kvb ^= 1;
+        // The buffer being replaced was last read by tile it-2 or earlier:
+        // wait for that P.V (with one TMEM buffer, the in-order issue makes
+        // P.V of tile it-1 the one to wait for; it never needs tile it).
+        if (used[kvb]) {
+          const int wt = nacc == 2 ? it - 2 : it - 1;
+          if (wt >= 0 && !tc::mbar_wait(&o_full[acc_of(wt)], round_of(wt) & 1)) { s_fail = 1; break; }
         }
-      }
-    }
-    cp_async_wait_all();
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    if (tid == 0) {
-      for (int ks = 0; ks < a.Dp / 16; ++ks) {
-        const int ch = ks >> 2, off = (ks & 3) * 32;
-        tc::mma_f16(tmem, tc::desc_sw128(qs_addr + ch * 128 * 128 + off),
-                    tc::desc_sw128(ks_addr + ch * a.C * 128 + off), idesc_s, ks > 0);
-      }
-      tc::mma_commit(&mbar);
-    }
-    if (!tc::mbar_wait(&mbar, phase)) ok = false;
-    phase ^= 1;
-    tc::fence_after_sync();
-
-    // masked softmax of this thread's row; P back to TMEM in the input type
-    const int row = tid;
-    const int r = row / a.G, g = row % a.G;
-    const int req = r < a.RT ? s_req[r] : -1;
-    int nvalid = 0;
-    if (req >= 0) {
-      const Req q = decode_req(req, a);
-      int64_t limit = a.N;
-      if (a.causal) limit = min64(limit, position_of(a, q.b, a.t0 + q.tl) + 1);
-      nvalid = int(max(int64_t(0), min64(int64_t(a.C), limit - int64_t(blk) * a.C)));
-    }
-    float mx = -INFINITY;
-    for_columns(tmem + lane_base, a.C, [&](int c, float x) {
-      if (c < nvalid) mx = fmaxf(mx, x * a.scale);
-    });
-    float l = 0.f;
-    for (int c0 = 0; c0 < a.C; c0 += 32) {
-      if (a.C - c0 >= 32) {
-        float v[32];
-        tc::tmem_ld32(tmem + lane_base + c0, v);
-        uint32_t w[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = (c0 + 2 * i < nvalid) ? expf(v[2 * i] * a.scale - mx) : 0.f;
-          const float p1 = (c0 + 2 * i + 1 < nvalid) ? expf(v[2 * i + 1] * a.scale - mx) : 0.f;
-          l += p0 + p1;
-          w[i] = pack2<T>(p0, p1);
+        used[kvb] = 1;
+        const uint32_t ks_addr = kv_addr + kvb * kv_bytes, vs_addr = ks_addr + qch * a.C * 128;
+        const int64_t tok0 = int64_t(blk) * a.C;
+        const T* kb = kbase + b * a.k_sb + int64_t(h) * a.k_sh;
+        const T* vb = vbase + b * a.v_sb + int64_t(h) * a.v_sh;
+        for (int idx = ptid; idx < a.C * vpr; idx += kLoadWarps * 32) {
+          const int r = idx / vpr, c = idx - r * vpr;
+          const uint32_t dst = ks_addr + (c >> 3) * a.C * 128 + tc::swizzle128(r, c & 7);
+          const int64_t tok = tok0 + r;
+          if (tok < a.N && c * 8 < a.D) cp_async16(dst, kb + tok * a.k_st + c * 8);
+          else st_zero16(dst);
         }
-        tc::tmem_st16(tmem + lane_base + a.p_col + c0 / 2, w);
-      } else {
-        float v[16];
-        tc::tmem_ld16(tmem + lane_base + c0, v);
-        uint32_t w[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float p0 = (c0 + 2 * i < nvalid) ? expf(v[2 * i] * a.scale - mx) : 0.f;
-          const float p1 = (c0 + 2 * i + 1 < nvalid) ? expf(v[2 * i + 1] * a.scale - mx) : 0.f;
-          l += p0 + p1;
-          w[i] = pack2<T>(p0, p1);
+        for (int idx = ptid; idx < a.C * vvpr; idx += kLoadWarps * 32) {
+          const int r = idx / vvpr, c = idx - r * vvpr;
+          const uint32_t dst = vs_addr + (c >> 3) * a.C * 128 + tc::swizzle128(r, c & 7);
+          const int64_t tok = tok0 + r;
+          if (tok < a.N && c * 8 < a.Dv) cp_async16(dst, vb + tok * a.v_st + c * 8);
+          else st_zero16(dst);
         }
-        tc::tmem_st8(tmem + lane_base + a.p_col + c0 / 2, w);
+        cur_kv = kv_key;
       }
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    if (tid == 0) {
-      for (int ks = 0; ks < a.C / 16; ++ks) {
-        const uint64_t vd = tc::desc_make(vs_addr + ks * 16 * 128, uint32_t(a.C) * 128, 1024, 2);
-        tc::mma_f16_ts(tmem + a.o_col, tmem + a.p_col + ks * 8, vd, idesc_o, ks > 0);
-      }
-      tc::mma_commit(&mbar);
-    }
-    if (!tc::mbar_wait(&mbar, phase)) ok = false;
-    phase ^= 1;
-    tc::fence_after_sync();
-
-    // block-local partial: (m, l) and O / l in the input type
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    const int64_t pi = int64_t(req) * a.G + g;
-    for (int c0 = 0; c0 < a.Dv; c0 += 32) {
-      if (a.Dv - c0 >= 32) {
-        float v[32];
-        tc::tmem_ld32(tmem + lane_base + a.o_col + c0, v);
+      if (ptid < a.RT) {
+        const int req = a.tile_req[int64_t(tile) * a.RT + ptid];
+        int64_t off = -1;
         if (req >= 0) {
+          const Req q = decode_req(req, a);
+          off = q.b * a.q_sb + int64_t(a.t0 + q.tl) * a.q_st + int64_t(q.h * a.G) * a.q_sh;
+        }
+        s_qoff[s][ptid] = off;
+      }
+      if (ptid == 0) s_kvb[s] = kvb;
+      tc::named_sync(1, kLoadWarps * 32);
+      const int c = ptid & (vpr - 1);
+      const uint32_t qdst = qs_addr + s * q_stage_bytes + (c >> 3) * 128 * 128;
+      for (int row = ptid / vpr; row < 128; row += kLoadWarps * 32 / vpr) {
+        const int r = row >> lgG, gh = row & (a.G - 1);
+        const int64_t off = r < a.RT ? s_qoff[s][r] : -1;
+        const uint32_t dst = qdst + tc::swizzle128(row, c & 7);
+        if (off >= 0 && c * 8 < a.D) cp_async16(dst, qbase + off + int64_t(gh) * a.q_sh + c * 8);
+        else st_zero16(dst);
+      }
+      cp_async_wait_all();
+      tc::fence_async_smem();
+      tc::mbar_arrive(&q_full[s]);
+    }
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issue ----------------
+    if (lane == 0) {
+      const uint32_t idesc_s = tc::idesc_f16(128, a.C, a.bf16);
+      const uint32_t idesc_o = tc::idesc_f16(128, a.Dv, a.bf16, 1);
+      int kv_of[2] = {0, 0};  // K/V buffer of the last two tiles (by parity)
+      // S = Q K^T of tile `it` into its buffer
+      auto issue_s = [&](int it) -> bool {
+        const int s = it & 1, ab = acc_of(it);
+        if (!tc::mbar_wait(&q_full[s], (it >> 1) & 1)) return false;
+        if (!tc::mbar_wait(&acc_empty[ab], (round_of(it) & 1) ^ 1)) return false;
+        tc::fence_after_sync();
+        kv_of[it & 1] = s_kvb[s];
+        const uint32_t ks_addr = kv_addr + kv_of[it & 1] * kv_bytes;
+        const uint32_t qa = qs_addr + s * q_stage_bytes;
+        const uint32_t sacc = tmem + ab * a.acc_cols;
+        for (int ks = 0; ks < a.Dp / 16; ++ks) {
+          const int ch = ks >> 2, off = (ks & 3) * 32;
+          tc::mma_f16(sacc, tc::desc_sw128(qa + ch * 128 * 128 + off),
+                      tc::desc_sw128(ks_addr + ch * a.C * 128 + off), idesc_s, ks > 0);
+        }
+        tc::mma_commit(&s_full[ab]);
+        tc::mma_commit(&q_empty[s]);
+        return true;
+      };
+      // O = P V of tile `pt` once its P is in TMEM
+      auto issue_o = [&](int pt) -> bool {
+        const int ab = acc_of(pt);
+        if (!tc::mbar_wait(&p_full[ab], round_of(pt) & 1)) return false;
+        tc::fence_after_sync();
+        const uint32_t base = tmem + ab * a.acc_cols;
+        const uint32_t vs_addr = kv_addr + kv_of[pt & 1] * kv_bytes + qch * a.C * 128;
+        for (int ks = 0; ks < a.C / 16; ++ks) {
+          const uint64_t vd = tc::desc_make(vs_addr + ks * 16 * 128, uint32_t(a.C) * 128, 1024, 2);
+          tc::mma_f16_ts(base + a.o_col, base + a.p_col + ks * 8, vd, idesc_o, ks > 0);
+        }
+        tc::mma_commit(&o_full[ab]);
+        return true;
+      };
+      // Two buffers: S(i) is issued before O(i-1) so the tensor core works on
+      // tile i while the epilogue computes P(i-1).  One buffer: strictly in order.
+      for (int it = 0; it <= ntiles; ++it) {
+        bool ok = true;
+        if (nacc == 2) {
+          if (it < ntiles) ok = issue_s(it);
+          if (ok && it >= 1) ok = issue_o(it - 1);
+        } else {
+          if (it >= 1) ok = issue_o(it - 1);
+          if (ok && it < ntiles) ok = issue_s(it);
+        }
+        if (!ok) { s_fail = 1; break; }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue groups ----------------
+    const int grp = warp >> 2, quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = (uint32_t(quarter) * 32) << 16;
+    const int r = row >> lgG, g = row & (a.G - 1);
+    T* part_o = static_cast<T*>(a.part_o);
+    const float l2e = 1.4426950408889634f;
+    const float sl = a.scale * l2e;
+    // two buffers: group g takes tiles g, g+2, ...; one buffer: group 0 takes all
+    const int step = nacc == 2 ? 2 : 1;
+    for (int it = grp; it < ntiles && (nacc == 2 || grp == 0); it += step) {
+      const int ab = acc_of(it), rnd = round_of(it), tile = first + it;
+      const bool got = tc::mbar_wait(&s_full[ab], rnd & 1);
+      if (!got) s_fail = 1;
+      tc::fence_after_sync();
+      const int owner = a.tile_owner[tile];
+      const int blk = owner % a.NB;
+      const int req = r < a.RT ? a.tile_req[int64_t(tile) * a.RT + r] : -1;
+      int nvalid = 0;
+      if (req >= 0) {
+        const Req q = decode_req(req, a);
+        int64_t limit = a.N;
+        if (a.causal) limit = min64(limit, position_of(a, q.b, a.t0 + q.tl) + 1);
+        nvalid = int(max(int64_t(0), min64(int64_t(a.C), limit - int64_t(blk) * a.C)));
+      }
+      const uint32_t base = tmem + lane_base + ab * a.acc_cols;
+      float mx = -INFINITY;
+      for_columns(base, a.C, [&](int c, float x) {
+        if (c < nvalid) mx = fmaxf(mx, x);
+      });
+      const float mb = mx * sl;
+      float l = 0.f;
+      for (int c0 = 0; c0 < a.C; c0 += 32) {
+        if (a.C - c0 >= 32) {
+          float v[32];
+          tc::tmem_ld32(base + c0, v);
           uint32_t w[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) w[i] = pack2<T>(v[2 * i] * inv, v[2 * i + 1] * inv);
-          uint4* dst = reinterpret_cast<uint4*>(part_o + pi * a.Dv + c0);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-        }
-      } else {
-        float v[16];
-        tc::tmem_ld16(tmem + lane_base + a.o_col + c0, v);
-        if (req >= 0) {
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = (c0 + 2 * i < nvalid) ? exp2f(fmaf(v[2 * i], sl, -mb)) : 0.f;
+            const float p1 = (c0 + 2 * i + 1 < nvalid) ? exp2f(fmaf(v[2 * i + 1], sl, -mb)) : 0.f;
+            l += p0 + p1;
+            w[i] = pack2<T>(p0, p1);
+          }
+          tc::tmem_st16(base + a.p_col + c0 / 2, w);
+        } else {
+          float v[16];
+          tc::tmem_ld16(base + c0, v);
           uint32_t w[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) w[i] = pack2<T>(v[2 * i] * inv, v[2 * i + 1] * inv);
-          uint4* dst = reinterpret_cast<uint4*>(part_o + pi * a.Dv + c0);
-          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          for (int i = 0; i < 8; ++i) {
+            const float p0 = (c0 + 2 * i < nvalid) ? exp2f(fmaf(v[2 * i], sl, -mb)) : 0.f;
+            const float p1 = (c0 + 2 * i + 1 < nvalid) ? exp2f(fmaf(v[2 * i + 1], sl, -mb)) : 0.f;
+            l += p0 + p1;
+            w[i] = pack2<T>(p0, p1);
+          }
+          tc::tmem_st8(base + a.p_col + c0 / 2, w);
         }
       }
+      tc::fence_before_sync();
+      tc::mbar_arrive(&p_full[ab]);
+      const bool got2 = tc::mbar_wait(&o_full[ab], rnd & 1);
+      if (!got2) s_fail = 1;
+      tc::fence_after_sync();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int64_t pi = int64_t(req) * a.G + g;
+      for (int c0 = 0; c0 < a.Dv; c0 += 32) {
+        if (a.Dv - c0 >= 32) {
+          float v[32];
+          tc::tmem_ld32(base + a.o_col + c0, v);
+          if (req >= 0) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) w[i] = pack2<T>(v[2 * i] * inv, v[2 * i + 1] * inv);
+            uint4* dst = reinterpret_cast<uint4*>(part_o + pi * a.Dv + c0);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          }
+        } else {
+          float v[16];
+          tc::tmem_ld16(base + a.o_col + c0, v);
+          if (req >= 0) {
+            uint32_t w[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w[i] = pack2<T>(v[2 * i] * inv, v[2 * i + 1] * inv);
+            uint4* dst = reinterpret_cast<uint4*>(part_o + pi * a.Dv + c0);
+            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          }
+        }
+      }
+      if (req >= 0) reinterpret_cast<float2*>(a.part_ml)[pi] = make_float2(mx * a.scale, l);
+      tc::fence_before_sync();
+      tc::mbar_arrive(&acc_empty[ab]);
+      if (!got || !got2) break;
     }
-    if (req >= 0) reinterpret_cast<float2*>(a.part_ml)[pi] = make_float2(mx, l);
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
   }
-  if (!ok && lane == 0) atomicExch(a.status, PISA_ERR_TIMEOUT);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
+  if (tid == 0 && s_fail) atomicExch(a.status, PISA_ERR_TIMEOUT);
   if (warp == 0) tc::tmem_free(tmem, a.tmem_cols);
 }
 
@@ -344,9 +436,7 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnTcArgs a) {
 template <typename T>
 int attn_tc_typed(AttnTcArgs a, cudaStream_t stream) {
   const int qch = a.Dp / 64, vch = a.Dvp / 64;
-  size_t smem = size_t(128) * 128 * qch + size_t(a.C) * 128 * (qch + vch) + 1024;
-  const size_t ctas_fit = 512 / size_t(a.tmem_cols);
-  if (ctas_fit < 16) smem = std::max(smem, size_t(228 * 1024) / ctas_fit - 4096);
+  const size_t smem = size_t(2) * 128 * 128 * qch + size_t(2) * a.C * 128 * (qch + vch) + 1024;
   cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return fail_cuda(e, "attention smem attribute");
   for (int t0 = 0; t0 < a.T; t0 += a.chunk) {
@@ -367,8 +457,7 @@ int attn_tc_typed(AttnTcArgs a, cudaStream_t stream) {
     PISA_CHECK_LAUNCH();
     attn_scatter_kernel<<<grid, 256, 0, stream>>>(a);
     PISA_CHECK_LAUNCH();
-    const int64_t ctas = (a.capacity + a.tiles_per_cta - 1) / a.tiles_per_cta;
-    attn_tc_kernel<T><<<unsigned(ctas), kThreads, smem, stream>>>(a);
+    attn_tc_kernel<T><<<unsigned(a.num_sms), kPipeThreads, smem, stream>>>(a);
     PISA_CHECK_LAUNCH();
     const unsigned cgrid = unsigned((int64_t(a.B) * a.tlen * a.Hq + 3) / 4);
     if (a.Dv <= 32) attn_combine_kernel<T, 1><<<cgrid, 128, 0, stream>>>(a);

@@ -36,6 +36,14 @@ static bool rows_aligned(const void* p, int dtype, int64_t sb, int64_t st, int64
 
 static int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
+// Multiprocessor count of the current device (persistent grids).
+static int num_sms() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
 struct Geometry {
   int64_t sizes[kMaxLevels];
   int64_t offsets[kMaxLevels];
@@ -141,7 +149,8 @@ static bool grouped_tc_eligible(int64_t Hq, int64_t H, int64_t D, int dtype, int
   const int64_t G = Hq / H;
   return schedule == PISA_SCHEDULE_GROUPED && (dtype == PISA_BF16 || dtype == PISA_F16) &&
          (method == PISA_METHOD_PISA || method == PISA_METHOD_PISA2) && is_pow2(G) && G <= 32 &&
-         D % 8 == 0 && D <= 256 && br * C <= 512;
+         D % 8 == 0 && D <= 256 && br * C <= 512 &&
+         (D <= 64 ? 1 : D <= 128 ? 2 : 4) * 128 * (2 * 128 + br * C) + 1024 + 4096 <= 227 * 1024;
 }
 
 static SelectPlan plan_select(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t N,
@@ -284,7 +293,7 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
   g.keys = keys; g.k_sb = key_sb; g.k_st = key_st; g.k_sh = key_sh;
   g.positions = positions; g.pos_offset = position_offset;
   g.B = int(B); g.T = int(Tq); g.H = int(H); g.G = int(Hq / H); g.D = int(D);
-  g.Dp = int((D + 63) / 64 * 64); g.N = int(N); g.C = int(block_size); g.K = int(topk);
+  g.Dp = int(D <= 64 ? 64 : D <= 128 ? 128 : 256); g.N = int(N); g.C = int(block_size); g.K = int(topk);
   g.br = int(branching); g.W0 = int(plan.W0); g.NF = int(plan.NF); g.NP = int(plan.NP);
   g.nwin = int(plan.nwin); g.TW = int(plan.TW); g.RT = int(plan.RT);
   g.method = method; g.bf16 = dtype == PISA_BF16 ? 1 : 0;
@@ -304,8 +313,11 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
   g.tile_req = g.tile_req_w;
   g.tile_capacity = plan.capacity;
   g.tiles_per_cta = 8;
+  // two accumulators (double buffering) whenever they fit in the 512 TMEM columns
   const int64_t nk = branching * block_size;
-  g.tmem_cols = nk <= 32 ? 32 : nk <= 64 ? 64 : nk <= 128 ? 128 : nk <= 256 ? 256 : 512;
+  const int64_t want = nk <= 256 ? 2 * nk : nk;
+  g.tmem_cols = want <= 32 ? 32 : want <= 64 ? 64 : want <= 128 ? 128 : want <= 256 ? 256 : 512;
+  g.num_sms = num_sms();
   g.out_ids = out_ids;
   return grouped_leaf(g, dtype, s);
 }
@@ -319,7 +331,7 @@ namespace pisa {
 struct AttnPlan {
   bool tc = false;
   int64_t TW = 4096, chunk = 0, NB = 0, RT = 0, num_buckets = 0, capacity = 0;
-  int64_t p_col = 0, o_col = 0, tmem_cols = 0;
+  int64_t p_col = 0, o_col = 0, tmem_cols = 0, acc_cols = 0, nacc = 1;
   int64_t counts_off = 0, cursors_off = 0, offsets_off = 0, misc_off = 0, owner_off = 0,
           req_off = 0, po_off = 0, pml_off = 0, total = 0;
 };
@@ -328,13 +340,18 @@ static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t 
                           int64_t N, int64_t S, int64_t C, int dtype) {
   AttnPlan p;
   const int64_t G = Hq / H;
+  // one TMEM buffer = S (C columns) | P (C/2 packed) | O (Dv); two when they fit
   p.p_col = C;
   p.o_col = (C + C / 2 + 31) / 32 * 32;
   const int64_t cols = p.o_col + Dv;
-  p.tmem_cols = cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
+  p.acc_cols = cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
+  p.nacc = 2 * p.acc_cols <= 512 ? 2 : 1;
+  p.tmem_cols = p.nacc * p.acc_cols;
+  const int64_t Dp = D <= 64 ? 64 : D <= 128 ? 128 : 256, Dvp = Dv <= 64 ? 64 : Dv <= 128 ? 128 : 256;
+  const int64_t smem = 2 * 128 * 2 * Dp + 2 * C * 2 * (Dp + Dvp) + 1024 + 4096;
   p.tc = (dtype == PISA_BF16 || dtype == PISA_F16) && is_pow2(G) && G <= 32 && D % 16 == 0 &&
          Dv % 16 == 0 && D <= 256 && Dv <= 256 && is_pow2(C) && C >= 16 && C <= 256 &&
-         cols <= 512 && S > 0 && B * Tq * H * S >= 4096;
+         cols <= 512 && smem <= 227 * 1024 && S > 0 && B * Tq * H * S >= 4096;
   if (!p.tc) return p;
   const int64_t per_token = H * S * G * (Dv * elem_size(dtype) + 8);
   const int64_t fit = ((int64_t(1) << 31) / per_token) / p.TW * p.TW;
@@ -399,7 +416,8 @@ int pisa_sparse_attn_fwd(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh
     a.indices = indices; a.index_bytes = index_bytes;
     a.positions = positions; a.pos_offset = position_offset;
     a.B = int(B); a.T = int(Tq); a.Hq = int(Hq); a.H = int(H); a.G = int(Hq / H);
-    a.D = int(D); a.Dp = int((D + 63) / 64 * 64); a.Dv = int(Dv); a.Dvp = int((Dv + 63) / 64 * 64);
+    a.D = int(D); a.Dp = int(D <= 64 ? 64 : D <= 128 ? 128 : 256);
+    a.Dv = int(Dv); a.Dvp = int(Dv <= 64 ? 64 : Dv <= 128 ? 128 : 256);
     a.N = int(N); a.S = int(S); a.C = int(block_size); a.NB = int(plan.NB); a.TW = int(plan.TW);
     a.RT = int(plan.RT); a.chunk = int(plan.chunk);
     a.scale = scale; a.causal = causal ? 1 : 0; a.bf16 = dtype == PISA_BF16 ? 1 : 0;
@@ -414,6 +432,7 @@ int pisa_sparse_attn_fwd(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh
     a.part_ml = reinterpret_cast<float*>(ws + plan.pml_off);
     a.tiles_per_cta = 8;
     a.tmem_cols = int(plan.tmem_cols); a.p_col = int(plan.p_col); a.o_col = int(plan.o_col);
+    a.acc_cols = int(plan.acc_cols); a.nacc = int(plan.nacc); a.num_sms = num_sms();
     a.out = out; a.lse = lse;
     return attn_fwd_tc(a, dtype, static_cast<cudaStream_t>(stream));
   }

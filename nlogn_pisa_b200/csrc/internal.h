@@ -80,6 +80,7 @@ struct GroupArgs {
   int64_t tile_capacity;
   int tiles_per_cta;
   int tmem_cols;
+  int num_sms;
   int64_t* out_ids;
   int* status;
 };
@@ -137,7 +138,7 @@ struct AttnTcArgs {
   int32_t* tile_req;
   int32_t* total_tiles;
   int64_t capacity;
-  int tiles_per_cta, tmem_cols, p_col, o_col;
+  int tiles_per_cta, tmem_cols, p_col, o_col, acc_cols, nacc, num_sms;
   void* part_o;
   float* part_ml;
   void* out;

@@ -77,143 +77,198 @@ __global__ void family_scatter_kernel(const GroupArgs g, const int32_t* __restri
   if (pos % g.RT == 0) tile_owner[tile] = int32_t(bucket);
 }
 
-// One CTA walks `tiles_per_cta` consecutive tiles, restaging the family keys
-// only when the bucket changes.  Four warps: all load, thread 0 issues the
-// MMAs, all four read back one TMEM lane (= one query-head row) each.
+// Warp roles of the pipelined tile kernel (one persistent CTA per SM):
+//   warps 0-7   epilogue: warp w reads TMEM lanes 32*(w%4).. (one query-head
+//               row per thread) and handles half of the b children
+//   warps 8-11  producers: gather the tile's query rows into a 2-stage ring,
+//               restage the family keys when the bucket changes
+//   warp 12     MMA issue (one thread): tile i accumulates into TMEM buffer i%2
+// mbarriers: full_q/empty_q guard the query stages, full_acc/empty_acc the
+// accumulators; the parity of round r is r & 1 (empty waits start at 1, so the
+// first round passes).  Every wait is bounded and records a timeout status.
+constexpr int kEpiWarps = 8, kLoadWarps = 4, kMmaWarp = 12;
+constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
+
 template <typename T>
-__global__ void __launch_bounds__(kLeafThreads) leaf_tc_kernel(const GroupArgs g) {
+__global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArgs g) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int Dp = g.Dp;                     // head_dim rounded up to 64
-  const int chunks = Dp / 64;              // 128-byte K chunks
-  const int NK = g.br * g.C;               // keys per family = MMA N (total)
-  uint8_t* Qs = smem;                      // [chunks][128 rows][128 B]
-  uint8_t* Ks = smem + chunks * 128 * 128; // [chunks][NK rows][128 B]
-  __shared__ uint64_t mbar;
+  const int Dp = g.Dp;                       // padded head_dim: 64, 128 or 256
+  const int chunks = Dp / 64;                // 128-byte K chunks per row
+  const int vpr = Dp / 8;                    // 16-byte vectors per row (divides 128)
+  const int NK = g.br * g.C;                 // keys per family = MMA N
+  const int q_stage_bytes = chunks * 128 * 128;
+  uint8_t* Ks = smem + 2 * q_stage_bytes;    // [chunks][NK][128 B]
+  __shared__ uint64_t full_q[2], empty_q[2], full_acc[2], empty_acc[2];
   __shared__ uint32_t tmem_slot;
-  __shared__ int32_t s_req[128];
+  __shared__ int64_t s_qoff[2][128];
+  __shared__ int s_fail;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int total = *g.total_tiles;
-  const int first = blockIdx.x * g.tiles_per_cta;
-  if (first >= total) return;
-  const int last = min(first + g.tiles_per_cta, total);
+  const int per = (total + gridDim.x - 1) / gridDim.x;
+  const int first = blockIdx.x * per;
+  const int last = min(first + per, total);
+  if (first >= last) return;
+  const int ntiles = last - first;
 
-  if (tid == 0) tc::mbar_init(&mbar, 1);
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&full_q[i], kLoadWarps * 32);
+      tc::mbar_init(&empty_q[i], 1);
+      tc::mbar_init(&full_acc[i], 1);
+      tc::mbar_init(&empty_acc[i], kEpiWarps * 32);
+    }
+    s_fail = 0;
+    tc::fence_barrier_init();
+  }
   if (warp == 0) tc::tmem_alloc(&tmem_slot, g.tmem_cols);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_slot;
-  const uint32_t lane_base = (uint32_t(warp) * 32) << 16;
-  const uint32_t qs_addr = tc::smem_u32(Qs), ks_addr = tc::smem_u32(Ks);
-  const T* qbase = static_cast<const T*>(g.q);
-  const T* kbase = static_cast<const T*>(g.keys);
-  const int vec_per_row = Dp / 8;          // 16-byte vectors per row (8 elements of 2 bytes)
-  const int dvec = g.D / 8;
-  uint32_t phase = 0;
-  int cur_owner = -1;
-  bool ok = true;
+  const int nacc = g.tmem_cols >= 2 * NK ? 2 : 1;
+  const uint32_t qs_addr = tc::smem_u32(smem), ks_addr = tc::smem_u32(Ks);
+  const int lgG = 31 - __clz(g.G);
 
-  for (int tile = first; tile < last; ++tile) {
-    const int owner = g.tile_owner[tile];
-    const int p = owner % g.NP;
-    const int h = (owner / g.NP) % g.H;
-    const int b = owner / (g.NP * g.H * g.nwin);
-    if (tid < g.RT) s_req[tid] = g.tile_req[int64_t(tile) * g.RT + tid];
-    if (owner != cur_owner) {
-      // stage the family's NK contiguous keys (zero past the sequence end / head_dim)
-      const int64_t tok0 = int64_t(p) * NK;
-      const T* kb = kbase + b * g.k_sb + int64_t(h) * g.k_sh;
-      for (int idx = tid; idx < NK * vec_per_row; idx += kLeafThreads) {
-        const int r = idx / vec_per_row, c = idx % vec_per_row;
-        const uint32_t dst = ks_addr + (c >> 3) * NK * 128 + tc::swizzle128(r, c & 7);
-        const int64_t tok = tok0 + r;
-        if (tok < g.N && c < dvec) cp_async16(dst, kb + tok * g.k_st + c * 8);
+  if (warp >= kEpiWarps && warp < kMmaWarp) {
+    // ---------------- producers ----------------
+    const int ptid = tid - kEpiWarps * 32;
+    const int c = ptid & (vpr - 1);          // this thread's 16-byte column
+    const int row_step = kLoadWarps * 32 / vpr;
+    const T* qbase = static_cast<const T*>(g.q);
+    const T* kbase = static_cast<const T*>(g.keys);
+    int cur_key = -1;
+    for (int it = 0; it < ntiles; ++it) {
+      const int tile = first + it, s = it & 1;
+      if (!tc::mbar_wait(&empty_q[s], ((it >> 1) & 1) ^ 1)) { s_fail = 1; break; }
+      const int owner = g.tile_owner[tile];
+      const int p = owner % g.NP;
+      const int h = (owner / g.NP) % g.H;
+      const int b = owner / (g.NP * g.H * g.nwin);
+      const int kkey = (b * g.H + h) * g.NP + p;
+      if (kkey != cur_key) {
+        // the previous tile's MMA must be done before its keys are replaced
+        if (it > 0 && !tc::mbar_wait(&empty_q[(it - 1) & 1], ((it - 1) >> 1) & 1)) { s_fail = 1; break; }
+        const int64_t tok0 = int64_t(p) * NK;
+        const T* kb = kbase + b * g.k_sb + int64_t(h) * g.k_sh;
+        for (int r = ptid / vpr; r < NK; r += row_step) {
+          const uint32_t dst = ks_addr + (c >> 3) * NK * 128 + tc::swizzle128(r, c & 7);
+          const int64_t tok = tok0 + r;
+          if (tok < g.N && c * 8 < g.D) cp_async16(dst, kb + tok * g.k_st + c * 8);
+          else st_zero16(dst);
+        }
+        cur_key = kkey;
+      }
+      if (ptid < g.RT) {
+        const int req = g.tile_req[int64_t(tile) * g.RT + ptid];
+        int64_t off = -1;
+        if (req >= 0) {
+          const int rowid = req / g.NF;
+          const int hh = rowid % g.H, t = (rowid / g.H) % g.T, bb = rowid / (g.H * g.T);
+          off = bb * g.q_sb + int64_t(t) * g.q_st + int64_t(hh * g.G) * g.q_sh;
+        }
+        s_qoff[s][ptid] = off;
+      }
+      tc::named_sync(1, kLoadWarps * 32);
+      const uint32_t qdst = qs_addr + s * q_stage_bytes + (c >> 3) * 128 * 128;
+      for (int row = ptid / vpr; row < 128; row += row_step) {
+        const int r = row >> lgG, gh = row & (g.G - 1);
+        const int64_t off = r < g.RT ? s_qoff[s][r] : -1;
+        const uint32_t dst = qdst + tc::swizzle128(row, c & 7);
+        if (off >= 0 && c * 8 < g.D) cp_async16(dst, qbase + off + int64_t(gh) * g.q_sh + c * 8);
         else st_zero16(dst);
       }
-      cur_owner = owner;
+      cp_async_wait_all();
+      tc::fence_async_smem();
+      tc::mbar_arrive(&full_q[s]);
     }
-    __syncthreads();  // s_req visible
-    for (int idx = tid; idx < 128 * vec_per_row; idx += kLeafThreads) {
-      const int row = idx / vec_per_row, c = idx % vec_per_row;
-      const int r = row / g.G, gh = row % g.G;
-      const uint32_t dst = qs_addr + (c >> 3) * 128 * 128 + tc::swizzle128(row, c & 7);
-      const int req = r < g.RT ? s_req[r] : -1;
-      if (req >= 0 && c < dvec) {
-        int bb, t, hh;
-        decode_row(req / g.NF, g.T, g.H, bb, t, hh);
-        cp_async16(dst, qbase + bb * g.q_sb + t * g.q_st + int64_t(hh * g.G + gh) * g.q_sh + c * 8);
-      } else {
-        st_zero16(dst);
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issue ----------------
+    if (lane == 0) {
+      for (int it = 0; it < ntiles; ++it) {
+        const int s = it & 1, a = nacc == 2 ? (it & 1) : 0;
+        const int ra = nacc == 2 ? (it >> 1) : it;
+        if (!tc::mbar_wait(&full_q[s], (it >> 1) & 1)) { s_fail = 1; break; }
+        if (!tc::mbar_wait(&empty_acc[a], (ra & 1) ^ 1)) { s_fail = 1; break; }
+        tc::fence_after_sync();
+        const uint32_t acc = tmem + a * NK;
+        const uint32_t qa = qs_addr + s * q_stage_bytes;
+        for (int n0 = 0; n0 < NK; n0 += 256) {
+          const int n = min(256, NK - n0);
+          const uint32_t idesc = tc::idesc_f16(128, n, g.bf16);
+          for (int ks = 0; ks < Dp / 16; ++ks) {
+            const int ch = ks >> 2, off = (ks & 3) * 32;
+            tc::mma_f16(acc + n0, tc::desc_sw128(qa + ch * 128 * 128 + off),
+                        tc::desc_sw128(ks_addr + ch * NK * 128 + n0 * 128 + off), idesc, ks > 0);
+          }
+        }
+        tc::mma_commit(&full_acc[a]);
+        tc::mma_commit(&empty_q[s]);
       }
     }
-    cp_async_wait_all();
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    if (tid == 0) {
-      for (int n0 = 0; n0 < NK; n0 += 256) {
-        const int n = min(256, NK - n0);
-        const uint32_t idesc = tc::idesc_f16(128, n, g.bf16);
-        for (int ks = 0; ks < Dp / 16; ++ks) {
-          const int ch = ks >> 2, off = (ks & 3) * 32;
-          const uint64_t ad = tc::desc_sw128(qs_addr + ch * 128 * 128 + off);
-          const uint64_t bd = tc::desc_sw128(ks_addr + ch * NK * 128 + n0 * 128 + off);
-          tc::mma_f16(tmem + n0, ad, bd, idesc, ks > 0);
+    __syncwarp();
+  } else {
+    // ---------------- epilogue ----------------
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = (uint32_t(quarter) * 32) << 16;
+    const int r = row >> lgG;
+    const int jn = g.br / 2;                 // children handled by this thread
+    const float l2e = 1.4426950408889634f;
+    const float sl = g.scale * l2e;          // exp(scale*x - m) = 2^(x*sl - m*l2e)
+    for (int it = 0; it < ntiles; ++it) {
+      const int tile = first + it;
+      const int a = nacc == 2 ? (it & 1) : 0;
+      const int ra = nacc == 2 ? (it >> 1) : it;
+      const bool got = tc::mbar_wait(&full_acc[a], ra & 1);
+      if (!got) s_fail = 1;
+      tc::fence_after_sync();
+      const int owner = g.tile_owner[tile];
+      const int p = owner % g.NP;
+      const int req = r < g.RT ? g.tile_req[int64_t(tile) * g.RT + r] : -1;
+      const uint32_t acc = tmem + lane_base + a * NK;
+      for (int jj = 0; jj < jn; ++jj) {
+        const int j = half * jn + jj;
+        const int64_t key0 = (int64_t(p) * g.br + j) * g.C;
+        const int valid_keys = int(min64(g.C, max(int64_t(0), g.N - key0)));
+        float score;
+        if (g.method == PISA_METHOD_PISA) {
+          float mx = -INFINITY;
+          for_columns(acc + j * g.C, g.C, [&](int cc, float x) {
+            if (cc < valid_keys) mx = fmaxf(mx, x);
+          });
+          const float mb = mx * sl;
+          float sum = 0.f;
+          for_columns(acc + j * g.C, g.C, [&](int cc, float x) {
+            if (cc < valid_keys) sum += exp2f(fmaf(x, sl, -mb));
+          });
+          score = mx * g.scale + logf(sum);
+        } else {
+          float s1 = 0.f, s2 = 0.f;
+          for_columns(acc + j * g.C, g.C, [&](int cc, float x) {
+            if (cc < valid_keys) { s1 += x; s2 = fmaf(x, x, s2); }
+          });
+          const float n = float(valid_keys > 0 ? valid_keys : 1);
+          const float mean = s1 / n, var = fmaxf(s2 / n - mean * mean, 0.f);
+          score = g.scale * mean + g.c2 * var;
+        }
+        if (valid_keys == 0) score = 0.f;
+        for (int o = 1; o < g.G; o <<= 1) score += __shfl_xor_sync(kFull, score, o);
+        if (req >= 0 && (row & (g.G - 1)) == 0) {
+          const int rowid = req / g.NF, k = req - (req / g.NF) * g.NF;
+          g.scores[int64_t(rowid) * g.W0 + k * g.br + j] = score;
         }
       }
-      tc::mma_commit(&mbar);
+      tc::fence_before_sync();
+      tc::mbar_arrive(&empty_acc[a]);
+      if (!got) break;
     }
-    if (!tc::mbar_wait(&mbar, phase)) ok = false;
-    phase ^= 1;
-    tc::fence_after_sync();
-
-    // epilogue: thread <-> TMEM lane <-> query-head row
-    const int row = tid;
-    const int r = row / g.G;
-    const int req = (r < g.RT) ? s_req[r] : -1;
-    for (int j = 0; j < g.br; ++j) {
-      const int64_t key0 = (int64_t(p) * g.br + j) * g.C;
-      const int col0 = j * g.C;
-      const int valid_keys = int(min64(g.C, max(int64_t(0), g.N - key0)));
-      float score;
-      if (g.method == PISA_METHOD_PISA) {
-        float mx = -INFINITY;
-        for_columns(tmem + lane_base + col0, g.C, [&](int c, float x) {
-          if (c < valid_keys) mx = fmaxf(mx, x * g.scale);
-        });
-        float sum = 0.f;
-        for_columns(tmem + lane_base + col0, g.C, [&](int c, float x) {
-          if (c < valid_keys) sum += expf(x * g.scale - mx);
-        });
-        score = mx + logf(sum);
-      } else {
-        float s1 = 0.f, s2 = 0.f;
-        for_columns(tmem + lane_base + col0, g.C, [&](int c, float x) {
-          if (c < valid_keys) { s1 += x; s2 += x * x; }
-        });
-        const float n = float(valid_keys > 0 ? valid_keys : 1);
-        const float mean = s1 / n, var = fmaxf(s2 / n - mean * mean, 0.f);
-        score = g.scale * mean + g.c2 * var;
-      }
-      if (key0 >= g.N) score = 0.f;  // child past the end: never scoreable
-      for (int o = 1; o < g.G; o <<= 1) score += __shfl_xor_sync(kFull, score, o);
-      if (req >= 0 && (row % g.G) == 0) {
-        const int64_t rowid = req / g.NF;
-        const int k = req % g.NF;
-        g.scores[rowid * g.W0 + k * g.br + j] = score;
-      }
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
   }
-  if (!ok && lane == 0) atomicExch(g.status, PISA_ERR_TIMEOUT);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
+  if (tid == 0 && s_fail) atomicExch(g.status, PISA_ERR_TIMEOUT);
   if (warp == 0) tc::tmem_free(tmem, g.tmem_cols);
 }
 
@@ -278,16 +333,11 @@ int grouped_leaf(const GroupArgs& g, int dtype, cudaStream_t stream) {
   PISA_CHECK_LAUNCH();
 
   const int chunks = g.Dp / 64;
-  size_t smem = size_t(chunks) * 128 * (128 + g.br * g.C) + 1024;
-  // Keep (resident CTAs per SM) x (TMEM columns per CTA) <= 512 so that no
-  // CTA waits in tcgen05.alloc: shared memory bounds the residency.
-  const size_t per_sm = 228 * 1024, ctas_fit = 512 / size_t(g.tmem_cols);
-  if (ctas_fit < 16) smem = std::max(smem, per_sm / ctas_fit - 4096);
+  const size_t smem = size_t(chunks) * 128 * (2 * 128 + g.br * g.C) + 1024;
   auto kernel = dtype == PISA_BF16 ? leaf_tc_kernel<__nv_bfloat16> : leaf_tc_kernel<__half>;
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return fail_cuda(e, "leaf smem attribute");
-  const int64_t ctas = (g.tile_capacity + g.tiles_per_cta - 1) / g.tiles_per_cta;
-  kernel<<<unsigned(ctas), kLeafThreads, smem, stream>>>(g);
+  kernel<<<unsigned(g.num_sms), kPipeThreads, smem, stream>>>(g);
   PISA_CHECK_LAUNCH();
 
   const unsigned fgrid = unsigned((rows + 3) / 4);
