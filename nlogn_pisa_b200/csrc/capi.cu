@@ -139,6 +139,9 @@ namespace pisa {
 struct SelectPlan {
   bool grouped_tc = false;
   Geometry geo{};
+  // dense tensor-core scoring of whole coarse levels (dense.cu), by token chunk
+  int dense_off[kMaxLevels];
+  int64_t dense_row = 0, dense_chunk = 0, dense_off_ws = 0, status_off = 0;
   int64_t W0 = 0, NF = 0, NP = 0, nwin = 0, TW = 4096, RT = 0, rows = 0, num_buckets = 0, capacity = 0;
   int64_t pyramid_off = 0, cand_off = 0, flags_off = 0, scores_off = 0, counts_off = 0,
           cursors_off = 0, offsets_off = 0, misc_off = 0, owner_off = 0, req_off = 0, total = 0;
@@ -159,9 +162,40 @@ static SelectPlan plan_select(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int6
   SelectPlan p;
   p.geo = level_geometry(N, C, br, top + 1);
   int64_t off = 0;
+  p.status_off = off;  // device status word (timeouts of bounded waits)
+  off += 256;
   if (build_summary) {
     p.pyramid_off = off;
     off += align_up(B * p.geo.total * H * D * elem_size(dtype), 256);
+  }
+  // Coarse levels scored densely: only for prefill-sized batches of queries,
+  // levels that can hold more than K candidates (else the all-fit shortcut
+  // scores nothing; pisa1 has no shortcut), children counts up to 8192.
+  const int64_t G = Hq / H;
+  const bool dense_ok = (dtype == PISA_BF16 || dtype == PISA_F16) && is_pow2(G) && G <= 32 &&
+                        D % 8 == 0 && D <= 256 && Tq * G >= 1024;
+  for (int l = 0; l < kMaxLevels; ++l) p.dense_off[l] = -1;
+  if (dense_ok) {
+    for (int64_t l = top; l >= 0; --l) {
+      const int64_t n = p.geo.sizes[l];
+      int64_t children;
+      if (method == PISA_METHOD_PISA1) {
+        children = n;
+      } else {
+        if (l == 0 || n <= K) continue;
+        children = p.geo.sizes[l - 1];
+      }
+      if (children > 8192) continue;
+      p.dense_off[l] = int(p.dense_row);
+      p.dense_row += n;
+    }
+  }
+  if (p.dense_row > 0) {
+    const int64_t budget = int64_t(1) << 30;  // bytes of scores per token chunk
+    const int64_t per_token = B * H * p.dense_row * 4;
+    p.dense_chunk = std::min<int64_t>(Tq, std::max<int64_t>(128, budget / per_token / 128 * 128));
+    p.dense_off_ws = off;
+    off += align_up(B * p.dense_chunk * H * p.dense_row * 4, 256);
   }
   p.grouped_tc = grouped_tc_eligible(Hq, H, D, dtype, method, C, br, schedule);
   if (p.grouped_tc) {
@@ -243,6 +277,10 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
   if (plan.total > 0 && (!workspace || workspace_bytes < plan.total))
     return fail(PISA_ERR_INVALID, "workspace too small");
   char* ws = static_cast<char*>(workspace);
+  {
+    cudaError_t e = cudaMemsetAsync(ws + plan.status_off, 0, 256, s);
+    if (e != cudaSuccess) return fail_cuda(e, "status clear");
+  }
 
   RouteArgs a{};
   if (summary == nullptr) {
@@ -277,17 +315,53 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
   a.scale = float(scale);
   a.c2 = float(0.5 * scale * scale);
   a.out_ids = out_ids;
-  if (!plan.grouped_tc) {
-    a.coarse_only = 0;
-    return route(a, dtype, s);
+  a.coarse_only = plan.grouped_tc ? 1 : 0;
+  if (plan.grouped_tc) {
+    // grouped: coarse levels -> leaf candidates + masks, then tensor-core leaf scoring
+    a.W0 = int(plan.W0);
+    a.candidates = reinterpret_cast<int32_t*>(ws + plan.cand_off);
+    a.flags = reinterpret_cast<uint8_t*>(ws + plan.flags_off);
   }
-  // grouped: coarse levels -> leaf candidates + masks, then tensor-core leaf scoring
-  a.coarse_only = 1;
-  a.W0 = int(plan.W0);
-  a.candidates = reinterpret_cast<int32_t*>(ws + plan.cand_off);
-  a.flags = reinterpret_cast<uint8_t*>(ws + plan.flags_off);
-  int rc = route(a, dtype, s);
-  if (rc) return rc;
+  for (int l = 0; l < kMaxLevels; ++l) a.dense_off[l] = plan.dense_off[l];
+  int rc = PISA_OK;
+  if (plan.dense_row == 0) {
+    a.t_begin = 0; a.t_count = int(Tq);
+    rc = route(a, dtype, s);
+  } else {
+    float* dense = reinterpret_cast<float*>(ws + plan.dense_off_ws);
+    a.dense = dense;
+    a.dense_stride = plan.dense_row;
+    DenseArgs d{};
+    d.q = q; d.q_sb = q_sb; d.q_st = q_st; d.q_sh = q_sh;
+    d.summary = a.summary; d.s_sb = a.s_sb;
+    d.positions = positions; d.pos_offset = position_offset;
+    d.B = int(B); d.T = int(Tq); d.H = int(H); d.G = int(Hq / H); d.D = int(D);
+    d.Dp = int(D <= 64 ? 64 : D <= 128 ? 128 : 256); d.method = method;
+    d.bf16 = dtype == PISA_BF16 ? 1 : 0; d.scale = a.scale; d.c2 = a.c2;
+    d.scores = dense; d.row_stride = plan.dense_row;
+    d.status = reinterpret_cast<int*>(ws + plan.status_off);
+    for (int64_t t0 = 0; t0 < Tq && rc == PISA_OK; t0 += plan.dense_chunk) {
+      const int tc = int(std::min<int64_t>(plan.dense_chunk, Tq - t0));
+      d.t_begin = int(t0); d.t_count = tc;
+      for (int l = 0; l <= top && rc == PISA_OK; ++l) {
+        if (plan.dense_off[l] < 0) continue;
+        const bool self = method == PISA_METHOD_PISA1;
+        const int child = self ? l : l - 1;
+        d.child_off = a.levels.offset[child];
+        d.n_child = a.levels.size[child];
+        d.support = self ? 1 : int(branching);
+        int64_t span = block_size;
+        for (int i = 0; i < l; ++i) span *= branching;
+        d.span = span;
+        d.out_off = plan.dense_off[l];
+        rc = dense_level(d, dtype, s);
+      }
+      if (rc) break;
+      a.t_begin = int(t0); a.t_count = tc;
+      rc = route(a, dtype, s);
+    }
+  }
+  if (rc || !plan.grouped_tc) return rc;
   GroupArgs g{};
   g.q = q; g.q_sb = q_sb; g.q_st = q_st; g.q_sh = q_sh;
   g.keys = keys; g.k_sb = key_sb; g.k_st = key_st; g.k_sh = key_sh;
@@ -306,7 +380,7 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
   g.num_buckets = plan.num_buckets;
   g.total_tiles_w = reinterpret_cast<int32_t*>(ws + plan.misc_off);
   g.total_tiles = g.total_tiles_w;
-  g.status = reinterpret_cast<int*>(ws + plan.misc_off + 4);
+  g.status = reinterpret_cast<int*>(ws + plan.status_off);
   g.tile_owner_w = reinterpret_cast<int32_t*>(ws + plan.owner_off);
   g.tile_owner = g.tile_owner_w;
   g.tile_req_w = reinterpret_cast<int32_t*>(ws + plan.req_off);

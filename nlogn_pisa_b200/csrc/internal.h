@@ -47,6 +47,10 @@ struct RouteArgs {
   uint8_t* flags;       // [B,T,H,W0] leaf masks: bit0 valid, bit1 forced, bit2 scoreable
   int W0;
   int coarse_only;
+  int t_begin, t_count;  // token range routed by this launch
+  const float* dense;   // precomputed level scores, rows local to the range
+  int64_t dense_stride;
+  int dense_off[kMaxLevels];  // per level offset in a dense row, -1 = compute here
 };
 
 int route(const RouteArgs& a, int dtype, cudaStream_t stream);
@@ -86,6 +90,28 @@ struct GroupArgs {
 };
 
 int grouped_leaf(const GroupArgs& g, int dtype, cudaStream_t stream);
+
+// Dense scoring of every node of one coarse level (see dense.cu).
+struct DenseArgs {
+  const void* q;
+  int64_t q_sb, q_st, q_sh;
+  const void* summary;       // pyramid storage [B, total, H, D]
+  int64_t s_sb;
+  int64_t child_off;         // node offset of the child level in the storage
+  int n_child;               // children at the child level
+  int support;               // children per node (b), or 1 for pisa1 (node itself)
+  int64_t span;              // tokens covered by one node of the scored level
+  const int64_t* positions;
+  int64_t pos_offset;
+  int B, T, H, G, D, Dp, method, bf16;
+  int t_begin, t_count;      // token range scored by this launch
+  float scale, c2;
+  float* scores;             // [B, t_count, H, row_stride] (rows local to the range)
+  int64_t row_stride, out_off;
+  int* status;
+};
+
+int dense_level(const DenseArgs& a, int dtype, cudaStream_t stream);
 
 struct AttnArgs {
   const void* q;

@@ -211,10 +211,13 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const RouteArgs a) {
   unsigned char* fl = reinterpret_cast<unsigned char*>(sc + kMaxWidth);
   __shared__ int s_valid;
 
-  const int item = blockIdx.x;
-  const int h = item % a.H;
-  const int t = (item / a.H) % a.T;
-  const int b = item / (a.H * a.T);
+  const int local = blockIdx.x;                 // (b, token in range, h)
+  const int h = local % a.H;
+  const int tl = (local / a.H) % a.t_count;
+  const int b = local / (a.H * a.t_count);
+  const int t = a.t_begin + tl;
+  const int64_t item = (int64_t(b) * a.T + t) * a.H + h;
+  const float* dense_row = a.dense ? a.dense + int64_t(local) * a.dense_stride : nullptr;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t pos = a.positions ? a.positions[int64_t(b) * a.T + t] : a.pos_offset + t;
 
@@ -277,13 +280,15 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const RouteArgs a) {
     }
 
     // fill values and thread-per-candidate scoring
-    const bool warp_leaf = level == 0 && a.method != PISA_METHOD_PISA1;
+    const bool warp_leaf = level == 0 && a.method != PISA_METHOD_PISA1 && a.dense_off[0] < 0;
     for (int w = tid; w < width; w += kThreads) {
       const int f = fl[w];
       const bool valid = f & 1, forced = f & 2;
       const bool scoreable = valid && !forced && !identity;
       float v = 0.f;
-      if (scoreable && !warp_leaf) {
+      if (scoreable && !warp_leaf && dense_row && a.dense_off[level] >= 0) {
+        v = dense_row[a.dense_off[level] + ids[w]];
+      } else if (scoreable && !warp_leaf) {
         if (a.method == PISA_METHOD_PISA1) {
           v = coarse_score<T, GMAX>(a, summary + a.levels.offset[level] * node_stride, len, ids[w], qs);
         } else {
@@ -330,7 +335,7 @@ int launch_route(const RouteArgs& a, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return fail_cuda(e, "route smem attribute");
   }
-  const int64_t items = int64_t(a.B) * a.T * a.H;
+  const int64_t items = int64_t(a.B) * a.t_count * a.H;
   if (items == 0) return PISA_OK;
   kernel<<<unsigned(items), kThreads, smem, stream>>>(a);
   PISA_CHECK_LAUNCH();

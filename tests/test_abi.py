@@ -36,7 +36,7 @@ def test_workspace_sizes_are_pure_host_functions():
     lib = _lib.lib()
     n = lib.pisa_select_workspace_bytes(1, 32768, 32, 8, 128, 32768, 1, 2, 64, 2, 32, 4, 32, 0, 1)
     assert n >= 1 * (512 + 256 + 128 + 64 + 32) * 8 * 128 * 2 + 32768 * 8 * 64 * 9
-    assert lib.pisa_select_workspace_bytes(1, 1, 32, 8, 128, 4096, 1, 2, 64, 2, 32, 1, 32, 1, 0) == 0
+    assert lib.pisa_select_workspace_bytes(1, 1, 32, 8, 128, 4096, 1, 2, 64, 2, 32, 1, 32, 1, 0) == 256
     assert lib.pisa_sparse_attn_bwd_workspace_bytes(1, 4, 4, 2, 64, 64, 100) >= 2 * 100 * 2 * 64 * 4
 
 
