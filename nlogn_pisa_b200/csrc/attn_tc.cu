@@ -310,11 +310,38 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
       }
       const uint32_t base = tmem + lane_base + ab * a.acc_cols;
       float mx = -INFINITY;
+      float l = 0.f;
+      if (a.C == 64) {
+        // one TMEM load; masked keys -> -inf -> exp 0; packed arithmetic
+        float v[64];
+        tc::tmem_ld64(base, v);
+        if (nvalid < 64) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) if (i >= nvalid) v[i] = -INFINITY;
+        }
+        mx = tc::max64(v);
+        const float mb = nvalid > 0 ? mx * sl : 0.f;
+        const float2 kk = make_float2(sl, sl), cc = make_float2(-mb, -mb);
+        float2 acc2 = make_float2(0.f, 0.f);
+        uint32_t w[32];
+#pragma unroll
+        for (int i = 0; i < 64; i += 2) {
+          const float2 x = tc::fma2(make_float2(v[i], v[i + 1]), kk, cc);
+          const float2 pr = make_float2(tc::ex2f(x.x), tc::ex2f(x.y));
+          acc2 = tc::add2(acc2, pr);
+          w[i / 2] = pack2<T>(pr.x, pr.y);
+        }
+        l = acc2.x + acc2.y;
+        uint32_t w0[16], w1[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) { w0[i] = w[i]; w1[i] = w[16 + i]; }
+        tc::tmem_st16(base + a.p_col, w0);
+        tc::tmem_st16(base + a.p_col + 16, w1);
+      } else {
       for_columns(base, a.C, [&](int c, float x) {
         if (c < nvalid) mx = fmaxf(mx, x);
       });
       const float mb = mx * sl;
-      float l = 0.f;
       for (int c0 = 0; c0 < a.C; c0 += 32) {
         if (a.C - c0 >= 32) {
           float v[32];
@@ -342,6 +369,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
           tc::tmem_st8(base + a.p_col + c0 / 2, w);
         }
       }
+      }
       tc::fence_before_sync();
       tc::mbar_arrive(&p_full[ab]);
       const bool got2 = tc::mbar_wait(&o_full[ab], rnd & 1);
@@ -349,7 +377,22 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
       tc::fence_after_sync();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int64_t pi = int64_t(req) * a.G + g;
-      for (int c0 = 0; c0 < a.Dv; c0 += 32) {
+      int c0 = 0;
+      for (; c0 + 64 <= a.Dv; c0 += 64) {
+        float v[64];
+        tc::tmem_ld64(base + a.o_col + c0, v);
+        if (req >= 0) {
+          uint4* dst = reinterpret_cast<uint4*>(part_o + pi * a.Dv + c0);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            dst[i] = make_uint4(pack2<T>(v[8 * i] * inv, v[8 * i + 1] * inv),
+                                pack2<T>(v[8 * i + 2] * inv, v[8 * i + 3] * inv),
+                                pack2<T>(v[8 * i + 4] * inv, v[8 * i + 5] * inv),
+                                pack2<T>(v[8 * i + 6] * inv, v[8 * i + 7] * inv));
+          }
+        }
+      }
+      for (; c0 < a.Dv; c0 += 32) {
         if (a.Dv - c0 >= 32) {
           float v[32];
           tc::tmem_ld32(base + a.o_col + c0, v);
@@ -387,7 +430,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
   if (warp == 0) tc::tmem_free(tmem, a.tmem_cols);
 }
 
-// Merge the S block partials of one query head (one warp per head row).
+// Merge the S block partials of one query head (one warp per head row):
+// lane s reads slot s's (m, l), the warp forms the softmax weights of the
+// blocks, then every lane accumulates its value columns over the slots with
+// the loads of four slots in flight.
 template <typename T, int DPL>
 __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnTcArgs a) {
   const int64_t idx = blockIdx.x * 4 + (threadIdx.x >> 5);
@@ -398,38 +444,55 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnTcArgs a) {
   const int b = int(idx / (int64_t(a.Hq) * a.tlen));
   const int h = hq / a.G, g = hq % a.G;
   const int t = a.t0 + tl;
-  const int64_t row_local = (int64_t(b) * a.tlen + tl) * a.H + h;
+  const int64_t slot0 = ((int64_t(b) * a.tlen + tl) * a.H + h) * a.S;   // chunk-local request of slot 0
   const T* part_o = static_cast<const T*>(a.part_o);
-  float M = -INFINITY, L = 0.f, acc[DPL];
+  const float2* part_ml = reinterpret_cast<const float2*>(a.part_ml);
+  // per-lane slots: s = lane, lane + 32
+  float m_s[2] = {-INFINITY, -INFINITY}, l_s[2] = {0.f, 0.f};
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int s = lane + 32 * k;
+    if (s < a.S && visible_block(a, b, t, h, s) >= 0) {
+      const float2 ml = part_ml[(slot0 + s) * a.G + g];
+      if (ml.y > 0.f) { m_s[k] = ml.x; l_s[k] = ml.y; }
+    }
+  }
+  const float M = warp_max(fmaxf(m_s[0], m_s[1]));
+  float w_s[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) w_s[k] = (M == -INFINITY || m_s[k] == -INFINITY) ? 0.f : l_s[k] * expf(m_s[k] - M);
+  const float L = warp_sum(w_s[0] + w_s[1]);
+  float acc[DPL];
 #pragma unroll
   for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-  for (int s = 0; s < a.S; ++s) {
-    if (visible_block(a, b, t, h, s) < 0) continue;
-    const int64_t pi = (row_local * a.S + s) * a.G + g;
-    const float2 ml = reinterpret_cast<const float2*>(a.part_ml)[pi];
-    if (ml.y <= 0.f) continue;
-    if (ml.x > M) {
-      const float f = M == -INFINITY ? 0.f : expf(M - ml.x);
-      L *= f;
+  const int dbase = lane * DPL;
+  for (int s0 = 0; s0 < a.S; s0 += 4) {
+    float w[4];
+    float x[4][DPL];
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) acc[i] *= f;
-      M = ml.x;
-    }
-    const float w = expf(ml.x - M) * ml.y;
-    L += w;
+    for (int u = 0; u < 4; ++u) {
+      const int s = s0 + u;
+      const float ws = __shfl_sync(kFull, s < 32 ? w_s[0] : w_s[1], s & 31);
+      w[u] = s < a.S ? ws : 0.f;
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) {
-      const int d = lane * DPL + i;
-      if (d < a.Dv) acc[i] = fmaf(w, to_f32<T>(part_o[pi * a.Dv + d]), acc[i]);
+      for (int i = 0; i < DPL; ++i) x[u][i] = 0.f;
+      if (w[u] > 0.f) {
+        const T* src = part_o + ((slot0 + s) * a.G + g) * a.Dv + dbase;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i)
+          if (dbase + i < a.Dv) x[u][i] = to_f32<T>(src[i]);
+      }
     }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[i] = fmaf(w[u], x[u][i], acc[i]);
   }
   T* out = static_cast<T*>(a.out) + ((int64_t(b) * a.T + t) * a.Hq + hq) * a.Dv;
   const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
-  for (int i = 0; i < DPL; ++i) {
-    const int d = lane * DPL + i;
-    if (d < a.Dv) out[d] = from_f32<T>(acc[i] * inv);
-  }
+  for (int i = 0; i < DPL; ++i)
+    if (dbase + i < a.Dv) out[dbase + i] = from_f32<T>(acc[i] * inv);
   if (lane == 0 && a.lse) a.lse[(int64_t(b) * a.T + t) * a.Hq + hq] = L > 0.f ? M + logf(L) : -INFINITY;
 }
 

@@ -425,7 +425,7 @@ static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t 
   const int64_t smem = 2 * 128 * 2 * Dp + 2 * C * 2 * (Dp + Dvp) + 1024 + 4096;
   p.tc = (dtype == PISA_BF16 || dtype == PISA_F16) && is_pow2(G) && G <= 32 && D % 16 == 0 &&
          Dv % 16 == 0 && D <= 256 && Dv <= 256 && is_pow2(C) && C >= 16 && C <= 256 &&
-         cols <= 512 && smem <= 227 * 1024 && S > 0 && B * Tq * H * S >= 4096;
+         cols <= 512 && smem <= 227 * 1024 && S > 0 && S <= 64 && B * Tq * H * S >= 4096;
   if (!p.tc) return p;
   const int64_t per_token = H * S * G * (Dv * elem_size(dtype) + 8);
   const int64_t fit = ((int64_t(1) << 31) / per_token) / p.TW * p.TW;

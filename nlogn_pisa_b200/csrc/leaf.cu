@@ -233,7 +233,26 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
         const int64_t key0 = (int64_t(p) * g.br + j) * g.C;
         const int valid_keys = int(min64(g.C, max(int64_t(0), g.N - key0)));
         float score;
-        if (g.method == PISA_METHOD_PISA) {
+        if (g.C == 64 && valid_keys == 64) {
+          // full 64-key block: one TMEM load, packed arithmetic, no masks
+          float v[64];
+          tc::tmem_ld64(acc + j * 64, v);
+          if (g.method == PISA_METHOD_PISA) {
+            const float mx = tc::max64(v);
+            score = mx * g.scale + logf(tc::sum_ex2_64(v, sl, mx * sl));
+          } else {
+            float2 a1 = make_float2(0.f, 0.f), a2 = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int i = 0; i < 64; i += 2) {
+              const float2 pv = make_float2(v[i], v[i + 1]);
+              a1 = tc::add2(a1, pv);
+              a2 = tc::fma2(pv, pv, a2);
+            }
+            const float mean = (a1.x + a1.y) / 64.f;
+            const float var = fmaxf((a2.x + a2.y) / 64.f - mean * mean, 0.f);
+            score = g.scale * mean + g.c2 * var;
+          }
+        } else if (g.method == PISA_METHOD_PISA) {
           float mx = -INFINITY;
           for_columns(acc + j * g.C, g.C, [&](int cc, float x) {
             if (cc < valid_keys) mx = fmaxf(mx, x);

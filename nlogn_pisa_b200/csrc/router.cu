@@ -327,6 +327,125 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const RouteArgs a) {
   }
 }
 
+// Warp-per-item router for descents whose every scored level has precomputed
+// scores (dense.cu): levels >= 1 for pisa/pisa2 when the leaf level is left to
+// the grouped tensor-core scorer (coarse_only), every level for pisa1.  The
+// candidates and scores live in registers (element i in lane i%32, slot
+// i/32), validity is counted with ballots, and the same comparison network
+// picks the K survivors; their children are expanded through shared memory.
+template <int WP>
+__device__ __forceinline__ void warp_sort(float (&s)[8], int (&id)[8], int lane) {
+  float ss[Network<WP>::E];
+  int ii[Network<WP>::E];
+#pragma unroll
+  for (int e = 0; e < Network<WP>::E; ++e) { ss[e] = s[e]; ii[e] = id[e]; }
+  Network<WP>::sort(ss, ii, lane);
+#pragma unroll
+  for (int e = 0; e < Network<WP>::E; ++e) { s[e] = ss[e]; id[e] = ii[e]; }
+}
+
+__global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
+  __shared__ int kept[4][64];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t local = int64_t(blockIdx.x) * 4 + warp;
+  if (local >= int64_t(a.B) * a.t_count * a.H) return;
+  const int h = int(local % a.H);
+  const int tl = int((local / a.H) % a.t_count);
+  const int b = int(local / (int64_t(a.H) * a.t_count));
+  const int t = a.t_begin + tl;
+  const int64_t item = (int64_t(b) * a.T + t) * a.H + h;
+  const int64_t pos = a.positions ? a.positions[int64_t(b) * a.T + t] : a.pos_offset + t;
+  const float* dense_row = a.dense + local * a.dense_stride;
+  const int64_t leaf = pos / a.C;
+  int64_t span = a.C, div = 1;
+  for (int l = 0; l < a.top; ++l) { span *= a.br; div *= a.br; }
+
+  int id[8];
+  float sc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) id[e] = e * 32 + lane;   // top level: 0..first_width-1
+  int width = a.first_width;
+  for (int level = a.top; level >= 0; --level) {
+    const int len = a.levels.size[level];
+    bool valid[8], forced[8];
+    int nvalid = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int i = e * 32 + lane;
+      int v = i < width ? id[e] : -1;
+      if (v >= len) v = -1;
+      id[e] = v;
+      valid[e] = v >= 0 && int64_t(v) * span <= pos;
+      bool f = false;
+      if (valid[e]) {
+        if (a.force_first && v == 0) f = true;
+        for (int r = 0; r < a.force_recent; ++r) {
+          const int64_t target = leaf - r;
+          if (target >= 0 && v == target / div) f = true;
+        }
+      }
+      forced[e] = f;
+      nvalid += __popc(__ballot_sync(kFull, valid[e]));
+    }
+    const bool identity = a.method != PISA_METHOD_PISA1 && nvalid <= a.K;
+    if (level == 0 && a.coarse_only) {
+      int32_t* dst = a.candidates + item * a.W0;
+      uint8_t* fdst = a.flags + item * a.W0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int i = e * 32 + lane;
+        if (i < width) {
+          const bool scoreable = valid[e] && !forced[e] && !identity;
+          dst[i] = id[e];
+          fdst[i] = uint8_t((valid[e] ? 1 : 0) | (forced[e] ? 2 : 0) | (scoreable ? 4 : 0));
+        }
+      }
+      return;
+    }
+    const int off = a.dense_off[level];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const bool scoreable = valid[e] && !forced[e] && !identity;
+      float v = scoreable ? dense_row[off + id[e]] : 0.f;
+      sc[e] = !valid[e] ? kNegFill : (forced[e] ? kPosFill : v);
+      if (e * 32 + lane >= width) { sc[e] = kNegFill; id[e] = -1; }
+    }
+    switch (width) {
+      case 16: warp_sort<16>(sc, id, lane); break;
+      case 32: warp_sort<32>(sc, id, lane); break;
+      case 64: warp_sort<64>(sc, id, lane); break;
+      case 128: warp_sort<128>(sc, id, lane); break;
+      default: warp_sort<256>(sc, id, lane); break;
+    }
+    if (level == 0) {
+      int64_t* out = a.out_ids + item * a.K;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int i = e * 32 + lane;
+        if (i < a.K) out[i] = (id[e] < 0 || int64_t(id[e]) * a.C > pos) ? -1 : id[e];
+      }
+      return;
+    }
+    // survivors -> shared memory -> children in network order
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int i = e * 32 + lane;
+      if (i < a.K) kept[warp][i] = id[e];
+    }
+    __syncwarp();
+    width = a.K * a.br;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int i = e * 32 + lane;
+      const int parent = i < width ? kept[warp][i / a.br] : -1;
+      id[e] = parent < 0 ? -1 : parent * a.br + i % a.br;
+    }
+    __syncwarp();
+    span /= a.br;
+    div /= a.br;
+  }
+}
+
 template <typename T, int GMAX>
 int launch_route(const RouteArgs& a, cudaStream_t stream) {
   const size_t smem = size_t(a.G) * a.D * sizeof(float) + kMaxWidth * (2 * sizeof(int) + 1);
@@ -355,6 +474,22 @@ int route_t(const RouteArgs& a, cudaStream_t stream) {
 }  // namespace
 
 int route(const RouteArgs& a, int dtype, cudaStream_t stream) {
+  // every scored level precomputed: the warp-per-item router
+  bool all_dense = a.dense != nullptr;
+  for (int l = a.top; l >= 0 && all_dense; --l) {
+    if (l == 0 && a.coarse_only) break;
+    if (a.dense_off[l] < 0) {
+      // unscored levels are fine only when every row takes the all-fit shortcut
+      if (a.method == PISA_METHOD_PISA1 || a.levels.size[l] > a.K) all_dense = false;
+    }
+  }
+  if (all_dense) {
+    const int64_t items = int64_t(a.B) * a.t_count * a.H;
+    if (items == 0) return PISA_OK;
+    route_warp_kernel<<<unsigned((items + 3) / 4), 128, 0, stream>>>(a);
+    PISA_CHECK_LAUNCH();
+    return PISA_OK;
+  }
   switch (dtype) {
     case PISA_F32: return route_t<float>(a, stream);
     case PISA_BF16: return route_t<__nv_bfloat16>(a, stream);
