@@ -123,6 +123,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
   __shared__ uint32_t tmem_slot;
   __shared__ int64_t s_qoff[2][128];
   __shared__ int s_kvb[2];
+  // per-tile metadata ring for the epilogue (4 slots; slot it%4 is rewritten
+  // only after tile it-4's epilogue, which tile it-2's Q K^T already waited for)
+  __shared__ uint64_t meta_full[4];
+  __shared__ int s_req[4][128], s_nv[4][128];
   __shared__ int s_fail;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -143,6 +147,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
       tc::mbar_init(&o_full[i], 1);
       tc::mbar_init(&acc_empty[i], 128);
     }
+    for (int i = 0; i < 4; ++i) tc::mbar_init(&meta_full[i], kLoadWarps * 32);
     s_fail = 0;
     tc::fence_barrier_init();
   }
@@ -165,11 +170,18 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
     const T* kbase = static_cast<const T*>(a.k);
     const T* vbase = static_cast<const T*>(a.v);
     int64_t cur_kv = -1;
-    int kvb = 1, used[2] = {0, 0};
+    int kvb = 1, used0 = 0, used1 = 0;
+    // metadata of the next tile is fetched one iteration ahead
+    int owner_next = a.tile_owner[first];
+    int req_next = ptid < a.RT ? a.tile_req[int64_t(first) * a.RT + ptid] : -1;
     for (int it = 0; it < ntiles; ++it) {
       const int tile = first + it, s = it & 1;
+      const int owner = owner_next, req = req_next;
+      if (it + 1 < ntiles) {
+        owner_next = a.tile_owner[tile + 1];
+        req_next = ptid < a.RT ? a.tile_req[int64_t(tile + 1) * a.RT + ptid] : -1;
+      }
       if (!tc::mbar_wait(&q_empty[s], ((it >> 1) & 1) ^ 1)) { s_fail = 1; break; }
-      const int owner = a.tile_owner[tile];
       const int blk = owner % a.NB;
       const int h = (owner / a.NB) % a.H;
       const int b = owner / (a.NB * a.H * a.nwin);
@@ -179,11 +191,11 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
         // The buffer being replaced was last read by tile it-2 or earlier:
         // wait for that P.V (with one TMEM buffer, the in-order issue makes
         // P.V of tile it-1 the one to wait for; it never needs tile it).
-        if (used[kvb]) {
+        if (kvb ? used1 : used0) {
           const int wt = nacc == 2 ? it - 2 : it - 1;
           if (wt >= 0 && !tc::mbar_wait(&o_full[acc_of(wt)], round_of(wt) & 1)) { s_fail = 1; break; }
         }
-        used[kvb] = 1;
+        if (kvb) used1 = 1; else used0 = 1;
         const uint32_t ks_addr = kv_addr + kvb * kv_bytes, vs_addr = ks_addr + qch * a.C * 128;
         const int64_t tok0 = int64_t(blk) * a.C;
         const T* kb = kbase + b * a.k_sb + int64_t(h) * a.k_sh;
@@ -204,16 +216,23 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
         }
         cur_kv = kv_key;
       }
-      if (ptid < a.RT) {
-        const int req = a.tile_req[int64_t(tile) * a.RT + ptid];
+      const int slot = it & 3;
+      if (ptid < 128) {
         int64_t off = -1;
+        int nv = 0;
         if (req >= 0) {
           const Req q = decode_req(req, a);
           off = q.b * a.q_sb + int64_t(a.t0 + q.tl) * a.q_st + int64_t(q.h * a.G) * a.q_sh;
+          int64_t limit = a.N;
+          if (a.causal) limit = min64(limit, position_of(a, q.b, a.t0 + q.tl) + 1);
+          nv = int(max(int64_t(0), min64(int64_t(a.C), limit - int64_t(blk) * a.C)));
         }
-        s_qoff[s][ptid] = off;
+        if (ptid < a.RT) s_qoff[s][ptid] = off;
+        s_req[slot][ptid] = req;
+        s_nv[slot][ptid] = nv;
       }
       if (ptid == 0) s_kvb[s] = kvb;
+      tc::mbar_arrive(&meta_full[slot]);
       tc::named_sync(1, kLoadWarps * 32);
       const int c = ptid & (vpr - 1);
       const uint32_t qdst = qs_addr + s * q_stage_bytes + (c >> 3) * 128 * 128;
@@ -233,15 +252,16 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
     if (lane == 0) {
       const uint32_t idesc_s = tc::idesc_f16(128, a.C, a.bf16);
       const uint32_t idesc_o = tc::idesc_f16(128, a.Dv, a.bf16, 1);
-      int kv_of[2] = {0, 0};  // K/V buffer of the last two tiles (by parity)
+      int kv_even = 0, kv_odd = 0;  // K/V buffer of the last even / odd tile
       // S = Q K^T of tile `it` into its buffer
       auto issue_s = [&](int it) -> bool {
         const int s = it & 1, ab = acc_of(it);
         if (!tc::mbar_wait(&q_full[s], (it >> 1) & 1)) return false;
         if (!tc::mbar_wait(&acc_empty[ab], (round_of(it) & 1) ^ 1)) return false;
         tc::fence_after_sync();
-        kv_of[it & 1] = s_kvb[s];
-        const uint32_t ks_addr = kv_addr + kv_of[it & 1] * kv_bytes;
+        const int kvb = s_kvb[s];
+        if (it & 1) kv_odd = kvb; else kv_even = kvb;
+        const uint32_t ks_addr = kv_addr + kvb * kv_bytes;
         const uint32_t qa = qs_addr + s * q_stage_bytes;
         const uint32_t sacc = tmem + ab * a.acc_cols;
         for (int ks = 0; ks < a.Dp / 16; ++ks) {
@@ -259,7 +279,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
         if (!tc::mbar_wait(&p_full[ab], round_of(pt) & 1)) return false;
         tc::fence_after_sync();
         const uint32_t base = tmem + ab * a.acc_cols;
-        const uint32_t vs_addr = kv_addr + kv_of[pt & 1] * kv_bytes + qch * a.C * 128;
+        const uint32_t vs_addr = kv_addr + ((pt & 1) ? kv_odd : kv_even) * kv_bytes + qch * a.C * 128;
         for (int ks = 0; ks < a.C / 16; ++ks) {
           const uint64_t vd = tc::desc_make(vs_addr + ks * 16 * 128, uint32_t(a.C) * 128, 1024, 2);
           tc::mma_f16_ts(base + a.o_col, base + a.p_col + ks * 8, vd, idesc_o, ks > 0);
@@ -298,16 +318,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
       const bool got = tc::mbar_wait(&s_full[ab], rnd & 1);
       if (!got) s_fail = 1;
       tc::fence_after_sync();
-      const int owner = a.tile_owner[tile];
-      const int blk = owner % a.NB;
-      const int req = r < a.RT ? a.tile_req[int64_t(tile) * a.RT + r] : -1;
-      int nvalid = 0;
-      if (req >= 0) {
-        const Req q = decode_req(req, a);
-        int64_t limit = a.N;
-        if (a.causal) limit = min64(limit, position_of(a, q.b, a.t0 + q.tl) + 1);
-        nvalid = int(max(int64_t(0), min64(int64_t(a.C), limit - int64_t(blk) * a.C)));
-      }
+      if (!tc::mbar_wait(&meta_full[it & 3], (it >> 2) & 1)) s_fail = 1;
+      const int req = r < a.RT ? s_req[it & 3][r] : -1;
+      const int nvalid = r < a.RT ? s_nv[it & 3][r] : 0;
+      (void)tile;
       const uint32_t base = tmem + lane_base + ab * a.acc_cols;
       float mx = -INFINITY;
       float l = 0.f;
@@ -385,10 +399,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
           uint4* dst = reinterpret_cast<uint4*>(part_o + pi * a.Dv + c0);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            dst[i] = make_uint4(pack2<T>(v[8 * i] * inv, v[8 * i + 1] * inv),
-                                pack2<T>(v[8 * i + 2] * inv, v[8 * i + 3] * inv),
-                                pack2<T>(v[8 * i + 4] * inv, v[8 * i + 5] * inv),
-                                pack2<T>(v[8 * i + 6] * inv, v[8 * i + 7] * inv));
+            __stcs(dst + i, make_uint4(pack2<T>(v[8 * i] * inv, v[8 * i + 1] * inv),
+                                       pack2<T>(v[8 * i + 2] * inv, v[8 * i + 3] * inv),
+                                       pack2<T>(v[8 * i + 4] * inv, v[8 * i + 5] * inv),
+                                       pack2<T>(v[8 * i + 6] * inv, v[8 * i + 7] * inv)));
           }
         }
       }
@@ -402,7 +416,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
             for (int i = 0; i < 16; ++i) w[i] = pack2<T>(v[2 * i] * inv, v[2 * i + 1] * inv);
             uint4* dst = reinterpret_cast<uint4*>(part_o + pi * a.Dv + c0);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            for (int i = 0; i < 4; ++i) __stcs(dst + i, make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]));
           }
         } else {
           float v[16];
@@ -412,12 +426,12 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
 #pragma unroll
             for (int i = 0; i < 8; ++i) w[i] = pack2<T>(v[2 * i] * inv, v[2 * i + 1] * inv);
             uint4* dst = reinterpret_cast<uint4*>(part_o + pi * a.Dv + c0);
-            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            __stcs(dst, make_uint4(w[0], w[1], w[2], w[3]));
+            __stcs(dst + 1, make_uint4(w[4], w[5], w[6], w[7]));
           }
         }
       }
-      if (req >= 0) reinterpret_cast<float2*>(a.part_ml)[pi] = make_float2(mx * a.scale, l);
+      if (req >= 0) __stcs(reinterpret_cast<float2*>(a.part_ml) + pi, make_float2(mx * a.scale, l));
       tc::fence_before_sync();
       tc::mbar_arrive(&acc_empty[ab]);
       if (!got || !got2) break;
@@ -453,7 +467,7 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnTcArgs a) {
   for (int k = 0; k < 2; ++k) {
     const int s = lane + 32 * k;
     if (s < a.S && visible_block(a, b, t, h, s) >= 0) {
-      const float2 ml = part_ml[(slot0 + s) * a.G + g];
+      const float2 ml = __ldcs(part_ml + (slot0 + s) * a.G + g);
       if (ml.y > 0.f) { m_s[k] = ml.x; l_s[k] = ml.y; }
     }
   }
@@ -480,7 +494,7 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnTcArgs a) {
         const T* src = part_o + ((slot0 + s) * a.G + g) * a.Dv + dbase;
 #pragma unroll
         for (int i = 0; i < DPL; ++i)
-          if (dbase + i < a.Dv) x[u][i] = to_f32<T>(src[i]);
+          if (dbase + i < a.Dv) x[u][i] = to_f32<T>(__ldcs(src + i));
       }
     }
 #pragma unroll

@@ -103,6 +103,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
   __shared__ uint32_t tmem_slot;
   __shared__ int64_t s_qoff[2][128];
   __shared__ int s_fail;
+  // per-tile metadata ring for the epilogue (slot it%4 is rewritten only after
+  // tile it-4's epilogue, which the MMA of tile it-2 already waited for)
+  __shared__ uint64_t meta_full[4];
+  __shared__ int s_dst[4][128], s_fam[4];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int total = *g.total_tiles;
@@ -119,6 +123,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
       tc::mbar_init(&full_acc[i], 1);
       tc::mbar_init(&empty_acc[i], kEpiWarps * 32);
     }
+    for (int i = 0; i < 4; ++i) tc::mbar_init(&meta_full[i], kLoadWarps * 32);
     s_fail = 0;
     tc::fence_barrier_init();
   }
@@ -139,10 +144,17 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
     const T* qbase = static_cast<const T*>(g.q);
     const T* kbase = static_cast<const T*>(g.keys);
     int cur_key = -1;
+    // metadata of the next tile is fetched one iteration ahead
+    int owner_next = g.tile_owner[first];
+    int req_next = ptid < g.RT ? g.tile_req[int64_t(first) * g.RT + ptid] : -1;
     for (int it = 0; it < ntiles; ++it) {
       const int tile = first + it, s = it & 1;
+      const int owner = owner_next, req = req_next;
+      if (it + 1 < ntiles) {
+        owner_next = g.tile_owner[tile + 1];
+        req_next = ptid < g.RT ? g.tile_req[int64_t(tile + 1) * g.RT + ptid] : -1;
+      }
       if (!tc::mbar_wait(&empty_q[s], ((it >> 1) & 1) ^ 1)) { s_fail = 1; break; }
-      const int owner = g.tile_owner[tile];
       const int p = owner % g.NP;
       const int h = (owner / g.NP) % g.H;
       const int b = owner / (g.NP * g.H * g.nwin);
@@ -160,15 +172,19 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
         }
         cur_key = kkey;
       }
-      if (ptid < g.RT) {
-        const int req = g.tile_req[int64_t(tile) * g.RT + ptid];
+      {
         int64_t off = -1;
+        int dst = -1;
         if (req >= 0) {
           const int rowid = req / g.NF;
           const int hh = rowid % g.H, t = (rowid / g.H) % g.T, bb = rowid / (g.H * g.T);
           off = bb * g.q_sb + int64_t(t) * g.q_st + int64_t(hh * g.G) * g.q_sh;
+          dst = rowid * g.W0 + (req - rowid * g.NF) * g.br;
         }
-        s_qoff[s][ptid] = off;
+        if (ptid < g.RT) s_qoff[s][ptid] = off;
+        s_dst[it & 3][ptid] = dst;
+        if (ptid == 0) s_fam[it & 3] = p;
+        tc::mbar_arrive(&meta_full[it & 3]);
       }
       tc::named_sync(1, kLoadWarps * 32);
       const uint32_t qdst = qs_addr + s * q_stage_bytes + (c >> 3) * 128 * 128;
@@ -224,9 +240,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
       const bool got = tc::mbar_wait(&full_acc[a], ra & 1);
       if (!got) s_fail = 1;
       tc::fence_after_sync();
-      const int owner = g.tile_owner[tile];
-      const int p = owner % g.NP;
-      const int req = r < g.RT ? g.tile_req[int64_t(tile) * g.RT + r] : -1;
+      if (!tc::mbar_wait(&meta_full[it & 3], (it >> 2) & 1)) s_fail = 1;
+      const int p = s_fam[it & 3];
+      const int dst = r < g.RT ? s_dst[it & 3][r] : -1;
+      (void)tile;
       const uint32_t acc = tmem + lane_base + a * NK;
       for (int jj = 0; jj < jn; ++jj) {
         const int j = half * jn + jj;
@@ -274,10 +291,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
         }
         if (valid_keys == 0) score = 0.f;
         for (int o = 1; o < g.G; o <<= 1) score += __shfl_xor_sync(kFull, score, o);
-        if (req >= 0 && (row & (g.G - 1)) == 0) {
-          const int rowid = req / g.NF, k = req - (req / g.NF) * g.NF;
-          g.scores[int64_t(rowid) * g.W0 + k * g.br + j] = score;
-        }
+        if (dst >= 0 && (row & (g.G - 1)) == 0) g.scores[int64_t(dst) + j] = score;
       }
       tc::fence_before_sync();
       tc::mbar_arrive(&empty_acc[a]);
