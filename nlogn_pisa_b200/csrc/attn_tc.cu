@@ -38,14 +38,17 @@ __device__ __forceinline__ int64_t index_at(const void* p, int bytes, int64_t i)
 struct Req {
   int b, tl, h, s;
 };
-__device__ __forceinline__ Req decode_req(int64_t lr, const AttnTcArgs& a) {
+__device__ __forceinline__ Req decode_req(int64_t lr64, const AttnTcArgs& a) {
+  // chunk-local request indices are below 2^31 (checked on the host)
+  const uint32_t lr = uint32_t(lr64);
   Req r;
-  r.s = int(lr % a.S);
-  int64_t row = lr / a.S;
-  r.h = int(row % a.H);
-  row /= a.H;
-  r.tl = int(row % a.tlen);
-  r.b = int(row / a.tlen);
+  uint32_t row = lr / uint32_t(a.S);
+  r.s = int(lr - row * uint32_t(a.S));
+  uint32_t rest = row / uint32_t(a.H);
+  r.h = int(row - rest * uint32_t(a.H));
+  const uint32_t b = rest / uint32_t(a.tlen);
+  r.tl = int(rest - b * uint32_t(a.tlen));
+  r.b = int(b);
   return r;
 }
 
@@ -106,7 +109,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 //   warp 12          MMA issue: S(i+1) = Q K^T is issued before O(i) = P V
 // mbarriers per stage/buffer: q_full/q_empty (query stages), s_full, p_full,
 // o_full, acc_empty (TMEM buffer of S, P and O).  All waits are bounded.
-constexpr int kEpiWarps = 8, kLoadWarps = 4, kMmaWarp = 12;
+constexpr int kEpiWarps = 8, kLoadWarps = 4, kMmaWarp = 12, kStages = 3;
 constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
 
 template <typename T>
@@ -118,15 +121,16 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
   // two K/V buffers, each [qch][C keys][128 B] of keys then [vch][C keys][128 B]
   // of values (value dims contiguous); a block change switches buffers
   const int kv_bytes = (qch + vch) * a.C * 128;
-  uint8_t* KV = smem + 2 * q_stage_bytes;
-  __shared__ uint64_t q_full[2], q_empty[2], s_full[2], p_full[2], o_full[2], acc_empty[2];
+  uint8_t* KV = smem + kStages * q_stage_bytes;
+  __shared__ uint64_t q_full[kStages], q_empty[kStages], s_full[2], p_full[2], o_full[2], acc_empty[2];
   __shared__ uint32_t tmem_slot;
-  __shared__ int64_t s_qoff[2][128];
-  __shared__ int s_kvb[2];
-  // per-tile metadata ring for the epilogue (4 slots; slot it%4 is rewritten
-  // only after tile it-4's epilogue, which tile it-2's Q K^T already waited for)
-  __shared__ uint64_t meta_full[4];
-  __shared__ int s_req[4][128], s_nv[4][128];
+  __shared__ int64_t s_qoff[kStages][128];
+  __shared__ int s_kvb[kStages];
+  // per-tile metadata ring for the epilogue (8 slots): the producer runs at
+  // most kStages tiles ahead of the MMAs and they at most two ahead of the
+  // epilogue, so slot it%8 is free again when tile it is produced
+  __shared__ uint64_t meta_full[8];
+  __shared__ int s_req[8][128], s_nv[8][128];
   __shared__ int s_fail;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -139,15 +143,17 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
   const int nacc = a.nacc;
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       tc::mbar_init(&q_full[i], kLoadWarps * 32);
       tc::mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&s_full[i], 1);
       tc::mbar_init(&p_full[i], 128);
       tc::mbar_init(&o_full[i], 1);
       tc::mbar_init(&acc_empty[i], 128);
     }
-    for (int i = 0; i < 4; ++i) tc::mbar_init(&meta_full[i], kLoadWarps * 32);
+    for (int i = 0; i < 8; ++i) tc::mbar_init(&meta_full[i], kLoadWarps * 32);
     s_fail = 0;
     tc::fence_barrier_init();
   }
@@ -175,13 +181,13 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
     int owner_next = a.tile_owner[first];
     int req_next = ptid < a.RT ? a.tile_req[int64_t(first) * a.RT + ptid] : -1;
     for (int it = 0; it < ntiles; ++it) {
-      const int tile = first + it, s = it & 1;
+      const int tile = first + it, s = it % kStages, rnd = it / kStages;
       const int owner = owner_next, req = req_next;
       if (it + 1 < ntiles) {
         owner_next = a.tile_owner[tile + 1];
         req_next = ptid < a.RT ? a.tile_req[int64_t(tile + 1) * a.RT + ptid] : -1;
       }
-      if (!tc::mbar_wait(&q_empty[s], ((it >> 1) & 1) ^ 1)) { s_fail = 1; break; }
+      if (!tc::mbar_wait(&q_empty[s], (rnd & 1) ^ 1)) { s_fail = 1; break; }
       const int blk = owner % a.NB;
       const int h = (owner / a.NB) % a.H;
       const int b = owner / (a.NB * a.H * a.nwin);
@@ -216,7 +222,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
         }
         cur_kv = kv_key;
       }
-      const int slot = it & 3;
+      const int slot = it & 7;
       if (ptid < 128) {
         int64_t off = -1;
         int nv = 0;
@@ -243,10 +249,11 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
         if (off >= 0 && c * 8 < a.D) cp_async16(dst, qbase + off + int64_t(gh) * a.q_sh + c * 8);
         else st_zero16(dst);
       }
-      cp_async_wait_all();
+      // completion is tracked by the barrier; the next stage starts immediately
       tc::fence_async_smem();
-      tc::mbar_arrive(&q_full[s]);
+      tc::cp_async_arrive(&q_full[s]);
     }
+    cp_async_wait_all();
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issue ----------------
     if (lane == 0) {
@@ -255,9 +262,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
       int kv_even = 0, kv_odd = 0;  // K/V buffer of the last even / odd tile
       // S = Q K^T of tile `it` into its buffer
       auto issue_s = [&](int it) -> bool {
-        const int s = it & 1, ab = acc_of(it);
-        if (!tc::mbar_wait(&q_full[s], (it >> 1) & 1)) return false;
+        const int s = it % kStages, ab = acc_of(it);
+        if (!tc::mbar_wait(&q_full[s], (it / kStages) & 1)) return false;
         if (!tc::mbar_wait(&acc_empty[ab], (round_of(it) & 1) ^ 1)) return false;
+        tc::fence_async_smem();
         tc::fence_after_sync();
         const int kvb = s_kvb[s];
         if (it & 1) kv_odd = kvb; else kv_even = kvb;
@@ -318,9 +326,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
       const bool got = tc::mbar_wait(&s_full[ab], rnd & 1);
       if (!got) s_fail = 1;
       tc::fence_after_sync();
-      if (!tc::mbar_wait(&meta_full[it & 3], (it >> 2) & 1)) s_fail = 1;
-      const int req = r < a.RT ? s_req[it & 3][r] : -1;
-      const int nvalid = r < a.RT ? s_nv[it & 3][r] : 0;
+      if (!tc::mbar_wait(&meta_full[it & 7], (it >> 3) & 1)) s_fail = 1;
+      const int req = r < a.RT ? s_req[it & 7][r] : -1;
+      const int nvalid = r < a.RT ? s_nv[it & 7][r] : 0;
       (void)tile;
       const uint32_t base = tmem + lane_base + ab * a.acc_cols;
       float mx = -INFINITY;
@@ -510,10 +518,85 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnTcArgs a) {
   if (lane == 0 && a.lse) a.lse[(int64_t(b) * a.T + t) * a.Hq + hq] = L > 0.f ? M + logf(L) : -INFINITY;
 }
 
+// Same merge with 16-byte loads: the two half-warps take alternate slots
+// and each lane covers VPL (= Dv/16) value columns; 8 slots in flight.
+template <typename T, int VPL>
+__global__ void __launch_bounds__(128) attn_combine16_kernel(const AttnTcArgs a) {
+  const int64_t idx = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (idx >= int64_t(a.B) * a.tlen * a.Hq) return;
+  const int hq = int(idx % a.Hq);
+  const int tl = int((idx / a.Hq) % a.tlen);
+  const int b = int(idx / (int64_t(a.Hq) * a.tlen));
+  const int h = hq / a.G, g = hq % a.G;
+  const int t = a.t0 + tl;
+  const int64_t slot0 = ((int64_t(b) * a.tlen + tl) * a.H + h) * a.S;
+  const T* part_o = static_cast<const T*>(a.part_o);
+  const float2* part_ml = reinterpret_cast<const float2*>(a.part_ml);
+  float m_s[2] = {-INFINITY, -INFINITY}, l_s[2] = {0.f, 0.f};
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int sl = lane + 32 * k;
+    if (sl < a.S && visible_block(a, b, t, h, sl) >= 0) {
+      const float2 ml = __ldcs(part_ml + (slot0 + sl) * a.G + g);
+      if (ml.y > 0.f) { m_s[k] = ml.x; l_s[k] = ml.y; }
+    }
+  }
+  const float M = warp_max(fmaxf(m_s[0], m_s[1]));
+  float w_s[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) w_s[k] = (M == -INFINITY || m_s[k] == -INFINITY) ? 0.f : l_s[k] * expf(m_s[k] - M);
+  const float L = warp_sum(w_s[0] + w_s[1]);
+  const int half = lane >> 4, hl = lane & 15;
+  float acc[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) acc[i] = 0.f;
+  constexpr int kBytes = VPL * int(sizeof(T));   // 8, 16 or 32 per lane and slot
+  for (int s0 = 0; s0 < a.S; s0 += 8) {
+    float w[4];
+    uint4 raw[4][(kBytes + 15) / 16];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int sl = s0 + 2 * u + half;
+      const float w0 = __shfl_sync(kFull, w_s[0], sl & 31);
+      const float w1 = __shfl_sync(kFull, w_s[1], sl & 31);
+      w[u] = sl < a.S ? (sl < 32 ? w0 : w1) : 0.f;
+      const T* src = part_o + ((slot0 + sl) * a.G + g) * a.Dv + hl * VPL;
+#pragma unroll
+      for (int c = 0; c < (kBytes + 15) / 16; ++c) {
+        if (w[u] > 0.f) {
+          if constexpr (kBytes >= 16) raw[u][c] = __ldcs(reinterpret_cast<const uint4*>(src) + c);
+          else {
+            const uint2 r2 = __ldcs(reinterpret_cast<const uint2*>(src));
+            raw[u][c] = make_uint4(r2.x, r2.y, 0u, 0u);
+          }
+        } else {
+          raw[u][c] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const T* e = reinterpret_cast<const T*>(raw[u]);
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) acc[i] = fmaf(w[u], to_f32<T>(e[i]), acc[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) acc[i] += __shfl_xor_sync(kFull, acc[i], 16);
+  T* out = static_cast<T*>(a.out) + ((int64_t(b) * a.T + t) * a.Hq + hq) * a.Dv;
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  if (half == 0) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) out[hl * VPL + i] = from_f32<T>(acc[i] * inv);
+  }
+  if (lane == 0 && a.lse) a.lse[(int64_t(b) * a.T + t) * a.Hq + hq] = L > 0.f ? M + logf(L) : -INFINITY;
+}
+
 template <typename T>
 int attn_tc_typed(AttnTcArgs a, cudaStream_t stream) {
   const int qch = a.Dp / 64, vch = a.Dvp / 64;
-  const size_t smem = size_t(2) * 128 * 128 * qch + size_t(2) * a.C * 128 * (qch + vch) + 1024;
+  const size_t smem = size_t(kStages) * 128 * 128 * qch + size_t(2) * a.C * 128 * (qch + vch) + 1024;
   cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return fail_cuda(e, "attention smem attribute");
   for (int t0 = 0; t0 < a.T; t0 += a.chunk) {
@@ -537,7 +620,10 @@ int attn_tc_typed(AttnTcArgs a, cudaStream_t stream) {
     attn_tc_kernel<T><<<unsigned(a.num_sms), kPipeThreads, smem, stream>>>(a);
     PISA_CHECK_LAUNCH();
     const unsigned cgrid = unsigned((int64_t(a.B) * a.tlen * a.Hq + 3) / 4);
-    if (a.Dv <= 32) attn_combine_kernel<T, 1><<<cgrid, 128, 0, stream>>>(a);
+    if (a.Dv == 64) attn_combine16_kernel<T, 4><<<cgrid, 128, 0, stream>>>(a);
+    else if (a.Dv == 128) attn_combine16_kernel<T, 8><<<cgrid, 128, 0, stream>>>(a);
+    else if (a.Dv == 256) attn_combine16_kernel<T, 16><<<cgrid, 128, 0, stream>>>(a);
+    else if (a.Dv <= 32) attn_combine_kernel<T, 1><<<cgrid, 128, 0, stream>>>(a);
     else if (a.Dv <= 64) attn_combine_kernel<T, 2><<<cgrid, 128, 0, stream>>>(a);
     else if (a.Dv <= 128) attn_combine_kernel<T, 4><<<cgrid, 128, 0, stream>>>(a);
     else attn_combine_kernel<T, 8><<<cgrid, 128, 0, stream>>>(a);

@@ -153,7 +153,7 @@ static bool grouped_tc_eligible(int64_t Hq, int64_t H, int64_t D, int dtype, int
   return schedule == PISA_SCHEDULE_GROUPED && (dtype == PISA_BF16 || dtype == PISA_F16) &&
          (method == PISA_METHOD_PISA || method == PISA_METHOD_PISA2) && is_pow2(G) && G <= 32 &&
          D % 8 == 0 && D <= 256 && br * C <= 512 &&
-         (D <= 64 ? 1 : D <= 128 ? 2 : 4) * 128 * (2 * 128 + br * C) + 1024 + 4096 <= 227 * 1024;
+         (D <= 64 ? 1 : D <= 128 ? 2 : 4) * 128 * (3 * 128 + br * C) + 1024 + 8192 <= 227 * 1024;
 }
 
 static SelectPlan plan_select(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t N,
@@ -422,7 +422,7 @@ static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t 
   p.nacc = 2 * p.acc_cols <= 512 ? 2 : 1;
   p.tmem_cols = p.nacc * p.acc_cols;
   const int64_t Dp = D <= 64 ? 64 : D <= 128 ? 128 : 256, Dvp = Dv <= 64 ? 64 : Dv <= 128 ? 128 : 256;
-  const int64_t smem = 2 * 128 * 2 * Dp + 2 * C * 2 * (Dp + Dvp) + 1024 + 4096;
+  const int64_t smem = 3 * 128 * 2 * Dp + 2 * C * 2 * (Dp + Dvp) + 1024 + 8192;
   p.tc = (dtype == PISA_BF16 || dtype == PISA_F16) && is_pow2(G) && G <= 32 && D % 16 == 0 &&
          Dv % 16 == 0 && D <= 256 && Dv <= 256 && is_pow2(C) && C >= 16 && C <= 256 &&
          cols <= 512 && smem <= 227 * 1024 && S > 0 && S <= 64 && B * Tq * H * S >= 4096;

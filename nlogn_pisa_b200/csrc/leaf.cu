@@ -86,7 +86,7 @@ __global__ void family_scatter_kernel(const GroupArgs g, const int32_t* __restri
 // mbarriers: full_q/empty_q guard the query stages, full_acc/empty_acc the
 // accumulators; the parity of round r is r & 1 (empty waits start at 1, so the
 // first round passes).  Every wait is bounded and records a timeout status.
-constexpr int kEpiWarps = 8, kLoadWarps = 4, kMmaWarp = 12;
+constexpr int kEpiWarps = 8, kLoadWarps = 4, kMmaWarp = 12, kStages = 3;
 constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
 
 template <typename T>
@@ -98,15 +98,16 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
   const int vpr = Dp / 8;                    // 16-byte vectors per row (divides 128)
   const int NK = g.br * g.C;                 // keys per family = MMA N
   const int q_stage_bytes = chunks * 128 * 128;
-  uint8_t* Ks = smem + 2 * q_stage_bytes;    // [chunks][NK][128 B]
-  __shared__ uint64_t full_q[2], empty_q[2], full_acc[2], empty_acc[2];
+  uint8_t* Ks = smem + kStages * q_stage_bytes;    // [chunks][NK][128 B]
+  __shared__ uint64_t full_q[kStages], empty_q[kStages], full_acc[2], empty_acc[2];
   __shared__ uint32_t tmem_slot;
-  __shared__ int64_t s_qoff[2][128];
+  __shared__ int64_t s_qoff[kStages][128];
   __shared__ int s_fail;
-  // per-tile metadata ring for the epilogue (slot it%4 is rewritten only after
-  // tile it-4's epilogue, which the MMA of tile it-2 already waited for)
-  __shared__ uint64_t meta_full[4];
-  __shared__ int s_dst[4][128], s_fam[4];
+  // per-tile metadata ring for the epilogue (8 slots): the producer runs at
+  // most kStages tiles ahead of the MMAs and they at most two ahead of the
+  // epilogue, so slot it%8 is free again when tile it is produced
+  __shared__ uint64_t meta_full[8];
+  __shared__ int s_dst[8][128], s_fam[8];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int total = *g.total_tiles;
@@ -117,13 +118,15 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
   const int ntiles = last - first;
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       tc::mbar_init(&full_q[i], kLoadWarps * 32);
       tc::mbar_init(&empty_q[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&full_acc[i], 1);
       tc::mbar_init(&empty_acc[i], kEpiWarps * 32);
     }
-    for (int i = 0; i < 4; ++i) tc::mbar_init(&meta_full[i], kLoadWarps * 32);
+    for (int i = 0; i < 8; ++i) tc::mbar_init(&meta_full[i], kLoadWarps * 32);
     s_fail = 0;
     tc::fence_barrier_init();
   }
@@ -148,20 +151,20 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
     int owner_next = g.tile_owner[first];
     int req_next = ptid < g.RT ? g.tile_req[int64_t(first) * g.RT + ptid] : -1;
     for (int it = 0; it < ntiles; ++it) {
-      const int tile = first + it, s = it & 1;
+      const int tile = first + it, s = it % kStages, rnd = it / kStages;
       const int owner = owner_next, req = req_next;
       if (it + 1 < ntiles) {
         owner_next = g.tile_owner[tile + 1];
         req_next = ptid < g.RT ? g.tile_req[int64_t(tile + 1) * g.RT + ptid] : -1;
       }
-      if (!tc::mbar_wait(&empty_q[s], ((it >> 1) & 1) ^ 1)) { s_fail = 1; break; }
+      if (!tc::mbar_wait(&empty_q[s], (rnd & 1) ^ 1)) { s_fail = 1; break; }
       const int p = owner % g.NP;
       const int h = (owner / g.NP) % g.H;
       const int b = owner / (g.NP * g.H * g.nwin);
       const int kkey = (b * g.H + h) * g.NP + p;
       if (kkey != cur_key) {
         // the previous tile's MMA must be done before its keys are replaced
-        if (it > 0 && !tc::mbar_wait(&empty_q[(it - 1) & 1], ((it - 1) >> 1) & 1)) { s_fail = 1; break; }
+        if (it > 0 && !tc::mbar_wait(&empty_q[(it - 1) % kStages], ((it - 1) / kStages) & 1)) { s_fail = 1; break; }
         const int64_t tok0 = int64_t(p) * NK;
         const T* kb = kbase + b * g.k_sb + int64_t(h) * g.k_sh;
         for (int r = ptid / vpr; r < NK; r += row_step) {
@@ -182,9 +185,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
           dst = rowid * g.W0 + (req - rowid * g.NF) * g.br;
         }
         if (ptid < g.RT) s_qoff[s][ptid] = off;
-        s_dst[it & 3][ptid] = dst;
-        if (ptid == 0) s_fam[it & 3] = p;
-        tc::mbar_arrive(&meta_full[it & 3]);
+        s_dst[it & 7][ptid] = dst;
+        if (ptid == 0) s_fam[it & 7] = p;
+        tc::mbar_arrive(&meta_full[it & 7]);
       }
       tc::named_sync(1, kLoadWarps * 32);
       const uint32_t qdst = qs_addr + s * q_stage_bytes + (c >> 3) * 128 * 128;
@@ -195,18 +198,20 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
         if (off >= 0 && c * 8 < g.D) cp_async16(dst, qbase + off + int64_t(gh) * g.q_sh + c * 8);
         else st_zero16(dst);
       }
-      cp_async_wait_all();
+      // completion is tracked by the barrier; the next stage starts immediately
       tc::fence_async_smem();
-      tc::mbar_arrive(&full_q[s]);
+      tc::cp_async_arrive(&full_q[s]);
     }
+    cp_async_wait_all();
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issue ----------------
     if (lane == 0) {
       for (int it = 0; it < ntiles; ++it) {
-        const int s = it & 1, a = nacc == 2 ? (it & 1) : 0;
+        const int s = it % kStages, a = nacc == 2 ? (it & 1) : 0;
         const int ra = nacc == 2 ? (it >> 1) : it;
-        if (!tc::mbar_wait(&full_q[s], (it >> 1) & 1)) { s_fail = 1; break; }
+        if (!tc::mbar_wait(&full_q[s], (it / kStages) & 1)) { s_fail = 1; break; }
         if (!tc::mbar_wait(&empty_acc[a], (ra & 1) ^ 1)) { s_fail = 1; break; }
+        tc::fence_async_smem();
         tc::fence_after_sync();
         const uint32_t acc = tmem + a * NK;
         const uint32_t qa = qs_addr + s * q_stage_bytes;
@@ -240,9 +245,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
       const bool got = tc::mbar_wait(&full_acc[a], ra & 1);
       if (!got) s_fail = 1;
       tc::fence_after_sync();
-      if (!tc::mbar_wait(&meta_full[it & 3], (it >> 2) & 1)) s_fail = 1;
-      const int p = s_fam[it & 3];
-      const int dst = r < g.RT ? s_dst[it & 3][r] : -1;
+      if (!tc::mbar_wait(&meta_full[it & 7], (it >> 3) & 1)) s_fail = 1;
+      const int p = s_fam[it & 7];
+      const int dst = r < g.RT ? s_dst[it & 7][r] : -1;
       (void)tile;
       const uint32_t acc = tmem + lane_base + a * NK;
       for (int jj = 0; jj < jn; ++jj) {
@@ -366,7 +371,7 @@ int grouped_leaf(const GroupArgs& g, int dtype, cudaStream_t stream) {
   PISA_CHECK_LAUNCH();
 
   const int chunks = g.Dp / 64;
-  const size_t smem = size_t(chunks) * 128 * (2 * 128 + g.br * g.C) + 1024;
+  const size_t smem = size_t(chunks) * 128 * (kStages * 128 + g.br * g.C) + 1024;
   auto kernel = dtype == PISA_BF16 ? leaf_tc_kernel<__nv_bfloat16> : leaf_tc_kernel<__half>;
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return fail_cuda(e, "leaf smem attribute");

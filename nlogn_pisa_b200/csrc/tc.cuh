@@ -100,6 +100,12 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(mbar)) : "memory");
 }
 
+// Arrive on `mbar` once every cp.async issued so far by this thread has
+// landed (the arrival counts toward the barrier's initial count).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* mbar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(smem_u32(mbar)) : "memory");
+}
+
 // Barrier among `count` threads of the CTA on hardware barrier `id` (1..15).
 __device__ __forceinline__ void named_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(count) : "memory");
