@@ -121,8 +121,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
   // two K/V buffers, each [qch][C keys][128 B] of keys then [vch][C keys][128 B]
   // of values (value dims contiguous); a block change switches buffers
   const int kv_bytes = (qch + vch) * a.C * 128;
-  uint8_t* KV = smem + kStages * q_stage_bytes;
-  __shared__ uint64_t q_full[kStages], q_empty[kStages], s_full[2], p_full[2], o_full[2], acc_empty[2];
+  uint8_t* KV = smem + a.nstages * q_stage_bytes;
+  __shared__ uint64_t q_full[kStages], q_empty[kStages], s_full[2], p_full[2], o_full[2], o_empty[2];
   __shared__ uint32_t tmem_slot;
   __shared__ int64_t s_qoff[kStages][128];
   __shared__ int s_kvb[kStages];
@@ -140,10 +140,11 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
   const int last = min(first + per, total);
   if (first >= last) return;
   const int ntiles = last - first;
-  const int nacc = a.nacc;
+  const int nacc = a.nacc;                    // S/P and O buffers: 2 (double) or 1
+  const int nst = a.nstages;                  // query stages: 3 or 2
 
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < nst; ++i) {
       tc::mbar_init(&q_full[i], kLoadWarps * 32);
       tc::mbar_init(&q_empty[i], 1);
     }
@@ -151,7 +152,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
       tc::mbar_init(&s_full[i], 1);
       tc::mbar_init(&p_full[i], 128);
       tc::mbar_init(&o_full[i], 1);
-      tc::mbar_init(&acc_empty[i], 128);
+      tc::mbar_init(&o_empty[i], 128);
     }
     for (int i = 0; i < 8; ++i) tc::mbar_init(&meta_full[i], kLoadWarps * 32);
     s_fail = 0;
@@ -181,7 +182,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
     int owner_next = a.tile_owner[first];
     int req_next = ptid < a.RT ? a.tile_req[int64_t(first) * a.RT + ptid] : -1;
     for (int it = 0; it < ntiles; ++it) {
-      const int tile = first + it, s = it % kStages, rnd = it / kStages;
+      const int tile = first + it, s = it % nst, rnd = it / nst;
       const int owner = owner_next, req = req_next;
       if (it + 1 < ntiles) {
         owner_next = a.tile_owner[tile + 1];
@@ -260,18 +261,19 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
       const uint32_t idesc_s = tc::idesc_f16(128, a.C, a.bf16);
       const uint32_t idesc_o = tc::idesc_f16(128, a.Dv, a.bf16, 1);
       int kv_even = 0, kv_odd = 0;  // K/V buffer of the last even / odd tile
-      // S = Q K^T of tile `it` into its buffer
+      // S = Q K^T of tile `it` into its S/P buffer; only the query stage is
+      // awaited: the buffer's previous P was consumed by a P.V issued earlier
+      // from this thread, and tensor-core operations run in issue order.
       auto issue_s = [&](int it) -> bool {
-        const int s = it % kStages, ab = acc_of(it);
-        if (!tc::mbar_wait(&q_full[s], (it / kStages) & 1)) return false;
-        if (!tc::mbar_wait(&acc_empty[ab], (round_of(it) & 1) ^ 1)) return false;
+        const int s = it % nst, ab = acc_of(it);
+        if (!tc::mbar_wait(&q_full[s], (it / nst) & 1)) return false;
         tc::fence_async_smem();
         tc::fence_after_sync();
         const int kvb = s_kvb[s];
         if (it & 1) kv_odd = kvb; else kv_even = kvb;
         const uint32_t ks_addr = kv_addr + kvb * kv_bytes;
         const uint32_t qa = qs_addr + s * q_stage_bytes;
-        const uint32_t sacc = tmem + ab * a.acc_cols;
+        const uint32_t sacc = tmem + ab * a.sp_cols;
         for (int ks = 0; ks < a.Dp / 16; ++ks) {
           const int ch = ks >> 2, off = (ks & 3) * 32;
           tc::mma_f16(sacc, tc::desc_sw128(qa + ch * 128 * 128 + off),
@@ -281,22 +283,24 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
         tc::mma_commit(&q_empty[s]);
         return true;
       };
-      // O = P V of tile `pt` once its P is in TMEM
+      // O = P V of tile `pt` once its P is in TMEM and its O buffer was read out
       auto issue_o = [&](int pt) -> bool {
         const int ab = acc_of(pt);
         if (!tc::mbar_wait(&p_full[ab], round_of(pt) & 1)) return false;
+        if (!tc::mbar_wait(&o_empty[ab], (round_of(pt) & 1) ^ 1)) return false;
         tc::fence_after_sync();
-        const uint32_t base = tmem + ab * a.acc_cols;
+        const uint32_t sp = tmem + ab * a.sp_cols;
+        const uint32_t ob = tmem + nacc * a.sp_cols + ab * a.o_cols;
         const uint32_t vs_addr = kv_addr + ((pt & 1) ? kv_odd : kv_even) * kv_bytes + qch * a.C * 128;
         for (int ks = 0; ks < a.C / 16; ++ks) {
           const uint64_t vd = tc::desc_make(vs_addr + ks * 16 * 128, uint32_t(a.C) * 128, 1024, 2);
-          tc::mma_f16_ts(base + a.o_col, base + a.p_col + ks * 8, vd, idesc_o, ks > 0);
+          tc::mma_f16_ts(ob, sp + a.C + ks * 8, vd, idesc_o, ks > 0);
         }
         tc::mma_commit(&o_full[ab]);
         return true;
       };
-      // Two buffers: S(i) is issued before O(i-1) so the tensor core works on
-      // tile i while the epilogue computes P(i-1).  One buffer: strictly in order.
+      // Two buffers: S(i) before O(i-1), so Q K^T of the next tile overlaps the
+      // softmax of the current one.  One buffer: O(i-1) first (S(i) overwrites P(i-1)).
       for (int it = 0; it <= ntiles; ++it) {
         bool ok = true;
         if (nacc == 2) {
@@ -330,7 +334,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
       const int req = r < a.RT ? s_req[it & 7][r] : -1;
       const int nvalid = r < a.RT ? s_nv[it & 7][r] : 0;
       (void)tile;
-      const uint32_t base = tmem + lane_base + ab * a.acc_cols;
+      const uint32_t base = tmem + lane_base + ab * a.sp_cols;                 // S, then P at +C
+      const uint32_t obase = tmem + lane_base + nacc * a.sp_cols + ab * a.o_cols;
       float mx = -INFINITY;
       float l = 0.f;
       if (a.C == 64) {
@@ -357,8 +362,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
         uint32_t w0[16], w1[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) { w0[i] = w[i]; w1[i] = w[16 + i]; }
-        tc::tmem_st16(base + a.p_col, w0);
-        tc::tmem_st16(base + a.p_col + 16, w1);
+        tc::tmem_st16(base + a.C, w0);
+        tc::tmem_st16(base + a.C + 16, w1);
       } else {
       for_columns(base, a.C, [&](int c, float x) {
         if (c < nvalid) mx = fmaxf(mx, x);
@@ -376,7 +381,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
             l += p0 + p1;
             w[i] = pack2<T>(p0, p1);
           }
-          tc::tmem_st16(base + a.p_col + c0 / 2, w);
+          tc::tmem_st16(base + a.C + c0 / 2, w);
         } else {
           float v[16];
           tc::tmem_ld16(base + c0, v);
@@ -388,7 +393,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
             l += p0 + p1;
             w[i] = pack2<T>(p0, p1);
           }
-          tc::tmem_st8(base + a.p_col + c0 / 2, w);
+          tc::tmem_st8(base + a.C + c0 / 2, w);
         }
       }
       }
@@ -402,7 +407,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
       int c0 = 0;
       for (; c0 + 64 <= a.Dv; c0 += 64) {
         float v[64];
-        tc::tmem_ld64(base + a.o_col + c0, v);
+        tc::tmem_ld64(obase + c0, v);
         if (req >= 0) {
           uint4* dst = reinterpret_cast<uint4*>(part_o + pi * a.Dv + c0);
 #pragma unroll
@@ -417,7 +422,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
       for (; c0 < a.Dv; c0 += 32) {
         if (a.Dv - c0 >= 32) {
           float v[32];
-          tc::tmem_ld32(base + a.o_col + c0, v);
+          tc::tmem_ld32(obase + c0, v);
           if (req >= 0) {
             uint32_t w[16];
 #pragma unroll
@@ -428,7 +433,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
           }
         } else {
           float v[16];
-          tc::tmem_ld16(base + a.o_col + c0, v);
+          tc::tmem_ld16(obase + c0, v);
           if (req >= 0) {
             uint32_t w[8];
 #pragma unroll
@@ -441,7 +446,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
       }
       if (req >= 0) __stcs(reinterpret_cast<float2*>(a.part_ml) + pi, make_float2(mx * a.scale, l));
       tc::fence_before_sync();
-      tc::mbar_arrive(&acc_empty[ab]);
+      tc::mbar_arrive(&o_empty[ab]);
       if (!got || !got2) break;
     }
   }
@@ -596,7 +601,7 @@ __global__ void __launch_bounds__(128) attn_combine16_kernel(const AttnTcArgs a)
 template <typename T>
 int attn_tc_typed(AttnTcArgs a, cudaStream_t stream) {
   const int qch = a.Dp / 64, vch = a.Dvp / 64;
-  const size_t smem = size_t(kStages) * 128 * 128 * qch + size_t(2) * a.C * 128 * (qch + vch) + 1024;
+  const size_t smem = size_t(a.nstages) * 128 * 128 * qch + size_t(2) * a.C * 128 * (qch + vch) + 1024;
   cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return fail_cuda(e, "attention smem attribute");
   for (int t0 = 0; t0 < a.T; t0 += a.chunk) {

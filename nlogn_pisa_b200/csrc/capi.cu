@@ -405,7 +405,7 @@ namespace pisa {
 struct AttnPlan {
   bool tc = false;
   int64_t TW = 4096, chunk = 0, NB = 0, RT = 0, num_buckets = 0, capacity = 0;
-  int64_t p_col = 0, o_col = 0, tmem_cols = 0, acc_cols = 0, nacc = 1;
+  int64_t sp_cols = 0, o_cols = 0, tmem_cols = 0, nacc = 1, nstages = 2;
   int64_t counts_off = 0, cursors_off = 0, offsets_off = 0, misc_off = 0, owner_off = 0,
           req_off = 0, po_off = 0, pml_off = 0, total = 0;
 };
@@ -414,15 +414,17 @@ static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t 
                           int64_t N, int64_t S, int64_t C, int dtype) {
   AttnPlan p;
   const int64_t G = Hq / H;
-  // one TMEM buffer = S (C columns) | P (C/2 packed) | O (Dv); two when they fit
-  p.p_col = C;
-  p.o_col = (C + C / 2 + 31) / 32 * 32;
-  const int64_t cols = p.o_col + Dv;
-  p.acc_cols = cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
-  p.nacc = 2 * p.acc_cols <= 512 ? 2 : 1;
-  p.tmem_cols = p.nacc * p.acc_cols;
+  // TMEM: S/P buffers (C columns of S, then C/2 packed columns of P) and O
+  // buffers (Dv columns), two of each when they fit in 512 columns
+  p.sp_cols = (C + C / 2 + 31) / 32 * 32;
+  p.o_cols = (Dv + 31) / 32 * 32;
+  p.nacc = 2 * (p.sp_cols + p.o_cols) <= 512 ? 2 : 1;
+  const int64_t cols = p.nacc * (p.sp_cols + p.o_cols);
+  p.tmem_cols = cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
   const int64_t Dp = D <= 64 ? 64 : D <= 128 ? 128 : 256, Dvp = Dv <= 64 ? 64 : Dv <= 128 ? 128 : 256;
-  const int64_t smem = 3 * 128 * 2 * Dp + 2 * C * 2 * (Dp + Dvp) + 1024 + 8192;
+  const int64_t kv_smem = 2 * C * 2 * (Dp + Dvp) + 1024 + 12288;
+  p.nstages = 3 * 128 * 2 * Dp + kv_smem <= 227 * 1024 ? 3 : 2;
+  const int64_t smem = p.nstages * 128 * 2 * Dp + kv_smem;
   p.tc = (dtype == PISA_BF16 || dtype == PISA_F16) && is_pow2(G) && G <= 32 && D % 16 == 0 &&
          Dv % 16 == 0 && D <= 256 && Dv <= 256 && is_pow2(C) && C >= 16 && C <= 256 &&
          cols <= 512 && smem <= 227 * 1024 && S > 0 && S <= 64 && B * Tq * H * S >= 4096;
@@ -505,8 +507,8 @@ int pisa_sparse_attn_fwd(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh
     a.part_o = ws + plan.po_off;
     a.part_ml = reinterpret_cast<float*>(ws + plan.pml_off);
     a.tiles_per_cta = 8;
-    a.tmem_cols = int(plan.tmem_cols); a.p_col = int(plan.p_col); a.o_col = int(plan.o_col);
-    a.acc_cols = int(plan.acc_cols); a.nacc = int(plan.nacc); a.num_sms = num_sms();
+    a.tmem_cols = int(plan.tmem_cols); a.sp_cols = int(plan.sp_cols); a.o_cols = int(plan.o_cols);
+    a.nacc = int(plan.nacc); a.nstages = int(plan.nstages); a.num_sms = num_sms();
     a.out = out; a.lse = lse;
     return attn_fwd_tc(a, dtype, static_cast<cudaStream_t>(stream));
   }

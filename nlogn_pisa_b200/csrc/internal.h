@@ -164,7 +164,7 @@ struct AttnTcArgs {
   int32_t* tile_req;
   int32_t* total_tiles;
   int64_t capacity;
-  int tiles_per_cta, tmem_cols, p_col, o_col, acc_cols, nacc, num_sms;
+  int tiles_per_cta, tmem_cols, sp_cols, o_cols, nacc, nstages, num_sms;
   void* part_o;
   float* part_ml;
   void* out;
