@@ -87,7 +87,20 @@ __global__ void attn_scatter_kernel(const AttnTcArgs a) {
   const int pos = atomicAdd(a.cursors + bucket, 1);
   const int64_t tile = a.offsets[bucket] + pos / a.RT;
   a.tile_req[tile * a.RT + pos % a.RT] = int32_t(lr);
+  a.tile_pos[lr] = int32_t(tile * a.RT + pos % a.RT);
   if (pos % a.RT == 0) a.tile_owner[tile] = int32_t(bucket);
+}
+
+// 32-byte streaming store / load (partials are written once and read once)
+__device__ __forceinline__ void st_cs32(void* p, const uint32_t (&w)[8]) {
+  asm volatile("st.global.cs.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+               :: "l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]),
+                  "r"(w[7]) : "memory");
+}
+__device__ __forceinline__ void ld_cs32(const void* p, uint32_t (&w)[8]) {
+  asm volatile("ld.global.cs.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]),
+                 "=r"(w[7]) : "l"(p));
 }
 
 template <typename T>
@@ -402,49 +415,24 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
       const bool got2 = tc::mbar_wait(&o_full[ab], rnd & 1);
       if (!got2) s_fail = 1;
       tc::fence_after_sync();
+      // block-local partial (m, l, O / l) in the tile-major layout
+      // part_o[tile][column group of 16][row][16]: one warp store = 1 KiB contiguous
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      const int64_t pi = int64_t(req) * a.G + g;
-      int c0 = 0;
-      for (; c0 + 64 <= a.Dv; c0 += 64) {
-        float v[64];
-        tc::tmem_ld64(obase + c0, v);
-        if (req >= 0) {
-          uint4* dst = reinterpret_cast<uint4*>(part_o + pi * a.Dv + c0);
+      const int ncg = a.Dv / 16;
+      T* pbase = part_o + (int64_t(tile) * ncg * 128 + row) * 16;
+      for (int c0 = 0; c0 < a.Dv; c0 += 32) {
+        float v[32];
+        tc::tmem_ld32(obase + c0, v);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            __stcs(dst + i, make_uint4(pack2<T>(v[8 * i] * inv, v[8 * i + 1] * inv),
-                                       pack2<T>(v[8 * i + 2] * inv, v[8 * i + 3] * inv),
-                                       pack2<T>(v[8 * i + 4] * inv, v[8 * i + 5] * inv),
-                                       pack2<T>(v[8 * i + 6] * inv, v[8 * i + 7] * inv)));
-          }
+        for (int hgrp = 0; hgrp < 2; ++hgrp) {
+          uint32_t w[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) w[i] = pack2<T>(v[16 * hgrp + 2 * i] * inv, v[16 * hgrp + 2 * i + 1] * inv);
+          st_cs32(pbase + int64_t(c0 / 16 + hgrp) * 128 * 16, w);
         }
       }
-      for (; c0 < a.Dv; c0 += 32) {
-        if (a.Dv - c0 >= 32) {
-          float v[32];
-          tc::tmem_ld32(obase + c0, v);
-          if (req >= 0) {
-            uint32_t w[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) w[i] = pack2<T>(v[2 * i] * inv, v[2 * i + 1] * inv);
-            uint4* dst = reinterpret_cast<uint4*>(part_o + pi * a.Dv + c0);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) __stcs(dst + i, make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]));
-          }
-        } else {
-          float v[16];
-          tc::tmem_ld16(obase + c0, v);
-          if (req >= 0) {
-            uint32_t w[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) w[i] = pack2<T>(v[2 * i] * inv, v[2 * i + 1] * inv);
-            uint4* dst = reinterpret_cast<uint4*>(part_o + pi * a.Dv + c0);
-            __stcs(dst, make_uint4(w[0], w[1], w[2], w[3]));
-            __stcs(dst + 1, make_uint4(w[4], w[5], w[6], w[7]));
-          }
-        }
-      }
-      if (req >= 0) __stcs(reinterpret_cast<float2*>(a.part_ml) + pi, make_float2(mx * a.scale, l));
+      __stcs(reinterpret_cast<float2*>(a.part_ml) + int64_t(tile) * 128 + row,
+             make_float2(req >= 0 ? mx * a.scale : -INFINITY, l));
       tc::fence_before_sync();
       tc::mbar_arrive(&o_empty[ab]);
       if (!got || !got2) break;
@@ -457,76 +445,12 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
   if (warp == 0) tc::tmem_free(tmem, a.tmem_cols);
 }
 
-// Merge the S block partials of one query head (one warp per head row):
-// lane s reads slot s's (m, l), the warp forms the softmax weights of the
-// blocks, then every lane accumulates its value columns over the slots with
-// the loads of four slots in flight.
-template <typename T, int DPL>
-__global__ void __launch_bounds__(128) attn_combine_kernel(const AttnTcArgs a) {
-  const int64_t idx = blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (idx >= int64_t(a.B) * a.tlen * a.Hq) return;
-  const int hq = int(idx % a.Hq);
-  const int tl = int((idx / a.Hq) % a.tlen);
-  const int b = int(idx / (int64_t(a.Hq) * a.tlen));
-  const int h = hq / a.G, g = hq % a.G;
-  const int t = a.t0 + tl;
-  const int64_t slot0 = ((int64_t(b) * a.tlen + tl) * a.H + h) * a.S;   // chunk-local request of slot 0
-  const T* part_o = static_cast<const T*>(a.part_o);
-  const float2* part_ml = reinterpret_cast<const float2*>(a.part_ml);
-  // per-lane slots: s = lane, lane + 32
-  float m_s[2] = {-INFINITY, -INFINITY}, l_s[2] = {0.f, 0.f};
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int s = lane + 32 * k;
-    if (s < a.S && visible_block(a, b, t, h, s) >= 0) {
-      const float2 ml = __ldcs(part_ml + (slot0 + s) * a.G + g);
-      if (ml.y > 0.f) { m_s[k] = ml.x; l_s[k] = ml.y; }
-    }
-  }
-  const float M = warp_max(fmaxf(m_s[0], m_s[1]));
-  float w_s[2];
-#pragma unroll
-  for (int k = 0; k < 2; ++k) w_s[k] = (M == -INFINITY || m_s[k] == -INFINITY) ? 0.f : l_s[k] * expf(m_s[k] - M);
-  const float L = warp_sum(w_s[0] + w_s[1]);
-  float acc[DPL];
-#pragma unroll
-  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-  const int dbase = lane * DPL;
-  for (int s0 = 0; s0 < a.S; s0 += 4) {
-    float w[4];
-    float x[4][DPL];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int s = s0 + u;
-      const float ws = __shfl_sync(kFull, s < 32 ? w_s[0] : w_s[1], s & 31);
-      w[u] = s < a.S ? ws : 0.f;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) x[u][i] = 0.f;
-      if (w[u] > 0.f) {
-        const T* src = part_o + ((slot0 + s) * a.G + g) * a.Dv + dbase;
-#pragma unroll
-        for (int i = 0; i < DPL; ++i)
-          if (dbase + i < a.Dv) x[u][i] = to_f32<T>(__ldcs(src + i));
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u)
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) acc[i] = fmaf(w[u], x[u][i], acc[i]);
-  }
-  T* out = static_cast<T*>(a.out) + ((int64_t(b) * a.T + t) * a.Hq + hq) * a.Dv;
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-  for (int i = 0; i < DPL; ++i)
-    if (dbase + i < a.Dv) out[dbase + i] = from_f32<T>(acc[i] * inv);
-  if (lane == 0 && a.lse) a.lse[(int64_t(b) * a.T + t) * a.Hq + hq] = L > 0.f ? M + logf(L) : -INFINITY;
-}
-
-// Same merge with 16-byte loads: the two half-warps take alternate slots
-// and each lane covers VPL (= Dv/16) value columns; 8 slots in flight.
-template <typename T, int VPL>
-__global__ void __launch_bounds__(128) attn_combine16_kernel(const AttnTcArgs a) {
+// Merge the S block partials of one query head (one warp per head row).
+// Partials live in the tile-major layout; tile_pos maps each request to its
+// (tile, row).  Lane = (slot offset, column group of 16 values): one 32-byte
+// load per lane per slot, 32 / NCG slots per warp instruction.
+template <typename T, int NCG>
+__global__ void __launch_bounds__(128) attn_combine_tiles_kernel(const AttnTcArgs a) {
   const int64_t idx = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (idx >= int64_t(a.B) * a.tlen * a.Hq) return;
@@ -538,12 +462,17 @@ __global__ void __launch_bounds__(128) attn_combine16_kernel(const AttnTcArgs a)
   const int64_t slot0 = ((int64_t(b) * a.tlen + tl) * a.H + h) * a.S;
   const T* part_o = static_cast<const T*>(a.part_o);
   const float2* part_ml = reinterpret_cast<const float2*>(a.part_ml);
+  // lane k-th slot: s = lane + 32k; its partial row index tile*128 + row
   float m_s[2] = {-INFINITY, -INFINITY}, l_s[2] = {0.f, 0.f};
+  int prow[2] = {-1, -1};
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     const int sl = lane + 32 * k;
     if (sl < a.S && visible_block(a, b, t, h, sl) >= 0) {
-      const float2 ml = __ldcs(part_ml + (slot0 + sl) * a.G + g);
+      const int pos = a.tile_pos[slot0 + sl];
+      const int tile = pos / a.RT, r = pos - tile * a.RT;
+      prow[k] = tile * 128 + r * a.G + g;
+      const float2 ml = __ldcs(part_ml + prow[k]);
       if (ml.y > 0.f) { m_s[k] = ml.x; l_s[k] = ml.y; }
     }
   }
@@ -552,48 +481,49 @@ __global__ void __launch_bounds__(128) attn_combine16_kernel(const AttnTcArgs a)
 #pragma unroll
   for (int k = 0; k < 2; ++k) w_s[k] = (M == -INFINITY || m_s[k] == -INFINITY) ? 0.f : l_s[k] * expf(m_s[k] - M);
   const float L = warp_sum(w_s[0] + w_s[1]);
-  const int half = lane >> 4, hl = lane & 15;
-  float acc[VPL];
+  constexpr int SPI = 32 / NCG;       // slots per warp instruction
+  const int cg = lane % NCG, sub = lane / NCG;
+  float acc[16];
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) acc[i] = 0.f;
-  constexpr int kBytes = VPL * int(sizeof(T));   // 8, 16 or 32 per lane and slot
-  for (int s0 = 0; s0 < a.S; s0 += 8) {
-    float w[4];
-    uint4 raw[4][(kBytes + 15) / 16];
+  for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+  for (int s0 = 0; s0 < a.S; s0 += 2 * SPI) {
+    float w[2];
+    uint32_t raw[2][8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int sl = s0 + 2 * u + half;
-      const float w0 = __shfl_sync(kFull, w_s[0], sl & 31);
-      const float w1 = __shfl_sync(kFull, w_s[1], sl & 31);
+    for (int u = 0; u < 2; ++u) {
+      const int sl = s0 + u * SPI + sub;
+      const float w0 = __shfl_sync(kFull, w_s[0], sl & 31), w1 = __shfl_sync(kFull, w_s[1], sl & 31);
+      const int r0 = __shfl_sync(kFull, prow[0], sl & 31), r1 = __shfl_sync(kFull, prow[1], sl & 31);
       w[u] = sl < a.S ? (sl < 32 ? w0 : w1) : 0.f;
-      const T* src = part_o + ((slot0 + sl) * a.G + g) * a.Dv + hl * VPL;
+      const int pr = sl < 32 ? r0 : r1;
+      if (w[u] > 0.f) {
+        const int tile = pr >> 7, row = pr & 127;
+        ld_cs32(part_o + ((int64_t(tile) * NCG + cg) * 128 + row) * 16, raw[u]);
+      } else {
 #pragma unroll
-      for (int c = 0; c < (kBytes + 15) / 16; ++c) {
-        if (w[u] > 0.f) {
-          if constexpr (kBytes >= 16) raw[u][c] = __ldcs(reinterpret_cast<const uint4*>(src) + c);
-          else {
-            const uint2 r2 = __ldcs(reinterpret_cast<const uint2*>(src));
-            raw[u][c] = make_uint4(r2.x, r2.y, 0u, 0u);
-          }
-        } else {
-          raw[u][c] = make_uint4(0u, 0u, 0u, 0u);
-        }
+        for (int i = 0; i < 8; ++i) raw[u][i] = 0u;
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 2; ++u) {
       const T* e = reinterpret_cast<const T*>(raw[u]);
 #pragma unroll
-      for (int i = 0; i < VPL; ++i) acc[i] = fmaf(w[u], to_f32<T>(e[i]), acc[i]);
+      for (int i = 0; i < 16; ++i) acc[i] = fmaf(w[u], to_f32<T>(e[i]), acc[i]);
     }
   }
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) acc[i] += __shfl_xor_sync(kFull, acc[i], 16);
+  for (int o = NCG; o < 32; o <<= 1)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] += __shfl_xor_sync(kFull, acc[i], o);
   T* out = static_cast<T*>(a.out) + ((int64_t(b) * a.T + t) * a.Hq + hq) * a.Dv;
   const float inv = L > 0.f ? 1.f / L : 0.f;
-  if (half == 0) {
+  if (sub == 0) {
+    uint32_t wv[8];
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) out[hl * VPL + i] = from_f32<T>(acc[i] * inv);
+    for (int i = 0; i < 8; ++i) wv[i] = pack2<T>(acc[2 * i] * inv, acc[2 * i + 1] * inv);
+    uint4* dst = reinterpret_cast<uint4*>(out + cg * 16);
+    dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
   }
   if (lane == 0 && a.lse) a.lse[(int64_t(b) * a.T + t) * a.Hq + hq] = L > 0.f ? M + logf(L) : -INFINITY;
 }
@@ -625,13 +555,13 @@ int attn_tc_typed(AttnTcArgs a, cudaStream_t stream) {
     attn_tc_kernel<T><<<unsigned(a.num_sms), kPipeThreads, smem, stream>>>(a);
     PISA_CHECK_LAUNCH();
     const unsigned cgrid = unsigned((int64_t(a.B) * a.tlen * a.Hq + 3) / 4);
-    if (a.Dv == 64) attn_combine16_kernel<T, 4><<<cgrid, 128, 0, stream>>>(a);
-    else if (a.Dv == 128) attn_combine16_kernel<T, 8><<<cgrid, 128, 0, stream>>>(a);
-    else if (a.Dv == 256) attn_combine16_kernel<T, 16><<<cgrid, 128, 0, stream>>>(a);
-    else if (a.Dv <= 32) attn_combine_kernel<T, 1><<<cgrid, 128, 0, stream>>>(a);
-    else if (a.Dv <= 64) attn_combine_kernel<T, 2><<<cgrid, 128, 0, stream>>>(a);
-    else if (a.Dv <= 128) attn_combine_kernel<T, 4><<<cgrid, 128, 0, stream>>>(a);
-    else attn_combine_kernel<T, 8><<<cgrid, 128, 0, stream>>>(a);
+    switch (a.Dv / 16) {
+      case 1: attn_combine_tiles_kernel<T, 1><<<cgrid, 128, 0, stream>>>(a); break;
+      case 2: attn_combine_tiles_kernel<T, 2><<<cgrid, 128, 0, stream>>>(a); break;
+      case 4: attn_combine_tiles_kernel<T, 4><<<cgrid, 128, 0, stream>>>(a); break;
+      case 8: attn_combine_tiles_kernel<T, 8><<<cgrid, 128, 0, stream>>>(a); break;
+      default: attn_combine_tiles_kernel<T, 16><<<cgrid, 128, 0, stream>>>(a); break;
+    }
     PISA_CHECK_LAUNCH();
   }
   return PISA_OK;

@@ -407,7 +407,7 @@ struct AttnPlan {
   int64_t TW = 4096, chunk = 0, NB = 0, RT = 0, num_buckets = 0, capacity = 0;
   int64_t sp_cols = 0, o_cols = 0, tmem_cols = 0, nacc = 1, nstages = 2;
   int64_t counts_off = 0, cursors_off = 0, offsets_off = 0, misc_off = 0, owner_off = 0,
-          req_off = 0, po_off = 0, pml_off = 0, total = 0;
+          req_off = 0, pos_off = 0, po_off = 0, pml_off = 0, total = 0;
 };
 
 static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t Dv,
@@ -426,10 +426,10 @@ static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t 
   p.nstages = 3 * 128 * 2 * Dp + kv_smem <= 227 * 1024 ? 3 : 2;
   const int64_t smem = p.nstages * 128 * 2 * Dp + kv_smem;
   p.tc = (dtype == PISA_BF16 || dtype == PISA_F16) && is_pow2(G) && G <= 32 && D % 16 == 0 &&
-         Dv % 16 == 0 && D <= 256 && Dv <= 256 && is_pow2(C) && C >= 16 && C <= 256 &&
+         Dv % 32 == 0 && D <= 256 && Dv <= 256 && is_pow2(C) && C >= 16 && C <= 256 &&
          cols <= 512 && smem <= 227 * 1024 && S > 0 && S <= 64 && B * Tq * H * S >= 4096;
   if (!p.tc) return p;
-  const int64_t per_token = H * S * G * (Dv * elem_size(dtype) + 8);
+  const int64_t per_token = H * S * G * (Dv * elem_size(dtype) + 8) * 9 / 8;
   const int64_t fit = ((int64_t(1) << 31) / per_token) / p.TW * p.TW;
   p.chunk = std::min<int64_t>(Tq, std::max<int64_t>(p.TW, fit));
   p.NB = (N + C - 1) / C;
@@ -446,8 +446,9 @@ static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t 
   p.misc_off = off; off += 256;
   p.owner_off = off; off += align_up(p.capacity * 4, 256);
   p.req_off = off; off += align_up(p.capacity * p.RT * 4, 256);
-  p.po_off = off; off += align_up(reqs * G * Dv * elem_size(dtype), 256);
-  p.pml_off = off; off += align_up(reqs * G * 8, 256);
+  p.pos_off = off; off += align_up(reqs * 4, 256);
+  p.po_off = off; off += align_up(p.capacity * 128 * Dv * elem_size(dtype), 256);
+  p.pml_off = off; off += align_up(p.capacity * 128 * 8, 256);
   p.total = off;
   return p;
 }
@@ -504,6 +505,7 @@ int pisa_sparse_attn_fwd(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh
     a.status = reinterpret_cast<int*>(ws + plan.misc_off + 4);
     a.tile_owner = reinterpret_cast<int32_t*>(ws + plan.owner_off);
     a.tile_req = reinterpret_cast<int32_t*>(ws + plan.req_off);
+    a.tile_pos = reinterpret_cast<int32_t*>(ws + plan.pos_off);
     a.part_o = ws + plan.po_off;
     a.part_ml = reinterpret_cast<float*>(ws + plan.pml_off);
     a.tiles_per_cta = 8;

@@ -163,6 +163,7 @@ struct AttnTcArgs {
   int32_t* tile_owner;
   int32_t* tile_req;
   int32_t* total_tiles;
+  int32_t* tile_pos;  // chunk-local request -> tile * RT + slot
   int64_t capacity;
   int tiles_per_cta, tmem_cols, sp_cols, o_cols, nacc, nstages, num_sms;
   void* part_o;
