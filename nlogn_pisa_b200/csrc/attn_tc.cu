@@ -122,11 +122,11 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 //   warp 12          MMA issue: S(i+1) = Q K^T is issued before O(i) = P V
 // mbarriers per stage/buffer: q_full/q_empty (query stages), s_full, p_full,
 // o_full, acc_empty (TMEM buffer of S, P and O).  All waits are bounded.
-constexpr int kEpiWarps = 8, kLoadWarps = 4, kMmaWarp = 12, kStages = 3;
+constexpr int kEpiWarps = 8, kLoadWarps = 1, kMmaWarp = 9, kStages = 3;
 constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
 
 template <typename T>
-__global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcArgs a) {
+__global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_constant__ AttnTcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int qch = a.Dp / 64, vch = a.Dvp / 64;
@@ -137,7 +137,6 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
   uint8_t* KV = smem + a.nstages * q_stage_bytes;
   __shared__ uint64_t q_full[kStages], q_empty[kStages], s_full[2], p_full[2], o_full[2], o_empty[2];
   __shared__ uint32_t tmem_slot;
-  __shared__ int64_t s_qoff[kStages][128];
   __shared__ int s_kvb[kStages];
   // per-tile metadata ring for the epilogue (8 slots): the producer runs at
   // most kStages tiles ahead of the MMAs and they at most two ahead of the
@@ -158,7 +157,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
 
   if (tid == 0) {
     for (int i = 0; i < nst; ++i) {
-      tc::mbar_init(&q_full[i], kLoadWarps * 32);
+      tc::mbar_init(&q_full[i], 1);
       tc::mbar_init(&q_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -167,7 +166,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
       tc::mbar_init(&o_full[i], 1);
       tc::mbar_init(&o_empty[i], 128);
     }
-    for (int i = 0; i < 8; ++i) tc::mbar_init(&meta_full[i], kLoadWarps * 32);
+    for (int i = 0; i < 8; ++i) tc::mbar_init(&meta_full[i], 1);
     s_fail = 0;
     tc::fence_barrier_init();
   }
@@ -183,29 +182,41 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
   auto round_of = [&](int it) { return nacc == 2 ? (it >> 1) : it; };
 
   if (warp >= kEpiWarps && warp < kMmaWarp) {
-    // ---------------- producers ----------------
-    const int ptid = tid - kEpiWarps * 32;
-    const int vpr = a.Dp / 8, vvpr = a.Dvp / 8;
-    const T* qbase = static_cast<const T*>(a.q);
-    const T* kbase = static_cast<const T*>(a.k);
-    const T* vbase = static_cast<const T*>(a.v);
+    // ---------------- producer warp: TMA ----------------
+    // Lane j issues the loads of requests j, j+32, ...: one TMA box of G rows
+    // x 64 dims per 128-byte chunk, landing in the swizzled MMA layout.  K/V
+    // of a new block (C rows per chunk, zero past the end of the keys) go into
+    // the other K/V buffer; their bytes count toward the same tile's barrier.
     int64_t cur_kv = -1;
     int kvb = 1, used0 = 0, used1 = 0;
-    // metadata of the next tile is fetched one iteration ahead
     int owner_next = a.tile_owner[first];
-    int req_next = ptid < a.RT ? a.tile_req[int64_t(first) * a.RT + ptid] : -1;
+    int req_next[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = lane + 32 * u;
+      req_next[u] = j < a.RT ? a.tile_req[int64_t(first) * a.RT + j] : -1;
+    }
+    const uint32_t rows_bytes = uint32_t(a.G) * 128;
     for (int it = 0; it < ntiles; ++it) {
       const int tile = first + it, s = it % nst, rnd = it / nst;
-      const int owner = owner_next, req = req_next;
+      const int owner = owner_next;
+      int req[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) req[u] = req_next[u];
       if (it + 1 < ntiles) {
         owner_next = a.tile_owner[tile + 1];
-        req_next = ptid < a.RT ? a.tile_req[int64_t(tile + 1) * a.RT + ptid] : -1;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = lane + 32 * u;
+          req_next[u] = j < a.RT ? a.tile_req[int64_t(tile + 1) * a.RT + j] : -1;
+        }
       }
       if (!tc::mbar_wait(&q_empty[s], (rnd & 1) ^ 1)) { s_fail = 1; break; }
       const int blk = owner % a.NB;
       const int h = (owner / a.NB) % a.H;
       const int b = owner / (a.NB * a.H * a.nwin);
       const int64_t kv_key = (int64_t(b) * a.H + h) * a.NB + blk;
+      uint32_t bytes = 0;
       if (kv_key != cur_kv) {
         kvb ^= 1;
         // The buffer being replaced was last read by tile it-2 or earlier:
@@ -217,57 +228,43 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const AttnTcAr
         }
         if (kvb) used1 = 1; else used0 = 1;
         const uint32_t ks_addr = kv_addr + kvb * kv_bytes, vs_addr = ks_addr + qch * a.C * 128;
-        const int64_t tok0 = int64_t(blk) * a.C;
-        const T* kb = kbase + b * a.k_sb + int64_t(h) * a.k_sh;
-        const T* vb = vbase + b * a.v_sb + int64_t(h) * a.v_sh;
-        for (int idx = ptid; idx < a.C * vpr; idx += kLoadWarps * 32) {
-          const int r = idx / vpr, c = idx - r * vpr;
-          const uint32_t dst = ks_addr + (c >> 3) * a.C * 128 + tc::swizzle128(r, c & 7);
-          const int64_t tok = tok0 + r;
-          if (tok < a.N && c * 8 < a.D) cp_async16(dst, kb + tok * a.k_st + c * 8);
-          else st_zero16(dst);
-        }
-        for (int idx = ptid; idx < a.C * vvpr; idx += kLoadWarps * 32) {
-          const int r = idx / vvpr, c = idx - r * vvpr;
-          const uint32_t dst = vs_addr + (c >> 3) * a.C * 128 + tc::swizzle128(r, c & 7);
-          const int64_t tok = tok0 + r;
-          if (tok < a.N && c * 8 < a.Dv) cp_async16(dst, vb + tok * a.v_st + c * 8);
-          else st_zero16(dst);
-        }
+        if (lane < qch)
+          tc::tma_load_4d(ks_addr + lane * a.C * 128, &a.tm_k, lane * 64, h, blk * a.C, b, &q_full[s]);
+        else if (lane < qch + vch)
+          tc::tma_load_4d(vs_addr + (lane - qch) * a.C * 128, &a.tm_v, (lane - qch) * 64, h, blk * a.C, b, &q_full[s]);
+        bytes += uint32_t(qch + vch) * a.C * 128;
         cur_kv = kv_key;
       }
       const int slot = it & 7;
-      if (ptid < 128) {
-        int64_t off = -1;
+      const uint32_t qa = qs_addr + s * q_stage_bytes;
+      int nreq = 0;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = lane + 32 * u;
+        if (j >= a.RT) break;
         int nv = 0;
-        if (req >= 0) {
-          const Req q = decode_req(req, a);
-          off = q.b * a.q_sb + int64_t(a.t0 + q.tl) * a.q_st + int64_t(q.h * a.G) * a.q_sh;
+        if (req[u] >= 0) {
+          const Req q = decode_req(req[u], a);
+          const int t = a.t0 + q.tl;
           int64_t limit = a.N;
-          if (a.causal) limit = min64(limit, position_of(a, q.b, a.t0 + q.tl) + 1);
+          if (a.causal) limit = min64(limit, position_of(a, q.b, t) + 1);
           nv = int(max(int64_t(0), min64(int64_t(a.C), limit - int64_t(blk) * a.C)));
+          for (int kc = 0; kc < qch; ++kc)
+            tc::tma_load_4d(qa + kc * 128 * 128 + j * rows_bytes, &a.tm_q, kc * 64, q.h * a.G, t, q.b, &q_full[s]);
+          ++nreq;
         }
-        if (ptid < a.RT) s_qoff[s][ptid] = off;
-        s_req[slot][ptid] = req;
-        s_nv[slot][ptid] = nv;
+        s_req[slot][j] = req[u];
+        s_nv[slot][j] = nv;
       }
-      if (ptid == 0) s_kvb[s] = kvb;
-      tc::mbar_arrive(&meta_full[slot]);
-      tc::named_sync(1, kLoadWarps * 32);
-      const int c = ptid & (vpr - 1);
-      const uint32_t qdst = qs_addr + s * q_stage_bytes + (c >> 3) * 128 * 128;
-      for (int row = ptid / vpr; row < 128; row += kLoadWarps * 32 / vpr) {
-        const int r = row >> lgG, gh = row & (a.G - 1);
-        const int64_t off = r < a.RT ? s_qoff[s][r] : -1;
-        const uint32_t dst = qdst + tc::swizzle128(row, c & 7);
-        if (off >= 0 && c * 8 < a.D) cp_async16(dst, qbase + off + int64_t(gh) * a.q_sh + c * 8);
-        else st_zero16(dst);
+      const int total_req = __reduce_add_sync(kFull, nreq);
+      __syncwarp();
+      if (lane == 0) {
+        s_kvb[s] = kvb;
+        tc::mbar_arrive_expect_tx(&q_full[s], bytes + uint32_t(total_req) * qch * rows_bytes);
+        tc::mbar_arrive(&meta_full[slot]);
       }
-      // completion is tracked by the barrier; the next stage starts immediately
-      tc::fence_async_smem();
-      tc::cp_async_arrive(&q_full[s]);
+      __syncwarp();
     }
-    cp_async_wait_all();
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issue ----------------
     if (lane == 0) {

@@ -1,6 +1,9 @@
 // extern "C" entry points of libpisa_b200: argument checks, workspace layout
 // and dispatch.  Each function documents the reference operator it replaces
 // in include/pisa_b200.h.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <cmath>
 #include <cstdio>
 #include <string>
@@ -22,6 +25,38 @@ int fail_cuda(cudaError_t err, const char* where) {
 }
 
 static bool is_pow2(int64_t x) { return x > 0 && (x & (x - 1)) == 0; }
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int make_tensor_map(CUtensorMap* map, const void* base, int dtype, int64_t B, int64_t T, int64_t H,
+                    int64_t D, int64_t sb, int64_t st, int64_t sh, uint32_t box_h, uint32_t box_t) {
+  auto encode = tensor_map_encoder();
+  if (!encode) return fail(PISA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int64_t es = dtype == PISA_F32 ? 4 : 2;
+  const cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(H), cuuint64_t(T), cuuint64_t(B)};
+  const cuuint64_t strides[3] = {cuuint64_t(sh * es), cuuint64_t(st * es), cuuint64_t((B > 1 ? sb : T * st) * es)};
+  const cuuint32_t box[4] = {64u, box_h, box_t, 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  const CUtensorMapDataType type = dtype == PISA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = encode(map, type, 4, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PISA_ERR_UNSUPPORTED, "tensor map encoding rejected the operand layout");
+  return PISA_OK;
+}
 
 static int elem_size(int dtype) { return dtype == PISA_F32 ? 4 : 2; }
 
@@ -152,7 +187,7 @@ static bool grouped_tc_eligible(int64_t Hq, int64_t H, int64_t D, int dtype, int
   const int64_t G = Hq / H;
   return schedule == PISA_SCHEDULE_GROUPED && (dtype == PISA_BF16 || dtype == PISA_F16) &&
          (method == PISA_METHOD_PISA || method == PISA_METHOD_PISA2) && is_pow2(G) && G <= 32 &&
-         D % 8 == 0 && D <= 256 && br * C <= 512 &&
+         D % 8 == 0 && D <= 256 && br * C <= 256 &&
          (D <= 64 ? 1 : D <= 128 ? 2 : 4) * 128 * (3 * 128 + br * C) + 1024 + 8192 <= 227 * 1024;
 }
 
@@ -393,6 +428,10 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
   g.tmem_cols = want <= 32 ? 32 : want <= 64 ? 64 : want <= 128 ? 128 : want <= 256 ? 256 : 512;
   g.num_sms = num_sms();
   g.out_ids = out_ids;
+  rc = make_tensor_map(&g.tm_q, q, dtype, B, Tq, Hq, D, q_sb, q_st, q_sh, uint32_t(g.G), 1);
+  if (rc == PISA_OK)
+    rc = make_tensor_map(&g.tm_k, keys, dtype, B, N, H, D, key_sb, key_st, key_sh, 1, uint32_t(nk));
+  if (rc) return rc;
   return grouped_leaf(g, dtype, s);
 }
 
@@ -512,6 +551,10 @@ int pisa_sparse_attn_fwd(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh
     a.tmem_cols = int(plan.tmem_cols); a.sp_cols = int(plan.sp_cols); a.o_cols = int(plan.o_cols);
     a.nacc = int(plan.nacc); a.nstages = int(plan.nstages); a.num_sms = num_sms();
     a.out = out; a.lse = lse;
+    int rc = make_tensor_map(&a.tm_q, q, dtype, B, Tq, Hq, D, q_sb, q_st, q_sh, uint32_t(a.G), 1);
+    if (rc == PISA_OK) rc = make_tensor_map(&a.tm_k, k, dtype, B, N, H, D, k_sb, k_st, k_sh, 1, uint32_t(block_size));
+    if (rc == PISA_OK) rc = make_tensor_map(&a.tm_v, v, dtype, B, N, H, Dv, v_sb, v_st, v_sh, 1, uint32_t(block_size));
+    if (rc) return rc;
     return attn_fwd_tc(a, dtype, static_cast<cudaStream_t>(stream));
   }
   AttnArgs a{};

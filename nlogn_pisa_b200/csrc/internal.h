@@ -1,6 +1,7 @@
 // Internal declarations shared by the translation units of libpisa_b200.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -12,6 +13,12 @@ namespace pisa {
 // Records `msg` as the calling thread's last error and returns `code`.
 int fail(int code, const char* msg);
 int fail_cuda(cudaError_t err, const char* where);
+
+// 4-D TMA map over a [B, T, H, D] view (element strides sb, st, sh; 16-byte
+// aligned rows) with 128-byte swizzle and a box of {64, box_h, box_t, 1}
+// elements; out-of-range elements read as zero.
+int make_tensor_map(CUtensorMap* map, const void* base, int dtype, int64_t B, int64_t T, int64_t H,
+                    int64_t D, int64_t sb, int64_t st, int64_t sh, uint32_t box_h, uint32_t box_t);
 
 #define PISA_CHECK_LAUNCH()                                        \
   do {                                                             \
@@ -59,6 +66,8 @@ int route(const RouteArgs& a, int dtype, cudaStream_t stream);
 // window, KV head, level-1 survivor), scored on the tensor cores, then the
 // final top-K.  Arrays are workspace slices laid out by the C entry point.
 struct GroupArgs {
+  CUtensorMap tm_q;   // q [B,T,Hq,D], box {64, G, 1, 1}
+  CUtensorMap tm_k;   // keys [B,N,H,D], box {64, 1, b*C, 1}
   const void* q;
   int64_t q_sb, q_st, q_sh;
   const void* keys;
@@ -142,6 +151,9 @@ int attn_fwd(const AttnArgs& a, int dtype, cudaStream_t stream);
 
 // Bucketed tensor-core attention forward (prefill): see attn_tc.cu.
 struct AttnTcArgs {
+  CUtensorMap tm_q;   // q [B,T,Hq,D], box {64, G, 1, 1}
+  CUtensorMap tm_k;   // k [B,N,H,D], box {64, 1, C, 1}
+  CUtensorMap tm_v;   // v [B,N,H,Dv], box {64, 1, C, 1}
   const void* q;
   int64_t q_sb, q_st, q_sh;
   const void* k;

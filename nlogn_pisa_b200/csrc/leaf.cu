@@ -86,11 +86,11 @@ __global__ void family_scatter_kernel(const GroupArgs g, const int32_t* __restri
 // mbarriers: full_q/empty_q guard the query stages, full_acc/empty_acc the
 // accumulators; the parity of round r is r & 1 (empty waits start at 1, so the
 // first round passes).  Every wait is bounded and records a timeout status.
-constexpr int kEpiWarps = 8, kLoadWarps = 4, kMmaWarp = 12, kStages = 3;
+constexpr int kEpiWarps = 8, kLoadWarps = 1, kMmaWarp = 9, kStages = 3;
 constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
 
 template <typename T>
-__global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArgs g) {
+__global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_constant__ GroupArgs g) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int Dp = g.Dp;                       // padded head_dim: 64, 128 or 256
@@ -101,7 +101,6 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
   uint8_t* Ks = smem + kStages * q_stage_bytes;    // [chunks][NK][128 B]
   __shared__ uint64_t full_q[kStages], empty_q[kStages], full_acc[2], empty_acc[2];
   __shared__ uint32_t tmem_slot;
-  __shared__ int64_t s_qoff[kStages][128];
   __shared__ int s_fail;
   // per-tile metadata ring for the epilogue (8 slots): the producer runs at
   // most kStages tiles ahead of the MMAs and they at most two ahead of the
@@ -119,14 +118,14 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
 
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
-      tc::mbar_init(&full_q[i], kLoadWarps * 32);
+      tc::mbar_init(&full_q[i], 1);
       tc::mbar_init(&empty_q[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&full_acc[i], 1);
       tc::mbar_init(&empty_acc[i], kEpiWarps * 32);
     }
-    for (int i = 0; i < 8; ++i) tc::mbar_init(&meta_full[i], kLoadWarps * 32);
+    for (int i = 0; i < 8; ++i) tc::mbar_init(&meta_full[i], 1);
     s_fail = 0;
     tc::fence_barrier_init();
   }
@@ -140,69 +139,74 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const GroupArg
   const int lgG = 31 - __clz(g.G);
 
   if (warp >= kEpiWarps && warp < kMmaWarp) {
-    // ---------------- producers ----------------
-    const int ptid = tid - kEpiWarps * 32;
-    const int c = ptid & (vpr - 1);          // this thread's 16-byte column
-    const int row_step = kLoadWarps * 32 / vpr;
-    const T* qbase = static_cast<const T*>(g.q);
-    const T* kbase = static_cast<const T*>(g.keys);
+    // ---------------- producer warp: TMA ----------------
+    // Lane j issues request j, j+32, ...: one TMA box (G rows x 64 dims) per
+    // 128-byte chunk into the swizzled layout; a new family's b*C keys (one
+    // box per chunk, zero past the sequence end) count on the same barrier.
     int cur_key = -1;
-    // metadata of the next tile is fetched one iteration ahead
     int owner_next = g.tile_owner[first];
-    int req_next = ptid < g.RT ? g.tile_req[int64_t(first) * g.RT + ptid] : -1;
+    int req_next[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = lane + 32 * u;
+      req_next[u] = j < g.RT ? g.tile_req[int64_t(first) * g.RT + j] : -1;
+    }
+    const uint32_t rows_bytes = uint32_t(g.G) * 128;
     for (int it = 0; it < ntiles; ++it) {
       const int tile = first + it, s = it % kStages, rnd = it / kStages;
-      const int owner = owner_next, req = req_next;
+      const int owner = owner_next;
+      int req[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) req[u] = req_next[u];
       if (it + 1 < ntiles) {
         owner_next = g.tile_owner[tile + 1];
-        req_next = ptid < g.RT ? g.tile_req[int64_t(tile + 1) * g.RT + ptid] : -1;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = lane + 32 * u;
+          req_next[u] = j < g.RT ? g.tile_req[int64_t(tile + 1) * g.RT + j] : -1;
+        }
       }
       if (!tc::mbar_wait(&empty_q[s], (rnd & 1) ^ 1)) { s_fail = 1; break; }
       const int p = owner % g.NP;
       const int h = (owner / g.NP) % g.H;
       const int b = owner / (g.NP * g.H * g.nwin);
       const int kkey = (b * g.H + h) * g.NP + p;
+      uint32_t bytes = 0;
       if (kkey != cur_key) {
         // the previous tile's MMA must be done before its keys are replaced
         if (it > 0 && !tc::mbar_wait(&empty_q[(it - 1) % kStages], ((it - 1) / kStages) & 1)) { s_fail = 1; break; }
-        const int64_t tok0 = int64_t(p) * NK;
-        const T* kb = kbase + b * g.k_sb + int64_t(h) * g.k_sh;
-        for (int r = ptid / vpr; r < NK; r += row_step) {
-          const uint32_t dst = ks_addr + (c >> 3) * NK * 128 + tc::swizzle128(r, c & 7);
-          const int64_t tok = tok0 + r;
-          if (tok < g.N && c * 8 < g.D) cp_async16(dst, kb + tok * g.k_st + c * 8);
-          else st_zero16(dst);
-        }
+        if (lane < chunks)
+          tc::tma_load_4d(ks_addr + lane * NK * 128, &g.tm_k, lane * 64, h, p * NK, b, &full_q[s]);
+        bytes += uint32_t(chunks) * NK * 128;
         cur_key = kkey;
       }
-      {
-        int64_t off = -1;
+      const int slot = it & 7;
+      const uint32_t qa = qs_addr + s * q_stage_bytes;
+      int nreq = 0;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = lane + 32 * u;
+        if (j >= g.RT) break;
         int dst = -1;
-        if (req >= 0) {
-          const int rowid = req / g.NF;
+        if (req[u] >= 0) {
+          const int rowid = req[u] / g.NF;
           const int hh = rowid % g.H, t = (rowid / g.H) % g.T, bb = rowid / (g.H * g.T);
-          off = bb * g.q_sb + int64_t(t) * g.q_st + int64_t(hh * g.G) * g.q_sh;
-          dst = rowid * g.W0 + (req - rowid * g.NF) * g.br;
+          dst = rowid * g.W0 + (req[u] - rowid * g.NF) * g.br;
+          for (int kc = 0; kc < chunks; ++kc)
+            tc::tma_load_4d(qa + kc * 128 * 128 + j * rows_bytes, &g.tm_q, kc * 64, hh * g.G, t, bb, &full_q[s]);
+          ++nreq;
         }
-        if (ptid < g.RT) s_qoff[s][ptid] = off;
-        s_dst[it & 7][ptid] = dst;
-        if (ptid == 0) s_fam[it & 7] = p;
-        tc::mbar_arrive(&meta_full[it & 7]);
+        s_dst[slot][j] = dst;
       }
-      tc::named_sync(1, kLoadWarps * 32);
-      const uint32_t qdst = qs_addr + s * q_stage_bytes + (c >> 3) * 128 * 128;
-      for (int row = ptid / vpr; row < 128; row += row_step) {
-        const int r = row >> lgG, gh = row & (g.G - 1);
-        const int64_t off = r < g.RT ? s_qoff[s][r] : -1;
-        const uint32_t dst = qdst + tc::swizzle128(row, c & 7);
-        if (off >= 0 && c * 8 < g.D) cp_async16(dst, qbase + off + int64_t(gh) * g.q_sh + c * 8);
-        else st_zero16(dst);
+      const int total_req = __reduce_add_sync(kFull, nreq);
+      __syncwarp();
+      if (lane == 0) {
+        s_fam[slot] = p;
+        tc::mbar_arrive_expect_tx(&full_q[s], bytes + uint32_t(total_req) * chunks * rows_bytes);
+        tc::mbar_arrive(&meta_full[slot]);
       }
-      // completion is tracked by the barrier; the next stage starts immediately
-      tc::fence_async_smem();
-      tc::cp_async_arrive(&full_q[s]);
+      __syncwarp();
     }
-    cp_async_wait_all();
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issue ----------------
     if (lane == 0) {

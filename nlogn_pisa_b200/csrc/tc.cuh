@@ -10,6 +10,7 @@
 // must be 1024-byte aligned; wider K is a sequence of such tiles.
 #pragma once
 
+#include <cuda.h>
 #include <stdint.h>
 
 namespace pisa {
@@ -104,6 +105,25 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
 // landed (the arrival counts toward the barrier's initial count).
 __device__ __forceinline__ void cp_async_arrive(uint64_t* mbar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(smem_u32(mbar)) : "memory");
+}
+
+// One arrival that also expects `bytes` more transaction bytes (TMA) this phase.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+               :: "r"(smem_u32(mbar)), "r"(bytes) : "memory");
+}
+
+// TMA: copy the box at coordinates (c0..c3) of a 4-D tensor map into shared
+// memory at `dst` (the map's swizzle applies); completion counts the box's
+// bytes on `mbar`.  c0 (innermost) is always a multiple of 64 elements here.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, int c3, uint64_t* mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6];"
+      :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+         "r"(smem_u32(mbar))
+      : "memory");
 }
 
 // Barrier among `count` threads of the CTA on hardware barrier `id` (1..15).
