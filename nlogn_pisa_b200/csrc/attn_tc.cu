@@ -122,7 +122,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 //   warp 12          MMA issue: S(i+1) = Q K^T is issued before O(i) = P V
 // mbarriers per stage/buffer: q_full/q_empty (query stages), s_full, p_full,
 // o_full, acc_empty (TMEM buffer of S, P and O).  All waits are bounded.
-constexpr int kEpiWarps = 8, kLoadWarps = 1, kMmaWarp = 9, kStages = 3;
+constexpr int kEpiWarps = 8, kLoadWarps = 1, kMmaWarp = 9, kStages = 3, kGroup = 8;
 constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
 
 template <typename T>
@@ -147,11 +147,16 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int total = *a.total_tiles;
-  const int per = (total + gridDim.x - 1) / gridDim.x;
-  const int first = blockIdx.x * per;
-  const int last = min(first + per, total);
-  if (first >= last) return;
-  const int ntiles = last - first;
+  // Tiles go out in groups of kGroup consecutive tiles (one bucket run keeps
+  // its staged keys), group k to CTA k mod gridDim: at any moment all SMs work
+  // on neighbouring buckets, so the gathered query rows stay in L2.
+  const int ngroups = (total + kGroup - 1) / kGroup;
+  const int my_groups = ngroups > int(blockIdx.x) ? (ngroups - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+  if (my_groups == 0) return;
+  const int last_group = int(blockIdx.x) + (my_groups - 1) * int(gridDim.x);
+  const int ntiles = (my_groups - 1) * kGroup + min(kGroup, total - last_group * kGroup);
+  auto tile_of = [&](int it) { return (int(blockIdx.x) + (it / kGroup) * int(gridDim.x)) * kGroup + it % kGroup; };
+  const int first = tile_of(0);
   const int nacc = a.nacc;                    // S/P and O buffers: 2 (double) or 1
   const int nst = a.nstages;                  // query stages: 3 or 2
 
@@ -198,17 +203,17 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
     }
     const uint32_t rows_bytes = uint32_t(a.G) * 128;
     for (int it = 0; it < ntiles; ++it) {
-      const int tile = first + it, s = it % nst, rnd = it / nst;
+      const int tile = tile_of(it), s = it % nst, rnd = it / nst;
       const int owner = owner_next;
       int req[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) req[u] = req_next[u];
       if (it + 1 < ntiles) {
-        owner_next = a.tile_owner[tile + 1];
+        owner_next = a.tile_owner[tile_of(it + 1)];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int j = lane + 32 * u;
-          req_next[u] = j < a.RT ? a.tile_req[int64_t(tile + 1) * a.RT + j] : -1;
+          req_next[u] = j < a.RT ? a.tile_req[int64_t(tile_of(it + 1)) * a.RT + j] : -1;
         }
       }
       if (!tc::mbar_wait(&q_empty[s], (rnd & 1) ^ 1)) { s_fail = 1; break; }
@@ -336,7 +341,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
     // two buffers: group g takes tiles g, g+2, ...; one buffer: group 0 takes all
     const int step = nacc == 2 ? 2 : 1;
     for (int it = grp; it < ntiles && (nacc == 2 || grp == 0); it += step) {
-      const int ab = acc_of(it), rnd = round_of(it), tile = first + it;
+      const int ab = acc_of(it), rnd = round_of(it), tile = tile_of(it);
       const bool got = tc::mbar_wait(&s_full[ab], rnd & 1);
       if (!got) s_fail = 1;
       tc::fence_after_sync();

@@ -86,7 +86,7 @@ __global__ void family_scatter_kernel(const GroupArgs g, const int32_t* __restri
 // mbarriers: full_q/empty_q guard the query stages, full_acc/empty_acc the
 // accumulators; the parity of round r is r & 1 (empty waits start at 1, so the
 // first round passes).  Every wait is bounded and records a timeout status.
-constexpr int kEpiWarps = 8, kLoadWarps = 1, kMmaWarp = 9, kStages = 3;
+constexpr int kEpiWarps = 8, kLoadWarps = 1, kMmaWarp = 9, kStages = 3, kGroup = 8;
 constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
 
 template <typename T>
@@ -110,11 +110,16 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int total = *g.total_tiles;
-  const int per = (total + gridDim.x - 1) / gridDim.x;
-  const int first = blockIdx.x * per;
-  const int last = min(first + per, total);
-  if (first >= last) return;
-  const int ntiles = last - first;
+  // Tiles go out in groups of kGroup consecutive tiles (one bucket run keeps
+  // its staged keys), group k to CTA k mod gridDim: at any moment all SMs work
+  // on neighbouring buckets, so the gathered query rows stay in L2.
+  const int ngroups = (total + kGroup - 1) / kGroup;
+  const int my_groups = ngroups > int(blockIdx.x) ? (ngroups - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+  if (my_groups == 0) return;
+  const int last_group = int(blockIdx.x) + (my_groups - 1) * int(gridDim.x);
+  const int ntiles = (my_groups - 1) * kGroup + min(kGroup, total - last_group * kGroup);
+  auto tile_of = [&](int it) { return (int(blockIdx.x) + (it / kGroup) * int(gridDim.x)) * kGroup + it % kGroup; };
+  const int first = tile_of(0);
 
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -153,17 +158,17 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
     }
     const uint32_t rows_bytes = uint32_t(g.G) * 128;
     for (int it = 0; it < ntiles; ++it) {
-      const int tile = first + it, s = it % kStages, rnd = it / kStages;
+      const int tile = tile_of(it), s = it % kStages, rnd = it / kStages;
       const int owner = owner_next;
       int req[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) req[u] = req_next[u];
       if (it + 1 < ntiles) {
-        owner_next = g.tile_owner[tile + 1];
+        owner_next = g.tile_owner[tile_of(it + 1)];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int j = lane + 32 * u;
-          req_next[u] = j < g.RT ? g.tile_req[int64_t(tile + 1) * g.RT + j] : -1;
+          req_next[u] = j < g.RT ? g.tile_req[int64_t(tile_of(it + 1)) * g.RT + j] : -1;
         }
       }
       if (!tc::mbar_wait(&empty_q[s], (rnd & 1) ^ 1)) { s_fail = 1; break; }
@@ -243,7 +248,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
     const float l2e = 1.4426950408889634f;
     const float sl = g.scale * l2e;          // exp(scale*x - m) = 2^(x*sl - m*l2e)
     for (int it = 0; it < ntiles; ++it) {
-      const int tile = first + it;
+      const int tile = tile_of(it);
       const int a = nacc == 2 ? (it & 1) : 0;
       const int ra = nacc == 2 ? (it >> 1) : it;
       const bool got = tc::mbar_wait(&full_acc[a], ra & 1);
