@@ -20,9 +20,9 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
+import re
 import sys
-import tempfile
+import threading
 import time
 from pathlib import Path
 
@@ -46,47 +46,76 @@ def parse_args():
 # clocks sampled during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock, power and clock-event reasons of one GPU, read through NVML
+    every 10 ms by a background thread while the timed region runs."""
 
-    def __init__(self, index):
-        self.index = index
-        self.proc = None
-        self.file = None
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
+
+    def __init__(self, device):
+        self.device = device
+        self.rows = []
+        self.error = None
+        self.thread = None
+        self.stop_flag = threading.Event()
+
+    def _handle(self, nvml):
+        import torch
+
+        props = torch.cuda.get_device_properties(self.device)
+        bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+        return nvml.nvmlDeviceGetHandleByPciBusId(bus)
 
     def start(self):
         try:
-            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.index), "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml as nvml
+
+            nvml.nvmlInit()
+            handle = self._handle(nvml)
+            self.max_mhz = nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM)
+            masks = [(name, getattr(nvml, attr)) for name, attr in self.REASONS if hasattr(nvml, attr)]
+        except Exception as exc:  # NVML missing or device not found: report, do not fail the bench
+            self.error = f"nvml unavailable: {type(exc).__name__}"
+            return
+
+        def loop():
+            while not self.stop_flag.is_set():
+                try:
+                    sm = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
+                    reasons = nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                    power = nvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
+                except Exception as exc:
+                    self.error = f"nvml read failed: {type(exc).__name__}"
+                    return
+                self.rows.append((sm, power, [name for name, bit in masks if reasons & bit]))
+                time.sleep(0.01)
+
+        self.thread = threading.Thread(target=loop, daemon=True)
+        self.thread.start()
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.file.flush()
-        rows = []
-        with open(self.file.name) as fh:
-            for line in fh:
-                parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
-                    rows.append(parts)
-        os.unlink(self.file.name)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows]
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace('.', '').isdigit())}
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.error or "no samples"]}
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": float(self.max_mhz),
+                "reasons": sorted({n for r in self.rows for n in r[2]}), "samples": len(self.rows),
+                "power_w_max": max(r[1] for r in self.rows)}
+
+
+def profiled_traffic(kernel, workload):
+    """DRAM bytes (read + write) per launch of `kernel` on `workload` from the
+    committed ncu summaries: a line `traffic <kernel> <workload>: <bytes>`."""
+    pattern = re.compile(rf"^traffic {kernel} {workload}: (\d+)", re.M)
+    for path in sorted((ROOT / "profiles").glob("*.md")):
+        m = pattern.search(path.read_text())
+        if m:
+            return int(m.group(1))
+    return None
 
 
 # ---------------------------------------------------------------------------
@@ -175,8 +204,6 @@ def main():
     method = _lib.METHODS[w.method]
     scale = D ** -0.5
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
-    # pyramid levels + router + bucket count/scan/scatter + leaf tiles + final top-K + attention
-    launches_per_step = len(sizes) + 7
 
     def pyramid():
         _lib.check(lib.pisa_build_pyramid(
@@ -224,10 +251,17 @@ def main():
     leaf_flops = scored.sum().item() * H * B * 2 * D * G * C
     pyramid_bytes = (B * N * H * D + B * sum(sizes) * H * D) * q.element_size()
 
+    # combine kernel: read every visible request's G partial rows, write the output
+    combine_bytes = valid_ids.sum().item() * G * (D * q.element_size() + 8) + B * N * Hq * D * q.element_size()
+
     clocks = ClockSampler(local)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    for name in _lib.KERNELS:
+        _lib.kernel_time(name)            # drop warm-up records
+    _lib.kernel_timing(True)
+    launches0 = lib.pisa_launch_count()
     clocks.start()
     events = [[torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)] for _ in range(args.steps)]
     for step in range(args.steps):
@@ -241,6 +275,9 @@ def main():
     if world > 1:
         dist.barrier()
     clock_info = clocks.stop()
+    launches = lib.pisa_launch_count() - launches0
+    _lib.kernel_timing(False)
+    kernel_ms = {name: _lib.kernel_time(name) for name in _lib.KERNELS}
     stage_ms = [sum(ev[i].elapsed_time(ev[i + 1]) for ev in events) / args.steps for i in range(len(stages))]
     step_ms = sum(ev[0].elapsed_time(ev[-1]) for ev in events) / args.steps
     times = torch.tensor([step_ms] + stage_ms, device=device, dtype=torch.float64)
@@ -297,8 +334,27 @@ def main():
         achieved = amount / (ms / 1000.0)
         stage_report[name] = {"ms": ms, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                               "frac": achieved / peak}
-    dominant = max(stage_report, key=lambda n: stage_report[n]["ms"])
-    dom = stage_report[dominant]
+    # the dominant kernel: largest device time per step among the timed tile kernels
+    kernel_work = {
+        "leaf_tiles": ("leaf_tc_kernel", "tensor", leaf_flops / 1e12, tensor, "TFLOP/s"),
+        "attn_tiles": ("attn_tc_kernel", "tensor", attn_flops / 1e12, tensor, "TFLOP/s"),
+        "attn_combine": ("attn_combine_tiles_kernel", "hbm", combine_bytes / 1e9, hbm, "GB/s"),
+    }
+    kt = torch.tensor([kernel_ms[n][0] for n in _lib.KERNELS], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(kt, op=dist.ReduceOp.MAX)
+    kernel_report = {}
+    for (name, (ms_total, count)), ms_max in zip(kernel_ms.items(), kt.tolist()):
+        if count == 0:
+            continue
+        kname, bound, amount, peak, unit = kernel_work[name]
+        per_step_ms = ms_max / args.steps
+        achieved = amount / (per_step_ms / 1000.0)
+        kernel_report[name] = {"kernel": kname, "bound": bound, "ms_per_step": per_step_ms,
+                               "launches_per_step": count / args.steps, "ms_per_launch": ms_max / count,
+                               "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak}
+    dominant = max(kernel_report, key=lambda n: kernel_report[n]["ms_per_step"])
+    dom = kernel_report[dominant]
 
     if rank == 0:
         cpu = None
@@ -328,14 +384,19 @@ def main():
                 "l2": "flushed between timed steps (256 MiB write outside the events)",
                 "parallelism": f"dp{world} (one sequence per GPU, no collective)",
             },
-            "roofline": {"kernel": dominant, "bound": dom["bound"], "achieved": dom["achieved"],
-                         "peak": dom["peak"], "unit": dom["unit"], "frac": dom["frac"], "traffic": None,
-                         "peak_source": src},
+            "roofline": {"kernel": dom["kernel"], "bound": dom["bound"], "achieved": dom["achieved"],
+                         "peak": dom["peak"], "unit": dom["unit"], "frac": dom["frac"],
+                         "traffic": profiled_traffic(dominant, w.name),
+                         "peak_source": f"{src} (burst)", "ms_per_launch": dom["ms_per_launch"],
+                         "launches_per_step": dom["launches_per_step"],
+                         "work_per_launch": dom["achieved"] * dom["ms_per_launch"] / 1000.0,
+                         "timing": "CUDA events around each launch on its stream, timed steps only"},
+            "kernels": kernel_report,
             "stages": stage_report,
             "cpu_baseline": cpu,
             "e2e": {"value": world * B * N / (e2e_ms / 1000.0), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches": launches,
             "clocks": clock_info,
         }
         print(json.dumps(line), flush=True)

@@ -184,6 +184,26 @@ PISA_API int pisa_sparse_attn_bwd(const void *q, const void *k, const void *v, c
 PISA_API int64_t pisa_sparse_attn_bwd_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H,
                                              int64_t D, int64_t Dv, int64_t N);
 
+/* ---- per-kernel device timing (profiling aid; the reference has no counterpart) ----
+ * With timing on, the library records a pair of CUDA events on the launch
+ * stream around every launch of the kernels below.  Reading returns the summed
+ * device time and the launch count since the previous read of that kernel and
+ * resets them; it waits for the recorded events.  Process-wide; calls from
+ * several host threads are serialised by a lock. */
+#define PISA_KERNEL_LEAF_TILES 0    /* tensor-core leaf scoring tiles */
+#define PISA_KERNEL_ATTN_TILES 1    /* tensor-core attention tiles */
+#define PISA_KERNEL_ATTN_COMBINE 2  /* merge of the attention block partials */
+#define PISA_KERNEL_COUNT 3
+
+/* Kernels this library has launched in this process so far. */
+PISA_API int64_t pisa_launch_count(void);
+
+/* enable = 1 starts recording, 0 stops it (recorded launches stay readable). */
+PISA_API int pisa_kernel_timing(int enable);
+
+/* Device milliseconds and launches of `kernel` since its last read. */
+PISA_API int pisa_kernel_time(int kernel, double *total_ms, int64_t *launches);
+
 #ifdef __cplusplus
 }
 #endif

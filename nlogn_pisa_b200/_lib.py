@@ -43,6 +43,9 @@ SIGNATURES = {
     "pisa_sparse_attn_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _L, _I, _L, _L, _L, _L, _L,
                                   _L, _L, _L, _L, _F, _I, _P, _P, _P, _P, _L, _P]),
     "pisa_sparse_attn_bwd_workspace_bytes": (_L, [_L, _L, _L, _L, _L, _L, _L]),
+    "pisa_launch_count": (_L, []),
+    "pisa_kernel_timing": (_I, [_I]),
+    "pisa_kernel_time": (_I, [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
 }
 
 _lib = None
@@ -87,3 +90,18 @@ def dtype_code(t):
         return DTYPES[t.dtype]
     except KeyError:
         raise ValueError("the CUDA kernels support FP16, BF16 and FP32") from None
+
+
+KERNELS = {"leaf_tiles": 0, "attn_tiles": 1, "attn_combine": 2}
+
+
+def kernel_timing(enable):
+    """Start (True) or stop (False) per-launch device timing of the tile kernels."""
+    check(lib().pisa_kernel_timing(int(bool(enable))))
+
+
+def kernel_time(name):
+    """(device milliseconds, launches) of one timed kernel since its last read."""
+    ms, n = ctypes.c_double(0.0), ctypes.c_int64(0)
+    check(lib().pisa_kernel_time(KERNELS[name], ctypes.byref(ms), ctypes.byref(n)))
+    return ms.value, n.value

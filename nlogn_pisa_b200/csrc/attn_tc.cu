@@ -554,17 +554,23 @@ int attn_tc_typed(AttnTcArgs a, cudaStream_t stream) {
     PISA_CHECK_LAUNCH();
     attn_scatter_kernel<<<grid, 256, 0, stream>>>(a);
     PISA_CHECK_LAUNCH();
-    attn_tc_kernel<T><<<unsigned(a.num_sms), kPipeThreads, smem, stream>>>(a);
-    PISA_CHECK_LAUNCH();
-    const unsigned cgrid = unsigned((int64_t(a.B) * a.tlen * a.Hq + 3) / 4);
-    switch (a.Dv / 16) {
-      case 1: attn_combine_tiles_kernel<T, 1><<<cgrid, 128, 0, stream>>>(a); break;
-      case 2: attn_combine_tiles_kernel<T, 2><<<cgrid, 128, 0, stream>>>(a); break;
-      case 4: attn_combine_tiles_kernel<T, 4><<<cgrid, 128, 0, stream>>>(a); break;
-      case 8: attn_combine_tiles_kernel<T, 8><<<cgrid, 128, 0, stream>>>(a); break;
-      default: attn_combine_tiles_kernel<T, 16><<<cgrid, 128, 0, stream>>>(a); break;
+    {
+      TimedLaunch timed(PISA_KERNEL_ATTN_TILES, stream);
+      attn_tc_kernel<T><<<unsigned(a.num_sms), kPipeThreads, smem, stream>>>(a);
+      PISA_CHECK_LAUNCH();
     }
-    PISA_CHECK_LAUNCH();
+    const unsigned cgrid = unsigned((int64_t(a.B) * a.tlen * a.Hq + 3) / 4);
+    {
+      TimedLaunch timed(PISA_KERNEL_ATTN_COMBINE, stream);
+      switch (a.Dv / 16) {
+        case 1: attn_combine_tiles_kernel<T, 1><<<cgrid, 128, 0, stream>>>(a); break;
+        case 2: attn_combine_tiles_kernel<T, 2><<<cgrid, 128, 0, stream>>>(a); break;
+        case 4: attn_combine_tiles_kernel<T, 4><<<cgrid, 128, 0, stream>>>(a); break;
+        case 8: attn_combine_tiles_kernel<T, 8><<<cgrid, 128, 0, stream>>>(a); break;
+        default: attn_combine_tiles_kernel<T, 16><<<cgrid, 128, 0, stream>>>(a); break;
+      }
+      PISA_CHECK_LAUNCH();
+    }
   }
   return PISA_OK;
 }

@@ -20,8 +20,26 @@ int fail_cuda(cudaError_t err, const char* where);
 int make_tensor_map(CUtensorMap* map, const void* base, int dtype, int64_t B, int64_t T, int64_t H,
                     int64_t D, int64_t sb, int64_t st, int64_t sh, uint32_t box_h, uint32_t box_t);
 
+// Scope guard that brackets one kernel launch with timing events when
+// per-kernel timing is on (timing.cu); a no-op otherwise.
+class TimedLaunch {
+ public:
+  TimedLaunch(int kernel, cudaStream_t stream);
+  ~TimedLaunch();
+  TimedLaunch(const TimedLaunch&) = delete;
+  TimedLaunch& operator=(const TimedLaunch&) = delete;
+
+ private:
+  int kernel_, slot_;
+  cudaStream_t stream_;
+};
+
+// Counts one launch of this library (pisa_launch_count) and reports a failed launch.
+void count_launch();
+
 #define PISA_CHECK_LAUNCH()                                        \
   do {                                                             \
+    ::pisa::count_launch();                                        \
     cudaError_t _e = cudaGetLastError();                           \
     if (_e != cudaSuccess) return ::pisa::fail_cuda(_e, __func__); \
   } while (0)

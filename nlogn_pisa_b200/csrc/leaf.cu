@@ -384,8 +384,11 @@ int grouped_leaf(const GroupArgs& g, int dtype, cudaStream_t stream) {
   auto kernel = dtype == PISA_BF16 ? leaf_tc_kernel<__nv_bfloat16> : leaf_tc_kernel<__half>;
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return fail_cuda(e, "leaf smem attribute");
-  kernel<<<unsigned(g.num_sms), kPipeThreads, smem, stream>>>(g);
-  PISA_CHECK_LAUNCH();
+  {
+    TimedLaunch timed(PISA_KERNEL_LEAF_TILES, stream);
+    kernel<<<unsigned(g.num_sms), kPipeThreads, smem, stream>>>(g);
+    PISA_CHECK_LAUNCH();
+  }
 
   const unsigned fgrid = unsigned((rows + 3) / 4);
   switch (g.W0) {

@@ -102,3 +102,13 @@ def test_cu_seqlens_contract():
     q = torch.zeros(1, 2, 4, 8)
     k = torch.zeros(1, 9, 2, 8)
     assert list(packed_queries(q, k, torch.tensor([0, 5, 9]))) == [(0, 1, 0, 5, 4), (1, 2, 5, 9, 3)]
+
+
+def test_kernel_timer_without_launches():
+    """Reading a kernel timer that recorded nothing needs no device."""
+    from nlogn_pisa_b200 import _lib
+
+    assert _lib.kernel_time("attn_tiles") == (0.0, 0)
+    lib = _lib.lib()
+    assert lib.pisa_kernel_time(7, None, None) == _lib.ERR_INVALID
+    _lib.kernel_timing(False)
