@@ -118,11 +118,13 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 //   warps 0-3 / 4-7  epilogue groups: group (tile % 2) turns S into P (softmax
 //                    in registers, P back to TMEM) and then O into the partial;
 //                    thread = TMEM lane = query-head row
-//   warps 8-11       producers: query rows into a 2-stage ring; block K/V
-//   warp 12          MMA issue: S(i+1) = Q K^T is issued before O(i) = P V
+//   next kLoadWarps  producers: query rows into a 3-stage ring (cp.async),
+//                    block K/V (TMA, first producer warp)
+//   last warp        MMA issue: S(i+1) = Q K^T is issued before O(i) = P V
 // mbarriers per stage/buffer: q_full/q_empty (query stages), s_full, p_full,
 // o_full, acc_empty (TMEM buffer of S, P and O).  All waits are bounded.
-constexpr int kEpiWarps = 8, kLoadWarps = 1, kMmaWarp = 9, kStages = 3, kGroup = 8;
+constexpr int kEpiWarps = 8, kLoadWarps = 4, kMmaWarp = kEpiWarps + kLoadWarps, kStages = 3, kGroup = 8;
+constexpr int kRowsPerLoader = 128 / kLoadWarps;  // tile rows per producer warp
 constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
 
 template <typename T>
@@ -162,7 +164,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
 
   if (tid == 0) {
     for (int i = 0; i < nst; ++i) {
-      tc::mbar_init(&q_full[i], 1);
+      // one cp.async arrival per producer thread + the K/V arrival of the first producer warp
+      tc::mbar_init(&q_full[i], kLoadWarps * 32 + 1);
       tc::mbar_init(&q_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -171,7 +174,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
       tc::mbar_init(&o_full[i], 1);
       tc::mbar_init(&o_empty[i], 128);
     }
-    for (int i = 0; i < 8; ++i) tc::mbar_init(&meta_full[i], 1);
+    for (int i = 0; i < 8; ++i) tc::mbar_init(&meta_full[i], kLoadWarps);
     s_fail = 0;
     tc::fence_barrier_init();
   }
@@ -187,101 +190,113 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
   auto round_of = [&](int it) { return nacc == 2 ? (it >> 1) : it; };
 
   if (warp >= kEpiWarps && warp < kMmaWarp) {
-    // ---------------- producer warp: TMA ----------------
-    // Lane j issues the loads of requests j, j+32, ...: one TMA box of G rows
-    // x 64 dims per 128-byte chunk, landing in the swizzled MMA layout.  K/V
-    // of a new block (C rows per chunk, zero past the end of the keys) go into
-    // the other K/V buffer; their bytes count toward the same tile's barrier.
+    // ---------------- producer warps ----------------
+    // Query rows move with 16-byte asynchronous copies (cp.async) straight
+    // into their swizzled K-major positions; every producer thread's copies
+    // arrive on the stage barrier when they land (cp.async.mbarrier.arrive),
+    // so the warps go on to the next stage without waiting for the data.
+    // Producer warp pw owns kRowsPerLoader tile rows, lane l decodes the
+    // request of its l-th row, and one warp instruction moves 512 contiguous
+    // bytes.  (A TMA box per request holds only G rows x 128 bytes, and the
+    // TMA unit's per-copy cost then bounds the tile rate.)  Producer warp 0
+    // also loads K/V of a new block through TMA (C rows per 64-dim chunk,
+    // zero past the end of the keys) into the other K/V buffer; those bytes
+    // count toward the same tile's barrier.
+    const int pw = warp - kEpiWarps;
+    const int row = pw * kRowsPerLoader + (lane & (kRowsPerLoader - 1));  // tile row of this lane
+    const int j = row >> lgG, gq = row & (a.G - 1);   // its request and head
+    const int lgS = 31 - __clz(a.Dp / 8);             // 16-byte segments per row (log2)
+    const int nseg = 1 << lgS, dsegs = a.D / 8;
+    const T* qbase = static_cast<const T*>(a.q);
     int64_t cur_kv = -1;
     int kvb = 1, used0 = 0, used1 = 0;
     int owner_next = a.tile_owner[first];
-    int req_next[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int j = lane + 32 * u;
-      req_next[u] = j < a.RT ? a.tile_req[int64_t(first) * a.RT + j] : -1;
-    }
-    const uint32_t rows_bytes = uint32_t(a.G) * 128;
+    int req_next = a.tile_req[int64_t(first) * a.RT + j];
     for (int it = 0; it < ntiles; ++it) {
-      const int tile = tile_of(it), s = it % nst, rnd = it / nst;
-      const int owner = owner_next;
-      int req[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) req[u] = req_next[u];
+      const int s = it % nst, rnd = it / nst;
+      const int owner = owner_next, req = req_next;
       if (it + 1 < ntiles) {
-        owner_next = a.tile_owner[tile_of(it + 1)];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int j = lane + 32 * u;
-          req_next[u] = j < a.RT ? a.tile_req[int64_t(tile_of(it + 1)) * a.RT + j] : -1;
-        }
+        const int nt = tile_of(it + 1);
+        owner_next = a.tile_owner[nt];
+        req_next = a.tile_req[int64_t(nt) * a.RT + j];
       }
-      if (!tc::mbar_wait(&q_empty[s], (rnd & 1) ^ 1)) { s_fail = 1; break; }
       const int blk = owner % a.NB;
       const int h = (owner / a.NB) % a.H;
       const int b = owner / (a.NB * a.H * a.nwin);
-      const int64_t kv_key = (int64_t(b) * a.H + h) * a.NB + blk;
-      uint32_t bytes = 0;
-      if (kv_key != cur_kv) {
-        kvb ^= 1;
-        // The buffer being replaced was last read by tile it-2 or earlier:
-        // wait for that P.V (with one TMEM buffer, the in-order issue makes
-        // P.V of tile it-1 the one to wait for; it never needs tile it).
-        if (kvb ? used1 : used0) {
-          const int wt = nacc == 2 ? it - 2 : it - 1;
-          if (wt >= 0 && !tc::mbar_wait(&o_full[acc_of(wt)], round_of(wt) & 1)) { s_fail = 1; break; }
-        }
-        if (kvb) used1 = 1; else used0 = 1;
-        const uint32_t ks_addr = kv_addr + kvb * kv_bytes, vs_addr = ks_addr + qch * a.C * 128;
-        if (lane < qch)
-          tc::tma_load_4d(ks_addr + lane * a.C * 128, &a.tm_k, lane * 64, h, blk * a.C, b, &q_full[s]);
-        else if (lane < qch + vch)
-          tc::tma_load_4d(vs_addr + (lane - qch) * a.C * 128, &a.tm_v, (lane - qch) * 64, h, blk * a.C, b, &q_full[s]);
-        bytes += uint32_t(qch + vch) * a.C * 128;
-        cur_kv = kv_key;
+      // source row of this lane, valid keys of its request
+      const T* src = nullptr;
+      int nv = 0;
+      if (req >= 0) {
+        const Req q = decode_req(req, a);
+        const int t = a.t0 + q.tl;
+        int64_t limit = a.N;
+        if (a.causal) limit = min64(limit, position_of(a, q.b, t) + 1);
+        nv = int(max(int64_t(0), min64(int64_t(a.C), limit - int64_t(blk) * a.C)));
+        src = qbase + int64_t(q.b) * a.q_sb + int64_t(t) * a.q_st + int64_t(q.h * a.G + gq) * a.q_sh;
       }
-      const int slot = it & 7;
-      const uint32_t qa = qs_addr + s * q_stage_bytes;
-      int nreq = 0;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = lane + 32 * u;
-        if (j >= a.RT) break;
-        int nv = 0;
-        if (req[u] >= 0) {
-          const Req q = decode_req(req[u], a);
-          const int t = a.t0 + q.tl;
-          int64_t limit = a.N;
-          if (a.causal) limit = min64(limit, position_of(a, q.b, t) + 1);
-          nv = int(max(int64_t(0), min64(int64_t(a.C), limit - int64_t(blk) * a.C)));
-          for (int kc = 0; kc < qch; ++kc)
-            tc::tma_load_4d(qa + kc * 128 * 128 + j * rows_bytes, &a.tm_q, kc * 64, q.h * a.G, t, q.b, &q_full[s]);
-          ++nreq;
+      if (!tc::mbar_wait(&q_empty[s], (rnd & 1) ^ 1)) { s_fail = 1; break; }
+      // rows of requests without a visible block are left as they are: their
+      // results are never read.  Dimensions past D are zero-filled.
+      const uint32_t stage = qs_addr + s * q_stage_bytes;
+      for (int u = 0; u < (kRowsPerLoader << lgS) / 32; ++u) {
+        const int f = u * 32 + lane;
+        const int rl = f >> lgS, seg = f & (nseg - 1);
+        const T* rs = reinterpret_cast<const T*>(__shfl_sync(kFull, reinterpret_cast<uintptr_t>(src), rl));
+        if (rs != nullptr) {
+          const int r = pw * kRowsPerLoader + rl, kc = seg >> 3, c = seg & 7;
+          const uint32_t dst = stage + kc * 128 * 128 + r * 128 + ((c ^ (r & 7)) << 4);
+          if (seg < dsegs) cp_async16(dst, rs + seg * 8);
+          else cp_async16_zfill(dst, qbase);
         }
-        s_req[slot][j] = req[u];
+      }
+      tc::cp_async_arrive(&q_full[s]);
+      const int slot = it & 7;
+      if (gq == 0 && lane < kRowsPerLoader) {
+        s_req[slot][j] = req;
         s_nv[slot][j] = nv;
       }
-      const int total_req = __reduce_add_sync(kFull, nreq);
+      uint32_t bytes = 0;
+      if (pw == 0) {
+        const int64_t kv_key = (int64_t(b) * a.H + h) * a.NB + blk;
+        if (kv_key != cur_kv) {
+          kvb ^= 1;
+          // The buffer being replaced was last read by tile it-2 or earlier:
+          // wait for that P.V (with one TMEM buffer, the in-order issue makes
+          // P.V of tile it-1 the one to wait for; it never needs tile it).
+          if (kvb ? used1 : used0) {
+            const int wt = nacc == 2 ? it - 2 : it - 1;
+            if (wt >= 0 && !tc::mbar_wait(&o_full[acc_of(wt)], round_of(wt) & 1)) { s_fail = 1; break; }
+          }
+          if (kvb) used1 = 1; else used0 = 1;
+          const uint32_t ks_addr = kv_addr + kvb * kv_bytes, vs_addr = ks_addr + qch * a.C * 128;
+          if (lane < qch)
+            tc::tma_load_4d(ks_addr + lane * a.C * 128, &a.tm_k, lane * 64, h, blk * a.C, b, &q_full[s]);
+          else if (lane < qch + vch)
+            tc::tma_load_4d(vs_addr + (lane - qch) * a.C * 128, &a.tm_v, (lane - qch) * 64, h, blk * a.C, b, &q_full[s]);
+          bytes = uint32_t(qch + vch) * a.C * 128;
+          cur_kv = kv_key;
+        }
+      }
       __syncwarp();
       if (lane == 0) {
-        s_kvb[s] = kvb;
-        tc::mbar_arrive_expect_tx(&q_full[s], bytes + uint32_t(total_req) * qch * rows_bytes);
+        if (pw == 0) {
+          s_kvb[s] = kvb;
+          tc::mbar_arrive_expect_tx(&q_full[s], bytes);
+        }
         tc::mbar_arrive(&meta_full[slot]);
       }
       __syncwarp();
     }
+    cp_async_wait_all();
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issue ----------------
     if (lane == 0) {
       const uint32_t idesc_s = tc::idesc_f16(128, a.C, a.bf16);
       const uint32_t idesc_o = tc::idesc_f16(128, a.Dv, a.bf16, 1);
       int kv_even = 0, kv_odd = 0;  // K/V buffer of the last even / odd tile
-      // S = Q K^T of tile `it` into its S/P buffer; only the query stage is
-      // awaited: the buffer's previous P was consumed by a P.V issued earlier
-      // from this thread, and tensor-core operations run in issue order.
-      auto issue_s = [&](int it) -> bool {
+      // S = Q K^T of tile `it` into its S/P buffer (its query stage has landed)
+      auto issue_s = [&](int it) {
         const int s = it % nst, ab = acc_of(it);
-        if (!tc::mbar_wait(&q_full[s], (it / nst) & 1)) return false;
         tc::fence_async_smem();
         tc::fence_after_sync();
         const int kvb = s_kvb[s];
@@ -296,13 +311,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
         }
         tc::mma_commit(&s_full[ab]);
         tc::mma_commit(&q_empty[s]);
-        return true;
       };
-      // O = P V of tile `pt` once its P is in TMEM and its O buffer was read out
-      auto issue_o = [&](int pt) -> bool {
+      // O = P V of tile `pt` (its P is in TMEM and its O buffer was read out)
+      auto issue_o = [&](int pt) {
         const int ab = acc_of(pt);
-        if (!tc::mbar_wait(&p_full[ab], round_of(pt) & 1)) return false;
-        if (!tc::mbar_wait(&o_empty[ab], (round_of(pt) & 1) ^ 1)) return false;
         tc::fence_after_sync();
         const uint32_t sp = tmem + ab * a.sp_cols;
         const uint32_t ob = tmem + nacc * a.sp_cols + ab * a.o_cols;
@@ -312,20 +324,35 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
           tc::mma_f16_ts(ob, sp + a.C + ks * 8, vd, idesc_o, ks > 0);
         }
         tc::mma_commit(&o_full[ab]);
-        return true;
       };
-      // Two buffers: S(i) before O(i-1), so Q K^T of the next tile overlaps the
-      // softmax of the current one.  One buffer: O(i-1) first (S(i) overwrites P(i-1)).
-      for (int it = 0; it <= ntiles; ++it) {
-        bool ok = true;
-        if (nacc == 2) {
-          if (it < ntiles) ok = issue_s(it);
-          if (ok && it >= 1) ok = issue_o(it - 1);
-        } else {
-          if (it >= 1) ok = issue_o(it - 1);
-          if (ok && it < ntiles) ok = issue_s(it);
+      // Issue whichever of O(no) and S(ns) is ready, O first: P.V of a tile
+      // never waits for the next tile's query rows.  Order rules (tensor-core
+      // operations run in issue order): S(ns) overwrites the S/P buffer of
+      // tile ns - nacc, so that tile's P.V must have been issued; O(no)
+      // needs S(no) issued, P(no) in TMEM and its O buffer read out.
+      int ns = 0, no = 0;
+      uint32_t idle = 0;
+      while (no < ntiles) {
+        bool issued = false;
+        if (no < ns) {
+          const int ab = acc_of(no), ph = round_of(no) & 1;
+          if (tc::mbar_test(&p_full[ab], ph) && tc::mbar_test(&o_empty[ab], ph ^ 1)) {
+            issue_o(no++);
+            issued = true;
+          }
         }
-        if (!ok) { s_fail = 1; break; }
+        if (!issued && ns < ntiles && no >= ns - nacc + 1) {
+          if (tc::mbar_test(&q_full[ns % nst], (ns / nst) & 1)) {
+            issue_s(ns++);
+            issued = true;
+          }
+        }
+        if (issued) {
+          idle = 0;
+        } else if (++idle > (1u << 24)) {
+          s_fail = 1;
+          break;
+        }
       }
     }
     __syncwarp();

@@ -51,6 +51,10 @@ tile_scan_kernel(const int32_t* __restrict__ counts, int32_t* __restrict__ offse
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst), "l"(src) : "memory");
 }
+// 16 zero bytes at dst through the same asynchronous path (source size 0)
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* any_global) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, 0;" :: "r"(dst), "l"(any_global) : "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }

@@ -131,6 +131,16 @@ __device__ __forceinline__ void named_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(count) : "memory");
 }
 
+// Non-blocking test of the phase with parity `phase` (no suspension).
+__device__ __forceinline__ bool mbar_test(uint64_t* mbar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(mbar)), "r"(phase) : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* mbar, uint32_t phase) {
   uint32_t ok;
   asm volatile(
