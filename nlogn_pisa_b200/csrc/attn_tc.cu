@@ -123,7 +123,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 //   last warp        MMA issue: S(i+1) = Q K^T is issued before O(i) = P V
 // mbarriers per stage/buffer: q_full/q_empty (query stages), s_full, p_full,
 // o_full, acc_empty (TMEM buffer of S, P and O).  All waits are bounded.
-constexpr int kEpiWarps = 8, kLoadWarps = 4, kMmaWarp = kEpiWarps + kLoadWarps, kStages = 3, kGroup = 8;
+constexpr int kEpiWarps = 8, kLoadWarps = 8, kMmaWarp = kEpiWarps + kLoadWarps, kStages = 3, kGroup = 8;
 constexpr int kRowsPerLoader = 128 / kLoadWarps;  // tile rows per producer warp
 constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
 

@@ -29,8 +29,6 @@ namespace pisa {
 
 namespace {
 
-constexpr int kLeafThreads = 128;
-
 __device__ __forceinline__ void decode_row(int64_t row, int T, int H, int& b, int& t, int& h) {
   h = int(row % H);
   t = int((row / H) % T);
@@ -80,13 +78,15 @@ __global__ void family_scatter_kernel(const GroupArgs g, const int32_t* __restri
 // Warp roles of the pipelined tile kernel (one persistent CTA per SM):
 //   warps 0-7   epilogue: warp w reads TMEM lanes 32*(w%4).. (one query-head
 //               row per thread) and handles half of the b children
-//   warps 8-11  producers: gather the tile's query rows into a 2-stage ring,
-//               restage the family keys when the bucket changes
-//   warp 12     MMA issue (one thread): tile i accumulates into TMEM buffer i%2
+//   next kLoadWarps warps  producers: gather the tile's query rows into a
+//               3-stage ring (cp.async), restage the family keys (TMA) when the
+//               bucket changes
+//   last warp   MMA issue (one thread): tile i accumulates into TMEM buffer i%2
 // mbarriers: full_q/empty_q guard the query stages, full_acc/empty_acc the
 // accumulators; the parity of round r is r & 1 (empty waits start at 1, so the
 // first round passes).  Every wait is bounded and records a timeout status.
-constexpr int kEpiWarps = 8, kLoadWarps = 1, kMmaWarp = 9, kStages = 3, kGroup = 8;
+constexpr int kEpiWarps = 8, kLoadWarps = 4, kMmaWarp = kEpiWarps + kLoadWarps, kStages = 3, kGroup = 8;
+constexpr int kRowsPerLoader = 128 / kLoadWarps;  // tile rows per producer warp
 constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
 
 template <typename T>
@@ -95,7 +95,6 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int Dp = g.Dp;                       // padded head_dim: 64, 128 or 256
   const int chunks = Dp / 64;                // 128-byte K chunks per row
-  const int vpr = Dp / 8;                    // 16-byte vectors per row (divides 128)
   const int NK = g.br * g.C;                 // keys per family = MMA N
   const int q_stage_bytes = chunks * 128 * 128;
   uint8_t* Ks = smem + kStages * q_stage_bytes;    // [chunks][NK][128 B]
@@ -123,14 +122,15 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
 
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
-      tc::mbar_init(&full_q[i], 1);
+      // one cp.async arrival per producer thread + the key arrival of the first producer warp
+      tc::mbar_init(&full_q[i], kLoadWarps * 32 + 1);
       tc::mbar_init(&empty_q[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&full_acc[i], 1);
       tc::mbar_init(&empty_acc[i], kEpiWarps * 32);
     }
-    for (int i = 0; i < 8; ++i) tc::mbar_init(&meta_full[i], 1);
+    for (int i = 0; i < 8; ++i) tc::mbar_init(&meta_full[i], kLoadWarps);
     s_fail = 0;
     tc::fence_barrier_init();
   }
@@ -144,74 +144,83 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
   const int lgG = 31 - __clz(g.G);
 
   if (warp >= kEpiWarps && warp < kMmaWarp) {
-    // ---------------- producer warp: TMA ----------------
-    // Lane j issues request j, j+32, ...: one TMA box (G rows x 64 dims) per
-    // 128-byte chunk into the swizzled layout; a new family's b*C keys (one
-    // box per chunk, zero past the sequence end) count on the same barrier.
+    // ---------------- producer warps ----------------
+    // Query rows move with 16-byte asynchronous copies (cp.async) into their
+    // swizzled K-major positions; each producer thread's copies arrive on the
+    // stage barrier when they land.  Producer warp pw owns kRowsPerLoader
+    // tile rows and lane l decodes the request of its l-th row.  Producer
+    // warp 0 also restages a new family's b*C keys through TMA (one box per
+    // 64-dim chunk, zero past the sequence end); those bytes count on the
+    // same barrier.
+    const int pw = warp - kEpiWarps;
+    const int row = pw * kRowsPerLoader + (lane & (kRowsPerLoader - 1));
+    const int j = row >> lgG, gq = row & (g.G - 1);
+    const int lgS = 31 - __clz(Dp / 8);
+    const int nseg = 1 << lgS, dsegs = g.D / 8;
+    const T* qbase = static_cast<const T*>(g.q);
     int cur_key = -1;
     int owner_next = g.tile_owner[first];
-    int req_next[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int j = lane + 32 * u;
-      req_next[u] = j < g.RT ? g.tile_req[int64_t(first) * g.RT + j] : -1;
-    }
-    const uint32_t rows_bytes = uint32_t(g.G) * 128;
+    int req_next = g.tile_req[int64_t(first) * g.RT + j];
     for (int it = 0; it < ntiles; ++it) {
-      const int tile = tile_of(it), s = it % kStages, rnd = it / kStages;
-      const int owner = owner_next;
-      int req[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) req[u] = req_next[u];
+      const int s = it % kStages, rnd = it / kStages;
+      const int owner = owner_next, req = req_next;
       if (it + 1 < ntiles) {
-        owner_next = g.tile_owner[tile_of(it + 1)];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int j = lane + 32 * u;
-          req_next[u] = j < g.RT ? g.tile_req[int64_t(tile_of(it + 1)) * g.RT + j] : -1;
-        }
+        const int nt = tile_of(it + 1);
+        owner_next = g.tile_owner[nt];
+        req_next = g.tile_req[int64_t(nt) * g.RT + j];
       }
-      if (!tc::mbar_wait(&empty_q[s], (rnd & 1) ^ 1)) { s_fail = 1; break; }
       const int p = owner % g.NP;
       const int h = (owner / g.NP) % g.H;
       const int b = owner / (g.NP * g.H * g.nwin);
-      const int kkey = (b * g.H + h) * g.NP + p;
-      uint32_t bytes = 0;
-      if (kkey != cur_key) {
-        // the previous tile's MMA must be done before its keys are replaced
-        if (it > 0 && !tc::mbar_wait(&empty_q[(it - 1) % kStages], ((it - 1) / kStages) & 1)) { s_fail = 1; break; }
-        if (lane < chunks)
-          tc::tma_load_4d(ks_addr + lane * NK * 128, &g.tm_k, lane * 64, h, p * NK, b, &full_q[s]);
-        bytes += uint32_t(chunks) * NK * 128;
-        cur_key = kkey;
+      const T* src = nullptr;
+      int dst = -1;
+      if (req >= 0) {
+        const int rowid = req / g.NF;
+        const int hh = rowid % g.H, t = (rowid / g.H) % g.T, bb = rowid / (g.H * g.T);
+        dst = rowid * g.W0 + (req - rowid * g.NF) * g.br;
+        src = qbase + int64_t(bb) * g.q_sb + int64_t(t) * g.q_st + int64_t(hh * g.G + gq) * g.q_sh;
       }
-      const int slot = it & 7;
-      const uint32_t qa = qs_addr + s * q_stage_bytes;
-      int nreq = 0;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = lane + 32 * u;
-        if (j >= g.RT) break;
-        int dst = -1;
-        if (req[u] >= 0) {
-          const int rowid = req[u] / g.NF;
-          const int hh = rowid % g.H, t = (rowid / g.H) % g.T, bb = rowid / (g.H * g.T);
-          dst = rowid * g.W0 + (req[u] - rowid * g.NF) * g.br;
-          for (int kc = 0; kc < chunks; ++kc)
-            tc::tma_load_4d(qa + kc * 128 * 128 + j * rows_bytes, &g.tm_q, kc * 64, hh * g.G, t, bb, &full_q[s]);
-          ++nreq;
+      if (!tc::mbar_wait(&empty_q[s], (rnd & 1) ^ 1)) { s_fail = 1; break; }
+      // rows of empty request slots are left as they are (their scores are
+      // never written); dimensions past D are zero-filled
+      const uint32_t stage = qs_addr + s * q_stage_bytes;
+      for (int u = 0; u < (kRowsPerLoader << lgS) / 32; ++u) {
+        const int f = u * 32 + lane;
+        const int rl = f >> lgS, seg = f & (nseg - 1);
+        const T* rs = reinterpret_cast<const T*>(__shfl_sync(kFull, reinterpret_cast<uintptr_t>(src), rl));
+        if (rs != nullptr) {
+          const int r = pw * kRowsPerLoader + rl, kc = seg >> 3, c = seg & 7;
+          const uint32_t dsta = stage + kc * 128 * 128 + r * 128 + ((c ^ (r & 7)) << 4);
+          if (seg < dsegs) cp_async16(dsta, rs + seg * 8);
+          else cp_async16_zfill(dsta, qbase);
         }
-        s_dst[slot][j] = dst;
       }
-      const int total_req = __reduce_add_sync(kFull, nreq);
+      tc::cp_async_arrive(&full_q[s]);
+      const int slot = it & 7;
+      if (gq == 0 && lane < kRowsPerLoader) s_dst[slot][j] = dst;
+      uint32_t bytes = 0;
+      if (pw == 0) {
+        const int kkey = (b * g.H + h) * g.NP + p;
+        if (kkey != cur_key) {
+          // the previous tile's MMA must be done before its keys are replaced
+          if (it > 0 && !tc::mbar_wait(&empty_q[(it - 1) % kStages], ((it - 1) / kStages) & 1)) { s_fail = 1; break; }
+          if (lane < chunks)
+            tc::tma_load_4d(ks_addr + lane * NK * 128, &g.tm_k, lane * 64, h, p * NK, b, &full_q[s]);
+          bytes = uint32_t(chunks) * NK * 128;
+          cur_key = kkey;
+        }
+      }
       __syncwarp();
       if (lane == 0) {
-        s_fam[slot] = p;
-        tc::mbar_arrive_expect_tx(&full_q[s], bytes + uint32_t(total_req) * chunks * rows_bytes);
+        if (pw == 0) {
+          s_fam[slot] = p;
+          tc::mbar_arrive_expect_tx(&full_q[s], bytes);
+        }
         tc::mbar_arrive(&meta_full[slot]);
       }
       __syncwarp();
     }
+    cp_async_wait_all();
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issue ----------------
     if (lane == 0) {
