@@ -17,7 +17,8 @@
  *    throws across the ABI.  pisa_last_error() describes the last failure of
  *    the calling thread.
  *  - Workspaces are caller-allocated; the *_workspace_bytes functions give the
- *    size.  The library allocates no device memory of its own.
+ *    size.  The library makes no device allocation calls; the only device
+ *    memory it holds is the fixed scratch of pisa_sparse_attn_bwd_noalloc.
  */
 #ifndef PISA_B200_H
 #define PISA_B200_H
@@ -183,6 +184,32 @@ PISA_API int pisa_sparse_attn_bwd(const void *q, const void *k, const void *v, c
 
 PISA_API int64_t pisa_sparse_attn_bwd_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H,
                                              int64_t D, int64_t Dv, int64_t N);
+
+/*
+ * pisa_sparse_attn_bwd without a caller workspace, for callers that cannot
+ * allocate device memory (a host runtime bound to this C ABI that owns only
+ * the tensors it passes, or a framework whose device memory is planned in
+ * advance).  No counterpart in the reference.  The fp32 dK/dV accumulators
+ * live in a fixed device array inside the library:
+ * pisa_sparse_attn_bwd_noalloc_max_bytes() bytes (32 MiB) on every GPU that
+ * loads the library, held until the process exits; shapes needing more
+ * (B*N*H*(D+Dv) above 8M values) return PISA_ERR_UNSUPPORTED.  The first call
+ * on a device looks up the array's device address (set-up); make that first
+ * call before any stream capture.  Every call uses the same array and clears
+ * it on `stream` first, so calls that overlap on the GPU (other streams,
+ * other host threads) race.  Arguments as pisa_sparse_attn_bwd.  Allocates
+ * nothing.
+ */
+PISA_API int pisa_sparse_attn_bwd_noalloc(const void *q, const void *k, const void *v, const void *out,
+                                          const void *dout, const float *lse, const void *indices,
+                                          int index_bytes, const int64_t *positions,
+                                          int64_t position_offset, int dtype, int64_t B, int64_t Tq,
+                                          int64_t Hq, int64_t H, int64_t D, int64_t Dv, int64_t N,
+                                          int64_t S, int64_t block_size, float scale, int causal,
+                                          void *dq, void *dk, void *dv, pisa_stream_t stream);
+
+/* Size of the fixed scratch of pisa_sparse_attn_bwd_noalloc, in bytes. */
+PISA_API int64_t pisa_sparse_attn_bwd_noalloc_max_bytes(void);
 
 /* ---- per-kernel device timing (profiling aid; the reference has no counterpart) ----
  * With timing on, the library records a pair of CUDA events on the launch

@@ -43,6 +43,9 @@ SIGNATURES = {
     "pisa_sparse_attn_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _L, _I, _L, _L, _L, _L, _L,
                                   _L, _L, _L, _L, _F, _I, _P, _P, _P, _P, _L, _P]),
     "pisa_sparse_attn_bwd_workspace_bytes": (_L, [_L, _L, _L, _L, _L, _L, _L]),
+    "pisa_sparse_attn_bwd_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _L, _I, _L, _L, _L, _L, _L,
+                                          _L, _L, _L, _L, _F, _I, _P, _P, _P, _P]),
+    "pisa_sparse_attn_bwd_noalloc_max_bytes": (_L, []),
     "pisa_launch_count": (_L, []),
     "pisa_kernel_timing": (_I, [_I]),
     "pisa_kernel_time": (_I, [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
