@@ -121,6 +121,17 @@ def profiled_traffic(kernel, workload):
 # ---------------------------------------------------------------------------
 # the reference arm: CPU restatement on a bounded sample
 # ---------------------------------------------------------------------------
+def arm_config(w, world):
+    """The `config` object of both arms' JSON lines."""
+    return {
+        "workload": w.name, "batch_per_gpu": w.batch, "tokens": w.tokens, "q_heads": w.q_heads,
+        "kv_heads": w.kv_heads, "head_dim": w.head_dim, "block_size": w.block_size, "branching": w.branching,
+        "topk": w.topk, "method": w.method, "forced": "first + current block", "schedule": "grouped",
+        "l2": "flushed between timed steps (256 MiB write outside the events)",
+        "parallelism": f"dp{world} (one sequence per GPU, no collective)",
+    }
+
+
 def run_reference(args, workload):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -131,7 +142,7 @@ def run_reference(args, workload):
     samples = []
     for _ in range(args.warmup):
         time_sample(workload, rows_per_worker=2)
-    for _ in range(max(1, min(args.steps, 3))):
+    for _ in range(max(1, args.steps)):
         samples.append(time_sample(workload, rows_per_worker=args.cpu_rows))
     value = statistics.median(s["value"] for s in samples)
     base = samples[0]
@@ -141,7 +152,7 @@ def run_reference(args, workload):
         "value": value,
         "unit": "tokens/s",
         "n_gpus": args.gpus,
-        "steps": len(samples),
+        "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": 1000.0 * workload.tokens / value,
         "higher_is_better": True,
@@ -149,7 +160,7 @@ def run_reference(args, workload):
         "vs_baseline": None,
         "dtype": workload.dtype,
         "data": "synthetic",
-        "config": {"workload": workload.name, **workload.as_dict()},
+        "config": arm_config(workload, int(os.environ.get("WORLD_SIZE", "1"))),
         "cpu_baseline": {k: base[k] for k in ("unit", "cores", "kind", "sample")} | {"value": value},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -377,13 +388,7 @@ def main():
             "vs_baseline": None,
             "dtype": w.dtype,
             "data": "synthetic",
-            "config": {
-                "workload": w.name, "batch_per_gpu": B, "tokens": N, "q_heads": Hq, "kv_heads": H,
-                "head_dim": D, "block_size": C, "branching": br, "topk": K, "method": w.method,
-                "forced": "first + current block", "schedule": "grouped",
-                "l2": "flushed between timed steps (256 MiB write outside the events)",
-                "parallelism": f"dp{world} (one sequence per GPU, no collective)",
-            },
+            "config": arm_config(w, world),
             "roofline": {"kernel": dom["kernel"], "bound": dom["bound"], "achieved": dom["achieved"],
                          "peak": dom["peak"], "unit": dom["unit"], "frac": dom["frac"],
                          "traffic": profiled_traffic(dominant, w.name),
