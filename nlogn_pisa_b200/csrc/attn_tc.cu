@@ -42,11 +42,11 @@ __device__ __forceinline__ Req decode_req(int64_t lr64, const AttnTcArgs& a) {
   // chunk-local request indices are below 2^31 (checked on the host)
   const uint32_t lr = uint32_t(lr64);
   Req r;
-  uint32_t row = lr / uint32_t(a.S);
+  const uint32_t row = a.fS.div(lr);
   r.s = int(lr - row * uint32_t(a.S));
-  uint32_t rest = row / uint32_t(a.H);
+  const uint32_t rest = a.fH.div(row);
   r.h = int(row - rest * uint32_t(a.H));
-  const uint32_t b = rest / uint32_t(a.tlen);
+  const uint32_t b = a.ftlen.div(rest);
   r.tl = int(rest - b * uint32_t(a.tlen));
   r.b = int(b);
   return r;
@@ -65,7 +65,7 @@ __device__ __forceinline__ int64_t visible_block(const AttnTcArgs& a, int b, int
 }
 
 __device__ __forceinline__ int64_t bucket_of(const AttnTcArgs& a, const Req& r, int64_t id) {
-  return ((int64_t(r.b) * a.nwin + r.tl / a.TW) * a.H + r.h) * a.NB + id;
+  return ((int64_t(r.b) * a.nwin + int(a.fTW.div(uint32_t(r.tl)))) * a.H + r.h) * a.NB + id;
 }
 
 __global__ void attn_count_kernel(const AttnTcArgs a) {
@@ -85,10 +85,11 @@ __global__ void attn_scatter_kernel(const AttnTcArgs a) {
   if (id < 0) return;
   const int64_t bucket = bucket_of(a, r, id);
   const int pos = atomicAdd(a.cursors + bucket, 1);
-  const int64_t tile = a.offsets[bucket] + pos / a.RT;
-  a.tile_req[tile * a.RT + pos % a.RT] = int32_t(lr);
-  a.tile_pos[lr] = int32_t(tile * a.RT + pos % a.RT);
-  if (pos % a.RT == 0) a.tile_owner[tile] = int32_t(bucket);
+  const int q = int(a.fRT.div(uint32_t(pos))), slot = pos - q * a.RT;
+  const int64_t tile = a.offsets[bucket] + q;
+  a.tile_req[tile * a.RT + slot] = int32_t(lr);
+  a.tile_pos[lr] = int32_t(tile * a.RT + slot);
+  if (slot == 0) a.tile_owner[tile] = int32_t(bucket);
 }
 
 // 32-byte streaming store / load (partials are written once and read once)
@@ -170,9 +171,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&s_full[i], 1);
-      tc::mbar_init(&p_full[i], 128);
+      tc::mbar_init(&p_full[i], 4);     // one arrival per epilogue warp of the group
       tc::mbar_init(&o_full[i], 1);
-      tc::mbar_init(&o_empty[i], 128);
+      tc::mbar_init(&o_empty[i], 4);
     }
     for (int i = 0; i < 8; ++i) tc::mbar_init(&meta_full[i], kLoadWarps);
     s_fail = 0;
@@ -210,22 +211,18 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
     const T* qbase = static_cast<const T*>(a.q);
     int64_t cur_kv = -1;
     int kvb = 1, used0 = 0, used1 = 0;
-    int owner_next = a.tile_owner[first];
-    int req_next = a.tile_req[int64_t(first) * a.RT + j];
-    for (int it = 0; it < ntiles; ++it) {
-      const int s = it % nst, rnd = it / nst;
-      const int owner = owner_next, req = req_next;
-      if (it + 1 < ntiles) {
-        const int nt = tile_of(it + 1);
-        owner_next = a.tile_owner[nt];
-        req_next = a.tile_req[int64_t(nt) * a.RT + j];
-      }
-      const int blk = owner % a.NB;
-      const int h = (owner / a.NB) % a.H;
-      const int b = owner / (a.NB * a.H * a.nwin);
-      // source row of this lane, valid keys of its request
-      const T* src = nullptr;
-      int nv = 0;
+    // request of this lane's row in tile `it`: K/V block coordinates, source
+    // row and valid keys; decoded one tile ahead, while the copies of the
+    // previous tile drain
+    int blk = 0, h = 0, b = 0, nv = 0;
+    const T* src = nullptr;
+    auto decode = [&](int owner, int req) {
+      const uint32_t o1 = a.fNB.div(uint32_t(owner)), o2 = a.fH.div(o1);
+      blk = owner - int(o1) * a.NB;
+      h = int(o1) - int(o2) * a.H;
+      b = int(a.fnwin.div(o2));
+      src = nullptr;
+      nv = 0;
       if (req >= 0) {
         const Req q = decode_req(req, a);
         const int t = a.t0 + q.tl;
@@ -234,6 +231,17 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
         nv = int(max(int64_t(0), min64(int64_t(a.C), limit - int64_t(blk) * a.C)));
         src = qbase + int64_t(q.b) * a.q_sb + int64_t(t) * a.q_st + int64_t(q.h * a.G + gq) * a.q_sh;
       }
+      return req;
+    };
+    int req = decode(a.tile_owner[first], a.tile_req[int64_t(first) * a.RT + j]);
+    // the next tile's owner and request index are loaded one iteration early
+    int owner_n = 0, req_n = -1;
+    if (ntiles > 1) {
+      owner_n = a.tile_owner[tile_of(1)];
+      req_n = a.tile_req[int64_t(tile_of(1)) * a.RT + j];
+    }
+    for (int it = 0; it < ntiles; ++it) {
+      const int s = it % nst, rnd = it / nst;
       if (!tc::mbar_wait(&q_empty[s], (rnd & 1) ^ 1)) { s_fail = 1; break; }
       // rows of requests without a visible block are left as they are: their
       // results are never read.  Dimensions past D are zero-filled.
@@ -286,6 +294,13 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
         tc::mbar_arrive(&meta_full[slot]);
       }
       __syncwarp();
+      if (it + 1 < ntiles) {
+        req = decode(owner_n, req_n);
+        if (it + 2 < ntiles) {
+          owner_n = a.tile_owner[tile_of(it + 2)];
+          req_n = a.tile_req[int64_t(tile_of(it + 2)) * a.RT + j];
+        }
+      }
     }
     cp_async_wait_all();
   } else if (warp == kMmaWarp) {
@@ -439,8 +454,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
         }
       }
       }
+      // one arrival per warp once all its lanes' TMEM stores are done
       tc::fence_before_sync();
-      tc::mbar_arrive(&p_full[ab]);
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&p_full[ab]);
       const bool got2 = tc::mbar_wait(&o_full[ab], rnd & 1);
       if (!got2) s_fail = 1;
       tc::fence_after_sync();
@@ -463,7 +480,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
       __stcs(reinterpret_cast<float2*>(a.part_ml) + int64_t(tile) * 128 + row,
              make_float2(req >= 0 ? mx * a.scale : -INFINITY, l));
       tc::fence_before_sync();
-      tc::mbar_arrive(&o_empty[ab]);
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&o_empty[ab]);
       if (!got || !got2) break;
     }
   }
@@ -483,9 +501,10 @@ __global__ void __launch_bounds__(128) attn_combine_tiles_kernel(const AttnTcArg
   const int64_t idx = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (idx >= int64_t(a.B) * a.tlen * a.Hq) return;
-  const int hq = int(idx % a.Hq);
-  const int tl = int((idx / a.Hq) % a.tlen);
-  const int b = int(idx / (int64_t(a.Hq) * a.tlen));
+  const uint32_t i1 = a.fHq.div(uint32_t(idx)), i2 = a.ftlen.div(i1);
+  const int hq = int(uint32_t(idx) - i1 * uint32_t(a.Hq));
+  const int tl = int(i1 - i2 * uint32_t(a.tlen));
+  const int b = int(i2);
   const int h = hq / a.G, g = hq % a.G;
   const int t = a.t0 + tl;
   const int64_t slot0 = ((int64_t(b) * a.tlen + tl) * a.H + h) * a.S;
@@ -499,7 +518,7 @@ __global__ void __launch_bounds__(128) attn_combine_tiles_kernel(const AttnTcArg
     const int sl = lane + 32 * k;
     if (sl < a.S && visible_block(a, b, t, h, sl) >= 0) {
       const int pos = a.tile_pos[slot0 + sl];
-      const int tile = pos / a.RT, r = pos - tile * a.RT;
+      const int tile = int(a.fRT.div(uint32_t(pos))), r = pos - tile * a.RT;
       prow[k] = tile * 128 + r * a.G + g;
       const float2 ml = __ldcs(part_ml + prow[k]);
       if (ml.y > 0.f) { m_s[k] = ml.x; l_s[k] = ml.y; }
@@ -563,10 +582,18 @@ int attn_tc_typed(AttnTcArgs a, cudaStream_t stream) {
   const size_t smem = size_t(a.nstages) * 128 * 128 * qch + size_t(2) * a.C * 128 * (qch + vch) + 1024;
   cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return fail_cuda(e, "attention smem attribute");
+  a.fS = FastDiv::make(uint32_t(a.S));
+  a.fH = FastDiv::make(uint32_t(a.H));
+  a.fHq = FastDiv::make(uint32_t(a.Hq));
+  a.fNB = FastDiv::make(uint32_t(a.NB));
+  a.fTW = FastDiv::make(uint32_t(a.TW));
+  a.fRT = FastDiv::make(uint32_t(a.RT));
   for (int t0 = 0; t0 < a.T; t0 += a.chunk) {
     a.t0 = t0;
     a.tlen = std::min(a.chunk, a.T - t0);
     a.nwin = (a.tlen + a.TW - 1) / a.TW;
+    a.ftlen = FastDiv::make(uint32_t(a.tlen));
+    a.fnwin = FastDiv::make(uint32_t(a.nwin));
     a.num_buckets = int64_t(a.B) * a.nwin * a.H * a.NB;
     const int64_t reqs = int64_t(a.B) * a.tlen * a.H * a.S;
     a.capacity = (reqs + a.RT - 1) / a.RT + a.num_buckets;

@@ -242,7 +242,8 @@ static SelectPlan plan_select(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int6
     p.rows = B * Tq * H;
     p.num_buckets = B * p.nwin * H * p.NP;
     p.capacity = (p.rows * p.NF + p.RT - 1) / p.RT + p.num_buckets;
-    if (p.rows * p.NF >= (int64_t(1) << 31)) p.grouped_tc = false;
+    // request and score-slot indices are decoded as 31-bit numbers
+    if (p.rows * p.W0 >= (int64_t(1) << 31) || p.capacity * p.RT >= (int64_t(1) << 31)) p.grouped_tc = false;
   }
   if (p.grouped_tc) {
     const int64_t slots = p.rows * p.W0;
@@ -476,8 +477,10 @@ static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t 
   const int64_t nwin = (p.chunk + p.TW - 1) / p.TW;
   p.num_buckets = B * nwin * H * p.NB;
   const int64_t reqs = B * p.chunk * H * S;
-  if (reqs >= (int64_t(1) << 31)) { p.tc = false; return p; }
+  if (reqs >= (int64_t(1) << 31) || B * p.chunk * Hq >= (int64_t(1) << 31)) { p.tc = false; return p; }
   p.capacity = (reqs + p.RT - 1) / p.RT + p.num_buckets;
+  // tile slots (tile * RT + slot) are decoded as 31-bit numbers
+  if (p.capacity * p.RT >= (int64_t(1) << 31)) { p.tc = false; return p; }
   int64_t off = 0;
   p.counts_off = off; off += align_up(p.num_buckets * 4, 256);
   p.cursors_off = off; off += align_up(p.num_buckets * 4, 256);

@@ -11,6 +11,26 @@
 namespace pisa {
 
 constexpr unsigned kFull = 0xffffffffu;
+
+// Division of 31-bit unsigned numerators by a divisor fixed for a launch,
+// by multiply-high and shift (Granlund and Montgomery, "Division by
+// invariant integers using multiplication", 1994): with s = ceil(log2 d) and
+// m = floor(2^32 * (2^s - d) / d) + 1, n / d = (umulhi(n, m) + n) >> s for
+// n < 2^31.  Keeps integer division off the MUFU pipe, which the softmax
+// exponentials of the tile kernels keep busy.
+struct FastDiv {
+  uint32_t d = 1, m = 1, s = 0;
+  __host__ static FastDiv make(uint32_t divisor) {
+    FastDiv f;
+    f.d = divisor < 1 ? 1 : divisor;
+    f.s = 0;
+    while ((uint64_t(1) << f.s) < f.d) ++f.s;
+    f.m = uint32_t(((uint64_t(1) << 32) * ((uint64_t(1) << f.s) - f.d)) / f.d + 1);
+    return f;
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const { return (__umulhi(n, m) + n) >> s; }
+  __device__ __forceinline__ uint32_t mod(uint32_t n) const { return n - div(n) * d; }
+};
 constexpr float kNegFill = -1.0e9f;  // invalid candidates (top_k_pyramid_torch.py:170)
 constexpr float kPosFill = 1.0e9f;   // forced candidates (top_k_pyramid_torch.py:171)
 constexpr int kMaxLevels = 32;

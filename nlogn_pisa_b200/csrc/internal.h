@@ -112,6 +112,8 @@ struct GroupArgs {
   int tiles_per_cta;
   int tmem_cols;
   int num_sms;
+  // divisors of the index decodes (set by the launcher from the fields above)
+  FastDiv fNF, fH, fT, fNP, fTW, fRT, fbr, fnwin;
   int64_t* out_ids;
   int* status;
 };
@@ -196,6 +198,8 @@ struct AttnTcArgs {
   int32_t* tile_pos;  // chunk-local request -> tile * RT + slot
   int64_t capacity;
   int tiles_per_cta, tmem_cols, sp_cols, o_cols, nacc, nstages, num_sms;
+  // divisors of the index decodes (set by the launcher from the fields above)
+  FastDiv fS, fH, fHq, fNB, fTW, fRT, ftlen, fnwin;
   void* part_o;
   float* part_ml;
   void* out;

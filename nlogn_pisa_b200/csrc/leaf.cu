@@ -29,10 +29,12 @@ namespace pisa {
 
 namespace {
 
-__device__ __forceinline__ void decode_row(int64_t row, int T, int H, int& b, int& t, int& h) {
-  h = int(row % H);
-  t = int((row / H) % T);
-  b = int(row / (int64_t(H) * T));
+// (batch, token, KV head) of a row index b*T*H + t*H + h (rows < 2^31)
+__device__ __forceinline__ void decode_row(const GroupArgs& g, uint32_t row, int& b, int& t, int& h) {
+  const uint32_t r1 = g.fH.div(row), r2 = g.fT.div(r1);
+  h = int(row - r1 * uint32_t(g.H));
+  t = int(r1 - r2 * uint32_t(g.T));
+  b = int(r2);
 }
 
 // Requests: one per (row, family) with at least one scoreable child.
@@ -40,16 +42,16 @@ __global__ void family_count_kernel(const GroupArgs g, int32_t* __restrict__ cou
   const int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
   const int64_t total = int64_t(g.B) * g.T * g.H * g.NF;
   if (idx >= total) return;
-  const int64_t row = idx / g.NF;
-  const int k = int(idx % g.NF);
-  const uint8_t* f = g.flags + row * g.W0 + k * g.br;
+  const uint32_t row = g.fNF.div(uint32_t(idx));
+  const int k = int(uint32_t(idx) - row * uint32_t(g.NF));
+  const uint8_t* f = g.flags + int64_t(row) * g.W0 + k * g.br;
   bool active = false;
   for (int j = 0; j < g.br; ++j) active |= (f[j] & 4) != 0;
   if (!active) return;
   int b, t, h;
-  decode_row(row, g.T, g.H, b, t, h);
-  const int p = g.cand[row * g.W0 + k * g.br] / g.br;
-  const int64_t bucket = ((int64_t(b) * g.nwin + t / g.TW) * g.H + h) * g.NP + p;
+  decode_row(g, row, b, t, h);
+  const int p = int(g.fbr.div(uint32_t(g.cand[int64_t(row) * g.W0 + k * g.br])));
+  const int64_t bucket = ((int64_t(b) * g.nwin + int(g.fTW.div(uint32_t(t)))) * g.H + h) * g.NP + p;
   atomicAdd(counts + bucket, 1);
 }
 
@@ -59,20 +61,21 @@ __global__ void family_scatter_kernel(const GroupArgs g, const int32_t* __restri
   const int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
   const int64_t total = int64_t(g.B) * g.T * g.H * g.NF;
   if (idx >= total) return;
-  const int64_t row = idx / g.NF;
-  const int k = int(idx % g.NF);
-  const uint8_t* f = g.flags + row * g.W0 + k * g.br;
+  const uint32_t row = g.fNF.div(uint32_t(idx));
+  const int k = int(uint32_t(idx) - row * uint32_t(g.NF));
+  const uint8_t* f = g.flags + int64_t(row) * g.W0 + k * g.br;
   bool active = false;
   for (int j = 0; j < g.br; ++j) active |= (f[j] & 4) != 0;
   if (!active) return;
   int b, t, h;
-  decode_row(row, g.T, g.H, b, t, h);
-  const int p = g.cand[row * g.W0 + k * g.br] / g.br;
-  const int64_t bucket = ((int64_t(b) * g.nwin + t / g.TW) * g.H + h) * g.NP + p;
+  decode_row(g, row, b, t, h);
+  const int p = int(g.fbr.div(uint32_t(g.cand[int64_t(row) * g.W0 + k * g.br])));
+  const int64_t bucket = ((int64_t(b) * g.nwin + int(g.fTW.div(uint32_t(t)))) * g.H + h) * g.NP + p;
   const int pos = atomicAdd(cursors + bucket, 1);
-  const int64_t tile = offsets[bucket] + pos / g.RT;
-  tile_req[tile * g.RT + pos % g.RT] = int32_t(idx);
-  if (pos % g.RT == 0) tile_owner[tile] = int32_t(bucket);
+  const int q = int(g.fRT.div(uint32_t(pos))), r = pos - q * g.RT;
+  const int64_t tile = offsets[bucket] + q;
+  tile_req[tile * g.RT + r] = int32_t(idx);
+  if (r == 0) tile_owner[tile] = int32_t(bucket);
 }
 
 // Warp roles of the pipelined tile kernel (one persistent CTA per SM):
@@ -128,7 +131,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&full_acc[i], 1);
-      tc::mbar_init(&empty_acc[i], kEpiWarps * 32);
+      tc::mbar_init(&empty_acc[i], kEpiWarps);
     }
     for (int i = 0; i < 8; ++i) tc::mbar_init(&meta_full[i], kLoadWarps);
     s_fail = 0;
@@ -159,27 +162,35 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
     const int nseg = 1 << lgS, dsegs = g.D / 8;
     const T* qbase = static_cast<const T*>(g.q);
     int cur_key = -1;
-    int owner_next = g.tile_owner[first];
-    int req_next = g.tile_req[int64_t(first) * g.RT + j];
-    for (int it = 0; it < ntiles; ++it) {
-      const int s = it % kStages, rnd = it / kStages;
-      const int owner = owner_next, req = req_next;
-      if (it + 1 < ntiles) {
-        const int nt = tile_of(it + 1);
-        owner_next = g.tile_owner[nt];
-        req_next = g.tile_req[int64_t(nt) * g.RT + j];
-      }
-      const int p = owner % g.NP;
-      const int h = (owner / g.NP) % g.H;
-      const int b = owner / (g.NP * g.H * g.nwin);
-      const T* src = nullptr;
-      int dst = -1;
+    // request of this lane's row in tile `it` (family coordinates, source
+    // row, score slot), decoded one tile ahead while the previous tile's
+    // copies drain
+    int p = 0, h = 0, b = 0, dst = -1;
+    const T* src = nullptr;
+    auto decode = [&](int owner, int req) {
+      const uint32_t o1 = g.fNP.div(uint32_t(owner)), o2 = g.fH.div(o1);
+      p = owner - int(o1) * g.NP;
+      h = int(o1) - int(o2) * g.H;
+      b = int(g.fnwin.div(o2));
+      src = nullptr;
+      dst = -1;
       if (req >= 0) {
-        const int rowid = req / g.NF;
-        const int hh = rowid % g.H, t = (rowid / g.H) % g.T, bb = rowid / (g.H * g.T);
+        const int rowid = int(g.fNF.div(uint32_t(req)));
+        int bb, t, hh;
+        decode_row(g, uint32_t(rowid), bb, t, hh);
         dst = rowid * g.W0 + (req - rowid * g.NF) * g.br;
         src = qbase + int64_t(bb) * g.q_sb + int64_t(t) * g.q_st + int64_t(hh * g.G + gq) * g.q_sh;
       }
+    };
+    decode(g.tile_owner[first], g.tile_req[int64_t(first) * g.RT + j]);
+    // the next tile's owner and request index are loaded one iteration early
+    int owner_n = 0, req_n = -1;
+    if (ntiles > 1) {
+      owner_n = g.tile_owner[tile_of(1)];
+      req_n = g.tile_req[int64_t(tile_of(1)) * g.RT + j];
+    }
+    for (int it = 0; it < ntiles; ++it) {
+      const int s = it % kStages, rnd = it / kStages;
       if (!tc::mbar_wait(&empty_q[s], (rnd & 1) ^ 1)) { s_fail = 1; break; }
       // rows of empty request slots are left as they are (their scores are
       // never written); dimensions past D are zero-filled
@@ -219,6 +230,13 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
         tc::mbar_arrive(&meta_full[slot]);
       }
       __syncwarp();
+      if (it + 1 < ntiles) {
+        decode(owner_n, req_n);
+        if (it + 2 < ntiles) {
+          owner_n = g.tile_owner[tile_of(it + 2)];
+          req_n = g.tile_req[int64_t(tile_of(it + 2)) * g.RT + j];
+        }
+      }
     }
     cp_async_wait_all();
   } else if (warp == kMmaWarp) {
@@ -316,8 +334,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
         for (int o = 1; o < g.G; o <<= 1) score += __shfl_xor_sync(kFull, score, o);
         if (dst >= 0 && (row & (g.G - 1)) == 0) g.scores[int64_t(dst) + j] = score;
       }
+      // one arrival per warp once all its lanes' TMEM loads are done
       tc::fence_before_sync();
-      tc::mbar_arrive(&empty_acc[a]);
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&empty_acc[a]);
       if (!got) break;
     }
   }
@@ -337,7 +357,7 @@ __global__ void __launch_bounds__(128) leaf_final_kernel(const GroupArgs g) {
   const int64_t rows = int64_t(g.B) * g.T * g.H;
   if (row >= rows) return;
   int b, t, h;
-  decode_row(row, g.T, g.H, b, t, h);
+  decode_row(g, uint32_t(row), b, t, h);
   const int64_t pos = g.positions ? g.positions[int64_t(b) * g.T + t] : g.pos_offset + t;
   constexpr int E = Network<WP>::E;
   float s[E];
@@ -370,7 +390,16 @@ __global__ void __launch_bounds__(128) leaf_final_kernel(const GroupArgs g) {
 
 }  // namespace
 
-int grouped_leaf(const GroupArgs& g, int dtype, cudaStream_t stream) {
+int grouped_leaf(const GroupArgs& args, int dtype, cudaStream_t stream) {
+  GroupArgs g = args;
+  g.fNF = FastDiv::make(uint32_t(g.NF));
+  g.fH = FastDiv::make(uint32_t(g.H));
+  g.fT = FastDiv::make(uint32_t(g.T));
+  g.fNP = FastDiv::make(uint32_t(g.NP));
+  g.fTW = FastDiv::make(uint32_t(g.TW));
+  g.fRT = FastDiv::make(uint32_t(g.RT));
+  g.fbr = FastDiv::make(uint32_t(g.br));
+  g.fnwin = FastDiv::make(uint32_t(g.nwin));
   const int64_t families = int64_t(g.B) * g.T * g.H * g.NF;
   const int64_t rows = int64_t(g.B) * g.T * g.H;
   cudaError_t e;
