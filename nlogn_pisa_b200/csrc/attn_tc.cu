@@ -13,9 +13,9 @@
 //   softmax per row in registers (causal mask by the row's own position),
 //          P = exp(S - m) rounded to the input type, stored back to TMEM
 //   MMA 2  O = P V             (A = P from TMEM, B = V MN-major) -> TMEM
-// and writes the block-local partial (m, l, O / l) of every row.  A combine
-// pass merges the S partials of each query head into the output and its
-// log-sum-exp.  Moving each query row to its blocks once (instead of every
+// and writes the block-local partial (m, l, sum_k e^(s_k - m) v_k) of every
+// row.  A combine pass merges the S partials of each query head into the
+// output and its log-sum-exp.  Moving each query row to its blocks once (instead of every
 // block to every query) cuts the L2->SM traffic by the bucket reuse factor;
 // the token window keeps the gathered query rows L2-resident.  Token chunks
 // bound the partial buffer.
@@ -116,14 +116,14 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 }
 
 // Warp roles (one persistent CTA per SM):
-//   warps 0-3 / 4-7  epilogue groups: group (tile % 2) turns S into P (softmax
-//                    in registers, P back to TMEM) and then O into the partial;
-//                    thread = TMEM lane = query-head row
+//   warps 0-3        softmax: S into P for every tile (registers, P back to
+//                    TMEM) and the row's (m, l); thread = TMEM lane = row
+//   warps 4-7        readout: O of every tile into its block partial
 //   next kLoadWarps  producers: query rows into a 3-stage ring (cp.async),
 //                    block K/V (TMA, first producer warp)
-//   last warp        MMA issue: S(i+1) = Q K^T is issued before O(i) = P V
+//   last warp        MMA issue: S = Q K^T and O = P V, whichever is ready
 // mbarriers per stage/buffer: q_full/q_empty (query stages), s_full, p_full,
-// o_full, acc_empty (TMEM buffer of S, P and O).  All waits are bounded.
+// o_full, o_empty (TMEM buffers of S/P and O).  All waits are bounded.
 constexpr int kEpiWarps = 8, kLoadWarps = 8, kMmaWarp = kEpiWarps + kLoadWarps, kStages = 3, kGroup = 8;
 constexpr int kRowsPerLoader = 128 / kLoadWarps;  // tile rows per producer warp
 constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
@@ -162,6 +162,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
   const int first = tile_of(0);
   const int nacc = a.nacc;                    // S/P and O buffers: 2 (double) or 1
   const int nst = a.nstages;                  // query stages: 3 or 2
+  // stage of tile i and the parity of its round (constant divisors only)
+  auto stage_of = [&](int i) { return nst == 3 ? i % 3 : (i & 1); };
+  auto round_par = [&](int i) { return (nst == 3 ? i / 3 : (i >> 1)) & 1; };
 
   if (tid == 0) {
     for (int i = 0; i < nst; ++i) {
@@ -241,8 +244,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
       req_n = a.tile_req[int64_t(tile_of(1)) * a.RT + j];
     }
     for (int it = 0; it < ntiles; ++it) {
-      const int s = it % nst, rnd = it / nst;
-      if (!tc::mbar_wait(&q_empty[s], (rnd & 1) ^ 1)) { s_fail = 1; break; }
+      const int s = stage_of(it), rpar = round_par(it);
+      if (!tc::mbar_wait(&q_empty[s], rpar ^ 1)) { s_fail = 1; break; }
       // rows of requests without a visible block are left as they are: their
       // results are never read.  Dimensions past D are zero-filled.
       const uint32_t stage = qs_addr + s * q_stage_bytes;
@@ -311,7 +314,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
       int kv_even = 0, kv_odd = 0;  // K/V buffer of the last even / odd tile
       // S = Q K^T of tile `it` into its S/P buffer (its query stage has landed)
       auto issue_s = [&](int it) {
-        const int s = it % nst, ab = acc_of(it);
+        const int s = stage_of(it), ab = acc_of(it);
         tc::fence_async_smem();
         tc::fence_after_sync();
         const int kvb = s_kvb[s];
@@ -357,7 +360,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
           }
         }
         if (!issued && ns < ntiles && no >= ns - nacc + 1) {
-          if (tc::mbar_test(&q_full[ns % nst], (ns / nst) & 1)) {
+          if (tc::mbar_test(&q_full[stage_of(ns)], round_par(ns))) {
             issue_s(ns++);
             issued = true;
           }
@@ -372,117 +375,125 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue groups ----------------
-    const int grp = warp >> 2, quarter = warp & 3;
+    // ---------------- epilogue: softmax warps 0-3, readout warps 4-7 ----------------
+    // Both roles walk every tile: warps 0-3 turn S into P (and write the
+    // row's (m, l)), warps 4-7 read O out; so the softmax of tile i+1 runs
+    // while tile i's P.V and readout are in flight.
+    const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t(quarter) * 32) << 16;
-    const int r = row >> lgG, g = row & (a.G - 1);
+    const int r = row >> lgG;
     T* part_o = static_cast<T*>(a.part_o);
     const float l2e = 1.4426950408889634f;
     const float sl = a.scale * l2e;
-    // two buffers: group g takes tiles g, g+2, ...; one buffer: group 0 takes all
-    const int step = nacc == 2 ? 2 : 1;
-    for (int it = grp; it < ntiles && (nacc == 2 || grp == 0); it += step) {
-      const int ab = acc_of(it), rnd = round_of(it), tile = tile_of(it);
-      const bool got = tc::mbar_wait(&s_full[ab], rnd & 1);
-      if (!got) s_fail = 1;
-      tc::fence_after_sync();
-      if (!tc::mbar_wait(&meta_full[it & 7], (it >> 3) & 1)) s_fail = 1;
-      const int req = r < a.RT ? s_req[it & 7][r] : -1;
-      const int nvalid = r < a.RT ? s_nv[it & 7][r] : 0;
-      (void)tile;
-      const uint32_t base = tmem + lane_base + ab * a.sp_cols;                 // S, then P at +C
-      const uint32_t obase = tmem + lane_base + nacc * a.sp_cols + ab * a.o_cols;
-      float mx = -INFINITY;
-      float l = 0.f;
-      if (a.C == 64) {
-        // one TMEM load; masked keys -> -inf -> exp 0; packed arithmetic
-        float v[64];
-        tc::tmem_ld64(base, v);
-        if (nvalid < 64) {
+    if (warp < 4) {
+      for (int it = 0; it < ntiles; ++it) {
+        const int ab = acc_of(it), rnd = round_of(it), tile = tile_of(it);
+        const bool got = tc::mbar_wait(&s_full[ab], rnd & 1);
+        if (!got) s_fail = 1;
+        tc::fence_after_sync();
+        if (!tc::mbar_wait(&meta_full[it & 7], (it >> 3) & 1)) s_fail = 1;
+        const int req = r < a.RT ? s_req[it & 7][r] : -1;
+        const int nvalid = r < a.RT ? s_nv[it & 7][r] : 0;
+        const uint32_t base = tmem + lane_base + ab * a.sp_cols;                 // S, then P at +C
+        float mx = -INFINITY;
+        float l = 0.f;
+        if (a.C == 64) {
+          // one TMEM load; masked keys -> -inf -> exp 0; packed arithmetic
+          float v[64];
+          tc::tmem_ld64(base, v);
+          if (nvalid < 64) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) if (i >= nvalid) v[i] = -INFINITY;
-        }
-        mx = tc::max64(v);
-        const float mb = nvalid > 0 ? mx * sl : 0.f;
-        const float2 kk = make_float2(sl, sl), cc = make_float2(-mb, -mb);
-        float2 acc2 = make_float2(0.f, 0.f);
-        uint32_t w[32];
-#pragma unroll
-        for (int i = 0; i < 64; i += 2) {
-          const float2 x = tc::fma2(make_float2(v[i], v[i + 1]), kk, cc);
-          const float2 pr = make_float2(tc::ex2f(x.x), tc::ex2f(x.y));
-          acc2 = tc::add2(acc2, pr);
-          w[i / 2] = pack2<T>(pr.x, pr.y);
-        }
-        l = acc2.x + acc2.y;
-        uint32_t w0[16], w1[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) { w0[i] = w[i]; w1[i] = w[16 + i]; }
-        tc::tmem_st16(base + a.C, w0);
-        tc::tmem_st16(base + a.C + 16, w1);
-      } else {
-      for_columns(base, a.C, [&](int c, float x) {
-        if (c < nvalid) mx = fmaxf(mx, x);
-      });
-      const float mb = mx * sl;
-      for (int c0 = 0; c0 < a.C; c0 += 32) {
-        if (a.C - c0 >= 32) {
-          float v[32];
-          tc::tmem_ld32(base + c0, v);
-          uint32_t w[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float p0 = (c0 + 2 * i < nvalid) ? exp2f(fmaf(v[2 * i], sl, -mb)) : 0.f;
-            const float p1 = (c0 + 2 * i + 1 < nvalid) ? exp2f(fmaf(v[2 * i + 1], sl, -mb)) : 0.f;
-            l += p0 + p1;
-            w[i] = pack2<T>(p0, p1);
+            for (int i = 0; i < 64; ++i) if (i >= nvalid) v[i] = -INFINITY;
           }
-          tc::tmem_st16(base + a.C + c0 / 2, w);
+          mx = tc::max64(v);
+          const float mb = nvalid > 0 ? mx * sl : 0.f;
+          const float2 kk = make_float2(sl, sl), cc = make_float2(-mb, -mb);
+          float2 acc2 = make_float2(0.f, 0.f);
+          uint32_t w[32];
+#pragma unroll
+          for (int i = 0; i < 64; i += 2) {
+            const float2 x = tc::fma2(make_float2(v[i], v[i + 1]), kk, cc);
+            const float2 pr = make_float2(tc::ex2f(x.x), tc::ex2f(x.y));
+            acc2 = tc::add2(acc2, pr);
+            w[i / 2] = pack2<T>(pr.x, pr.y);
+          }
+          l = acc2.x + acc2.y;
+          uint32_t w0[16], w1[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) { w0[i] = w[i]; w1[i] = w[16 + i]; }
+          tc::tmem_st16(base + a.C, w0);
+          tc::tmem_st16(base + a.C + 16, w1);
         } else {
-          float v[16];
-          tc::tmem_ld16(base + c0, v);
-          uint32_t w[8];
+          for_columns(base, a.C, [&](int c, float x) {
+            if (c < nvalid) mx = fmaxf(mx, x);
+          });
+          const float mb = mx * sl;
+          for (int c0 = 0; c0 < a.C; c0 += 32) {
+            if (a.C - c0 >= 32) {
+              float v[32];
+              tc::tmem_ld32(base + c0, v);
+              uint32_t w[16];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float p0 = (c0 + 2 * i < nvalid) ? exp2f(fmaf(v[2 * i], sl, -mb)) : 0.f;
-            const float p1 = (c0 + 2 * i + 1 < nvalid) ? exp2f(fmaf(v[2 * i + 1], sl, -mb)) : 0.f;
-            l += p0 + p1;
-            w[i] = pack2<T>(p0, p1);
+              for (int i = 0; i < 16; ++i) {
+                const float p0 = (c0 + 2 * i < nvalid) ? exp2f(fmaf(v[2 * i], sl, -mb)) : 0.f;
+                const float p1 = (c0 + 2 * i + 1 < nvalid) ? exp2f(fmaf(v[2 * i + 1], sl, -mb)) : 0.f;
+                l += p0 + p1;
+                w[i] = pack2<T>(p0, p1);
+              }
+              tc::tmem_st16(base + a.C + c0 / 2, w);
+            } else {
+              float v[16];
+              tc::tmem_ld16(base + c0, v);
+              uint32_t w[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float p0 = (c0 + 2 * i < nvalid) ? exp2f(fmaf(v[2 * i], sl, -mb)) : 0.f;
+                const float p1 = (c0 + 2 * i + 1 < nvalid) ? exp2f(fmaf(v[2 * i + 1], sl, -mb)) : 0.f;
+                l += p0 + p1;
+                w[i] = pack2<T>(p0, p1);
+              }
+              tc::tmem_st8(base + a.C + c0 / 2, w);
+            }
           }
-          tc::tmem_st8(base + a.C + c0 / 2, w);
         }
+        // the row's block max (scaled) and sum of exponentials
+        __stcs(reinterpret_cast<float2*>(a.part_ml) + int64_t(tile) * 128 + row,
+               make_float2(req >= 0 ? mx * a.scale : -INFINITY, l));
+        // one arrival per warp once all its lanes' TMEM stores are done
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&p_full[ab]);
+        if (!got) break;
       }
-      }
-      // one arrival per warp once all its lanes' TMEM stores are done
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&p_full[ab]);
-      const bool got2 = tc::mbar_wait(&o_full[ab], rnd & 1);
-      if (!got2) s_fail = 1;
-      tc::fence_after_sync();
-      // block-local partial (m, l, O / l) in the tile-major layout
-      // part_o[tile][column group of 16][row][16]: one warp store = 1 KiB contiguous
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+    } else {
+      // block-local partial O = sum_k exp(s_k - m) v_k (not divided by l) in
+      // the tile-major layout part_o[tile][column group of 16][row][16]: one
+      // warp store = 1 KiB contiguous
       const int ncg = a.Dv / 16;
-      T* pbase = part_o + (int64_t(tile) * ncg * 128 + row) * 16;
-      for (int c0 = 0; c0 < a.Dv; c0 += 32) {
-        float v[32];
-        tc::tmem_ld32(obase + c0, v);
+      for (int it = 0; it < ntiles; ++it) {
+        const int ab = acc_of(it), rnd = round_of(it), tile = tile_of(it);
+        const bool got = tc::mbar_wait(&o_full[ab], rnd & 1);
+        if (!got) s_fail = 1;
+        tc::fence_after_sync();
+        const uint32_t obase = tmem + lane_base + nacc * a.sp_cols + ab * a.o_cols;
+        T* pbase = part_o + (int64_t(tile) * ncg * 128 + row) * 16;
+        for (int c0 = 0; c0 < a.Dv; c0 += 32) {
+          float v[32];
+          tc::tmem_ld32(obase + c0, v);
 #pragma unroll
-        for (int hgrp = 0; hgrp < 2; ++hgrp) {
-          uint32_t w[8];
+          for (int hgrp = 0; hgrp < 2; ++hgrp) {
+            uint32_t w[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) w[i] = pack2<T>(v[16 * hgrp + 2 * i] * inv, v[16 * hgrp + 2 * i + 1] * inv);
-          st_cs32(pbase + int64_t(c0 / 16 + hgrp) * 128 * 16, w);
+            for (int i = 0; i < 8; ++i) w[i] = pack2<T>(v[16 * hgrp + 2 * i], v[16 * hgrp + 2 * i + 1]);
+            st_cs32(pbase + int64_t(c0 / 16 + hgrp) * 128 * 16, w);
+          }
         }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&o_empty[ab]);
+        if (!got) break;
       }
-      __stcs(reinterpret_cast<float2*>(a.part_ml) + int64_t(tile) * 128 + row,
-             make_float2(req >= 0 ? mx * a.scale : -INFINITY, l));
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&o_empty[ab]);
-      if (!got || !got2) break;
     }
   }
   tc::fence_before_sync();
@@ -525,10 +536,15 @@ __global__ void __launch_bounds__(128) attn_combine_tiles_kernel(const AttnTcArg
     }
   }
   const float M = warp_max(fmaxf(m_s[0], m_s[1]));
-  float w_s[2];
+  // partial O of a slot is sum exp(s - m_s) v: weight exp(m_s - M); the
+  // normaliser is L = sum l_s exp(m_s - M)
+  float w_s[2], lw = 0.f;
 #pragma unroll
-  for (int k = 0; k < 2; ++k) w_s[k] = (M == -INFINITY || m_s[k] == -INFINITY) ? 0.f : l_s[k] * expf(m_s[k] - M);
-  const float L = warp_sum(w_s[0] + w_s[1]);
+  for (int k = 0; k < 2; ++k) {
+    w_s[k] = (M == -INFINITY || m_s[k] == -INFINITY || l_s[k] <= 0.f) ? 0.f : expf(m_s[k] - M);
+    lw += l_s[k] * w_s[k];
+  }
+  const float L = warp_sum(lw);
   constexpr int SPI = 32 / NCG;       // slots per warp instruction
   const int cg = lane % NCG, sub = lane / NCG;
   float acc[16];
