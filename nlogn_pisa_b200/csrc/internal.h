@@ -76,6 +76,7 @@ struct RouteArgs {
   const float* dense;   // precomputed level scores, rows local to the range
   int64_t dense_stride;
   int dense_off[kMaxLevels];  // per level offset in a dense row, -1 = compute here
+  FastDiv fbr, fH, ftc;       // branching, KV heads, t_count (set by the launcher)
 };
 
 int route(const RouteArgs& a, int dtype, cudaStream_t stream);

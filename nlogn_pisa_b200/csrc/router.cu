@@ -349,14 +349,19 @@ __global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t local = int64_t(blockIdx.x) * 4 + warp;
   if (local >= int64_t(a.B) * a.t_count * a.H) return;
-  const int h = int(local % a.H);
-  const int tl = int((local / a.H) % a.t_count);
-  const int b = int(local / (int64_t(a.H) * a.t_count));
+  // items < 2^31 (checked by the launcher)
+  const uint32_t l1 = a.fH.div(uint32_t(local)), l2 = a.ftc.div(l1);
+  const int h = int(uint32_t(local) - l1 * uint32_t(a.H));
+  const int tl = int(l1 - l2 * uint32_t(a.t_count));
+  const int b = int(l2);
   const int t = a.t_begin + tl;
   const int64_t item = (int64_t(b) * a.T + t) * a.H + h;
   const int64_t pos = a.positions ? a.positions[int64_t(b) * a.T + t] : a.pos_offset + t;
   const float* dense_row = a.dense + local * a.dense_stride;
   const int64_t leaf = pos / a.C;
+  // forced-recent leaves leaf-r (r < force_recent, leaf-r >= 0) have, at any
+  // level, ancestors forming the contiguous id range [lo_leaf / div, leaf / div]
+  const int64_t lo_leaf = leaf - a.force_recent + 1 > 0 ? leaf - a.force_recent + 1 : 0;
   int64_t span = a.C, div = 1;
   for (int l = 0; l < a.top; ++l) { span *= a.br; div *= a.br; }
 
@@ -367,6 +372,7 @@ __global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
   int width = a.first_width;
   for (int level = a.top; level >= 0; --level) {
     const int len = a.levels.size[level];
+    const int64_t f_hi = leaf >= 0 ? leaf / div : -1, f_lo = leaf >= 0 ? lo_leaf / div : 0;
     bool valid[8], forced[8];
     int nvalid = 0;
 #pragma unroll
@@ -379,10 +385,7 @@ __global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
       bool f = false;
       if (valid[e]) {
         if (a.force_first && v == 0) f = true;
-        for (int r = 0; r < a.force_recent; ++r) {
-          const int64_t target = leaf - r;
-          if (target >= 0 && v == target / div) f = true;
-        }
+        if (a.force_recent > 0 && v >= f_lo && v <= f_hi) f = true;
       }
       forced[e] = f;
       nvalid += __popc(__ballot_sync(kFull, valid[e]));
@@ -437,8 +440,9 @@ __global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const int i = e * 32 + lane;
-      const int parent = i < width ? kept[warp][i / a.br] : -1;
-      id[e] = parent < 0 ? -1 : parent * a.br + i % a.br;
+      const int q = int(a.fbr.div(uint32_t(i)));
+      const int parent = i < width ? kept[warp][q] : -1;
+      id[e] = parent < 0 ? -1 : parent * a.br + (i - q * a.br);
     }
     __syncwarp();
     span /= a.br;
@@ -483,10 +487,14 @@ int route(const RouteArgs& a, int dtype, cudaStream_t stream) {
       if (a.method == PISA_METHOD_PISA1 || a.levels.size[l] > a.K) all_dense = false;
     }
   }
-  if (all_dense) {
-    const int64_t items = int64_t(a.B) * a.t_count * a.H;
+  const int64_t items = int64_t(a.B) * a.t_count * a.H;
+  if (all_dense && items < (int64_t(1) << 31)) {
     if (items == 0) return PISA_OK;
-    route_warp_kernel<<<unsigned((items + 3) / 4), 128, 0, stream>>>(a);
+    RouteArgs w = a;
+    w.fbr = FastDiv::make(uint32_t(a.br));
+    w.fH = FastDiv::make(uint32_t(a.H));
+    w.ftc = FastDiv::make(uint32_t(a.t_count));
+    route_warp_kernel<<<unsigned((items + 3) / 4), 128, 0, stream>>>(w);
     PISA_CHECK_LAUNCH();
     return PISA_OK;
   }
