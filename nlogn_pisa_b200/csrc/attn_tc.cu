@@ -88,7 +88,6 @@ __global__ void attn_scatter_kernel(const AttnTcArgs a) {
   const int q = int(a.fRT.div(uint32_t(pos))), slot = pos - q * a.RT;
   const int64_t tile = a.offsets[bucket] + q;
   a.tile_req[tile * a.RT + slot] = int32_t(lr);
-  a.tile_pos[lr] = int32_t(tile * a.RT + slot);
   if (slot == 0) a.tile_owner[tile] = int32_t(bucket);
 }
 
@@ -126,6 +125,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 // o_full, o_empty (TMEM buffers of S/P and O).  All waits are bounded.
 constexpr int kEpiWarps = 8, kLoadWarps = 8, kMmaWarp = kEpiWarps + kLoadWarps, kStages = 3, kGroup = 8;
 constexpr int kRowsPerLoader = 128 / kLoadWarps;  // tile rows per producer warp
+constexpr int kMeta = 16;                          // metadata ring slots
 constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
 
 template <typename T>
@@ -141,11 +141,11 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
   __shared__ uint64_t q_full[kStages], q_empty[kStages], s_full[2], p_full[2], o_full[2], o_empty[2];
   __shared__ uint32_t tmem_slot;
   __shared__ int s_kvb[kStages];
-  // per-tile metadata ring for the epilogue (8 slots): the producer runs at
-  // most kStages tiles ahead of the MMAs and they at most two ahead of the
-  // epilogue, so slot it%8 is free again when tile it is produced
-  __shared__ uint64_t meta_full[8];
-  __shared__ int s_req[8][128], s_nv[8][128];
+  // per-tile metadata ring for the epilogue (16 slots): the producer of tile
+  // i waits for S(i-3), S(i-3) for O(i-5) and O(i-5) for the readout of
+  // tile i-7, so the slot of tile i (i % 16) is no longer read when refilled
+  __shared__ uint64_t meta_full[kMeta];
+  __shared__ int s_req[kMeta][128], s_nv[kMeta][128];
   __shared__ int s_fail;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
       tc::mbar_init(&o_full[i], 1);
       tc::mbar_init(&o_empty[i], 4);
     }
-    for (int i = 0; i < 8; ++i) tc::mbar_init(&meta_full[i], kLoadWarps);
+    for (int i = 0; i < kMeta; ++i) tc::mbar_init(&meta_full[i], kLoadWarps);
     s_fail = 0;
     tc::fence_barrier_init();
   }
@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
         }
       }
       tc::cp_async_arrive(&q_full[s]);
-      const int slot = it & 7;
+      const int slot = it & (kMeta - 1);
       if (gq == 0 && lane < kRowsPerLoader) {
         s_req[slot][j] = req;
         s_nv[slot][j] = nv;
@@ -392,9 +392,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
         const bool got = tc::mbar_wait(&s_full[ab], rnd & 1);
         if (!got) s_fail = 1;
         tc::fence_after_sync();
-        if (!tc::mbar_wait(&meta_full[it & 7], (it >> 3) & 1)) s_fail = 1;
-        const int req = r < a.RT ? s_req[it & 7][r] : -1;
-        const int nvalid = r < a.RT ? s_nv[it & 7][r] : 0;
+        if (!tc::mbar_wait(&meta_full[it & (kMeta - 1)], (it >> 4) & 1)) s_fail = 1;
+        const int req = r < a.RT ? s_req[it & (kMeta - 1)][r] : -1;
+        const int nvalid = r < a.RT ? s_nv[it & (kMeta - 1)][r] : 0;
         const uint32_t base = tmem + lane_base + ab * a.sp_cols;                 // S, then P at +C
         float mx = -INFINITY;
         float l = 0.f;
@@ -458,8 +458,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
           }
         }
         // the row's block max (scaled) and sum of exponentials
-        __stcs(reinterpret_cast<float2*>(a.part_ml) + int64_t(tile) * 128 + row,
-               make_float2(req >= 0 ? mx * a.scale : -INFINITY, l));
+        if (req >= 0)
+          __stcs(reinterpret_cast<float2*>(a.part_ml) + int64_t(req) * a.G + (row & (a.G - 1)),
+                 make_float2(mx * a.scale, l));
         // one arrival per warp once all its lanes' TMEM stores are done
         tc::fence_before_sync();
         __syncwarp();
@@ -467,26 +468,28 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
         if (!got) break;
       }
     } else {
-      // block-local partial O = sum_k exp(s_k - m) v_k (not divided by l) in
-      // the tile-major layout part_o[tile][column group of 16][row][16]: one
-      // warp store = 1 KiB contiguous
-      const int ncg = a.Dv / 16;
+      // block-local partial O = sum_k exp(s_k - m) v_k (not divided by l) of
+      // the row's request and head, query-major: row request * G + head
       for (int it = 0; it < ntiles; ++it) {
-        const int ab = acc_of(it), rnd = round_of(it), tile = tile_of(it);
+        const int ab = acc_of(it), rnd = round_of(it);
         const bool got = tc::mbar_wait(&o_full[ab], rnd & 1);
         if (!got) s_fail = 1;
         tc::fence_after_sync();
+        if (!tc::mbar_wait(&meta_full[it & (kMeta - 1)], (it >> 4) & 1)) s_fail = 1;
+        const int req = r < a.RT ? s_req[it & (kMeta - 1)][r] : -1;
         const uint32_t obase = tmem + lane_base + nacc * a.sp_cols + ab * a.o_cols;
-        T* pbase = part_o + (int64_t(tile) * ncg * 128 + row) * 16;
+        T* pbase = part_o + (int64_t(req) * a.G + (row & (a.G - 1))) * a.Dv;
         for (int c0 = 0; c0 < a.Dv; c0 += 32) {
           float v[32];
           tc::tmem_ld32(obase + c0, v);
+          if (req >= 0) {
 #pragma unroll
-          for (int hgrp = 0; hgrp < 2; ++hgrp) {
-            uint32_t w[8];
+            for (int hgrp = 0; hgrp < 2; ++hgrp) {
+              uint32_t w[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) w[i] = pack2<T>(v[16 * hgrp + 2 * i], v[16 * hgrp + 2 * i + 1]);
-            st_cs32(pbase + int64_t(c0 / 16 + hgrp) * 128 * 16, w);
+              for (int i = 0; i < 8; ++i) w[i] = pack2<T>(v[16 * hgrp + 2 * i], v[16 * hgrp + 2 * i + 1]);
+              st_cs32(pbase + c0 + 16 * hgrp, w);
+            }
           }
         }
         tc::fence_before_sync();
@@ -503,93 +506,110 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
   if (warp == 0) tc::tmem_free(tmem, a.tmem_cols);
 }
 
-// Merge the S block partials of one query head (one warp per head row).
-// Partials live in the tile-major layout; tile_pos maps each request to its
-// (tile, row).  Lane = (slot offset, column group of 16 values): one 32-byte
-// load per lane per slot, 32 / NCG slots per warp instruction.
+// Merge the S block partials of each query head into its output row and LSE.
+// One warp per (batch, token, KV head, group of hpw heads): the partials of a
+// (token, KV head) are contiguous (request-major, heads inner), so one warp
+// instruction reads 32 x 32 bytes = 32 / NCG whole rows.  Lane = (replica,
+// head, column group of 16 values); replicas take every R-th slot and are
+// summed at the end.  Pass 1 turns each head's S (m, l) pairs into weights
+// exp(m_s - M) (kept in shared memory) and the normaliser L.
 template <typename T, int NCG>
-__global__ void __launch_bounds__(128) attn_combine_tiles_kernel(const AttnTcArgs a) {
-  const int64_t idx = blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (idx >= int64_t(a.B) * a.tlen * a.Hq) return;
-  const uint32_t i1 = a.fHq.div(uint32_t(idx)), i2 = a.ftlen.div(i1);
-  const int hq = int(uint32_t(idx) - i1 * uint32_t(a.Hq));
-  const int tl = int(i1 - i2 * uint32_t(a.tlen));
-  const int b = int(i2);
-  const int h = hq / a.G, g = hq % a.G;
+__global__ void __launch_bounds__(128) attn_combine_kernel(const AttnTcArgs a) {
+  __shared__ float s_w[4][64][16];           // [warp][slot][head of the warp]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hpw = min(a.G, 32 / NCG);        // heads per warp (power of two)
+  const int wpr = a.G / hpw;                 // warps per (token, KV head)
+  const uint32_t idx = blockIdx.x * 4u + uint32_t(warp);
+  if (idx >= uint32_t(a.B) * uint32_t(a.tlen) * uint32_t(a.H) * uint32_t(wpr)) return;
+  const uint32_t row = idx / uint32_t(wpr);  // (b, tl, h), wpr a power of two
+  const int gsub = int(idx - row * uint32_t(wpr));
+  const uint32_t r1 = a.fH.div(row), r2 = a.ftlen.div(r1);
+  const int h = int(row - r1 * uint32_t(a.H));
+  const int tl = int(r1 - r2 * uint32_t(a.tlen));
+  const int b = int(r2);
   const int t = a.t0 + tl;
-  const int64_t slot0 = ((int64_t(b) * a.tlen + tl) * a.H + h) * a.S;
+  const int64_t lr0 = int64_t(row) * a.S;    // chunk-local request of slot 0
+  const int g0 = gsub * hpw;
   const T* part_o = static_cast<const T*>(a.part_o);
   const float2* part_ml = reinterpret_cast<const float2*>(a.part_ml);
-  // lane k-th slot: s = lane + 32k; its partial row index tile*128 + row
-  float m_s[2] = {-INFINITY, -INFINITY}, l_s[2] = {0.f, 0.f};
-  int prow[2] = {-1, -1};
+
+  // slots this lane checks in pass 1: s = lane, lane + 32
+  bool vis[2];
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     const int sl = lane + 32 * k;
-    if (sl < a.S && visible_block(a, b, t, h, sl) >= 0) {
-      const int pos = a.tile_pos[slot0 + sl];
-      const int tile = int(a.fRT.div(uint32_t(pos))), r = pos - tile * a.RT;
-      prow[k] = tile * 128 + r * a.G + g;
-      const float2 ml = __ldcs(part_ml + prow[k]);
-      if (ml.y > 0.f) { m_s[k] = ml.x; l_s[k] = ml.y; }
-    }
+    vis[k] = sl < a.S && visible_block(a, b, t, h, sl) >= 0;
   }
-  const float M = warp_max(fmaxf(m_s[0], m_s[1]));
-  // partial O of a slot is sum exp(s - m_s) v: weight exp(m_s - M); the
-  // normaliser is L = sum l_s exp(m_s - M)
-  float w_s[2], lw = 0.f;
+  float my_M = -INFINITY, my_L = 0.f;
+  const int g_lane = (lane / NCG) & (hpw - 1);
+  for (int gl = 0; gl < hpw; ++gl) {
+    float m_s[2] = {-INFINITY, -INFINITY}, l_s[2] = {0.f, 0.f};
 #pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    w_s[k] = (M == -INFINITY || m_s[k] == -INFINITY || l_s[k] <= 0.f) ? 0.f : expf(m_s[k] - M);
-    lw += l_s[k] * w_s[k];
+    for (int k = 0; k < 2; ++k) {
+      if (vis[k]) {
+        const float2 ml = __ldcs(part_ml + (lr0 + lane + 32 * k) * a.G + g0 + gl);
+        if (ml.y > 0.f) { m_s[k] = ml.x; l_s[k] = ml.y; }
+      }
+    }
+    const float M = warp_max(fmaxf(m_s[0], m_s[1]));
+    float lw = 0.f;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float w = (M == -INFINITY || m_s[k] == -INFINITY) ? 0.f : expf(m_s[k] - M);
+      lw += l_s[k] * w;
+      const int sl = lane + 32 * k;
+      if (sl < a.S) s_w[warp][sl][gl] = w;
+    }
+    const float L = warp_sum(lw);
+    if (gl == g_lane) { my_M = M; my_L = L; }
   }
-  const float L = warp_sum(lw);
-  constexpr int SPI = 32 / NCG;       // slots per warp instruction
-  const int cg = lane % NCG, sub = lane / NCG;
+  __syncwarp();
+
+  const int cg = lane % NCG;
+  const int R = 32 / (NCG * hpw);            // replicas
+  const int rep = lane / (NCG * hpw);
   float acc[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-  for (int s0 = 0; s0 < a.S; s0 += 2 * SPI) {
-    float w[2];
-    uint32_t raw[2][8];
+  const T* base = part_o + (lr0 * a.G + g0 + g_lane) * a.Dv + cg * 16;
+  const int64_t slot_stride = int64_t(a.G) * a.Dv;
+  constexpr int kLoads = 4;
+  for (int s0 = rep; s0 < a.S; s0 += kLoads * R) {
+    float w[kLoads];
+    uint32_t raw[kLoads][8];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int sl = s0 + u * SPI + sub;
-      const float w0 = __shfl_sync(kFull, w_s[0], sl & 31), w1 = __shfl_sync(kFull, w_s[1], sl & 31);
-      const int r0 = __shfl_sync(kFull, prow[0], sl & 31), r1 = __shfl_sync(kFull, prow[1], sl & 31);
-      w[u] = sl < a.S ? (sl < 32 ? w0 : w1) : 0.f;
-      const int pr = sl < 32 ? r0 : r1;
+    for (int u = 0; u < kLoads; ++u) {
+      const int sl = s0 + u * R;
+      w[u] = sl < a.S ? s_w[warp][sl][g_lane] : 0.f;
       if (w[u] > 0.f) {
-        const int tile = pr >> 7, row = pr & 127;
-        ld_cs32(part_o + ((int64_t(tile) * NCG + cg) * 128 + row) * 16, raw[u]);
+        ld_cs32(base + sl * slot_stride, raw[u]);
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) raw[u][i] = 0u;
       }
     }
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < kLoads; ++u) {
       const T* e = reinterpret_cast<const T*>(raw[u]);
 #pragma unroll
       for (int i = 0; i < 16; ++i) acc[i] = fmaf(w[u], to_f32<T>(e[i]), acc[i]);
     }
   }
-#pragma unroll
-  for (int o = NCG; o < 32; o <<= 1)
+  for (int o = NCG * hpw; o < 32; o <<= 1)
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[i] += __shfl_xor_sync(kFull, acc[i], o);
-  T* out = static_cast<T*>(a.out) + ((int64_t(b) * a.T + t) * a.Hq + hq) * a.Dv;
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  if (sub == 0) {
+  if (rep == 0) {
+    const int hq = h * a.G + g0 + g_lane;
+    T* out = static_cast<T*>(a.out) + ((int64_t(b) * a.T + t) * a.Hq + hq) * a.Dv;
+    const float inv = my_L > 0.f ? 1.f / my_L : 0.f;
     uint32_t wv[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) wv[i] = pack2<T>(acc[2 * i] * inv, acc[2 * i + 1] * inv);
     uint4* dst = reinterpret_cast<uint4*>(out + cg * 16);
     dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
     dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+    if (cg == 0 && a.lse) a.lse[(int64_t(b) * a.T + t) * a.Hq + hq] = my_L > 0.f ? my_M + logf(my_L) : -INFINITY;
   }
-  if (lane == 0 && a.lse) a.lse[(int64_t(b) * a.T + t) * a.Hq + hq] = L > 0.f ? M + logf(L) : -INFINITY;
 }
 
 template <typename T>
@@ -629,15 +649,16 @@ int attn_tc_typed(AttnTcArgs a, cudaStream_t stream) {
       attn_tc_kernel<T><<<unsigned(a.num_sms), kPipeThreads, smem, stream>>>(a);
       PISA_CHECK_LAUNCH();
     }
-    const unsigned cgrid = unsigned((int64_t(a.B) * a.tlen * a.Hq + 3) / 4);
+    const int ncg = a.Dv / 16;
+    const int hpw = std::min(a.G, 32 / ncg);
+    const unsigned cgrid = unsigned((int64_t(a.B) * a.tlen * a.H * (a.G / hpw) + 3) / 4);
     {
       TimedLaunch timed(PISA_KERNEL_ATTN_COMBINE, stream);
-      switch (a.Dv / 16) {
-        case 1: attn_combine_tiles_kernel<T, 1><<<cgrid, 128, 0, stream>>>(a); break;
-        case 2: attn_combine_tiles_kernel<T, 2><<<cgrid, 128, 0, stream>>>(a); break;
-        case 4: attn_combine_tiles_kernel<T, 4><<<cgrid, 128, 0, stream>>>(a); break;
-        case 8: attn_combine_tiles_kernel<T, 8><<<cgrid, 128, 0, stream>>>(a); break;
-        default: attn_combine_tiles_kernel<T, 16><<<cgrid, 128, 0, stream>>>(a); break;
+      switch (ncg) {
+        case 2: attn_combine_kernel<T, 2><<<cgrid, 128, 0, stream>>>(a); break;
+        case 4: attn_combine_kernel<T, 4><<<cgrid, 128, 0, stream>>>(a); break;
+        case 8: attn_combine_kernel<T, 8><<<cgrid, 128, 0, stream>>>(a); break;
+        default: attn_combine_kernel<T, 16><<<cgrid, 128, 0, stream>>>(a); break;
       }
       PISA_CHECK_LAUNCH();
     }

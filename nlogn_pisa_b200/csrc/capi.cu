@@ -207,8 +207,10 @@ static SelectPlan plan_select(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int6
   // levels that can hold more than K candidates (else the all-fit shortcut
   // scores nothing; pisa1 has no shortcut), children counts up to 8192.
   const int64_t G = Hq / H;
+  // (the dense kernel groups children in 1, 2 or 4 columns: pisa1 or b in {2, 4})
   const bool dense_ok = (dtype == PISA_BF16 || dtype == PISA_F16) && is_pow2(G) && G <= 32 &&
-                        D % 8 == 0 && D <= 256 && Tq * G >= 1024;
+                        D % 8 == 0 && D <= 256 && Tq * G >= 1024 &&
+                        (method == PISA_METHOD_PISA1 || br == 2 || br == 4);
   for (int l = 0; l < kMaxLevels; ++l) p.dense_off[l] = -1;
   if (dense_ok) {
     for (int64_t l = top; l >= 0; --l) {
@@ -447,7 +449,7 @@ struct AttnPlan {
   int64_t TW = 4096, chunk = 0, NB = 0, RT = 0, num_buckets = 0, capacity = 0;
   int64_t sp_cols = 0, o_cols = 0, tmem_cols = 0, nacc = 1, nstages = 2;
   int64_t counts_off = 0, cursors_off = 0, offsets_off = 0, misc_off = 0, owner_off = 0,
-          req_off = 0, pos_off = 0, po_off = 0, pml_off = 0, total = 0;
+          req_off = 0, po_off = 0, pml_off = 0, total = 0;
 };
 
 static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t Dv,
@@ -488,9 +490,9 @@ static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t 
   p.misc_off = off; off += 256;
   p.owner_off = off; off += align_up(p.capacity * 4, 256);
   p.req_off = off; off += align_up(p.capacity * p.RT * 4, 256);
-  p.pos_off = off; off += align_up(reqs * 4, 256);
-  p.po_off = off; off += align_up(p.capacity * 128 * Dv * elem_size(dtype), 256);
-  p.pml_off = off; off += align_up(p.capacity * 128 * 8, 256);
+  // block partials, query-major: row (request, head) at request * G + head
+  p.po_off = off; off += align_up(reqs * G * Dv * elem_size(dtype), 256);
+  p.pml_off = off; off += align_up(reqs * G * 8, 256);
   p.total = off;
   return p;
 }
@@ -547,7 +549,6 @@ int pisa_sparse_attn_fwd(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh
     a.status = reinterpret_cast<int*>(ws + plan.misc_off + 4);
     a.tile_owner = reinterpret_cast<int32_t*>(ws + plan.owner_off);
     a.tile_req = reinterpret_cast<int32_t*>(ws + plan.req_off);
-    a.tile_pos = reinterpret_cast<int32_t*>(ws + plan.pos_off);
     a.part_o = ws + plan.po_off;
     a.part_ml = reinterpret_cast<float*>(ws + plan.pml_off);
     a.tiles_per_cta = 8;

@@ -196,13 +196,12 @@ struct AttnTcArgs {
   int32_t* tile_owner;
   int32_t* tile_req;
   int32_t* total_tiles;
-  int32_t* tile_pos;  // chunk-local request -> tile * RT + slot
   int64_t capacity;
   int tiles_per_cta, tmem_cols, sp_cols, o_cols, nacc, nstages, num_sms;
   // divisors of the index decodes (set by the launcher from the fields above)
   FastDiv fS, fH, fHq, fNB, fTW, fRT, ftlen, fnwin;
-  void* part_o;
-  float* part_ml;
+  void* part_o;     // [request * G + head][Dv] block partials (query-major, chunk-local requests)
+  float* part_ml;   // [request * G + head] (m, l)
   void* out;
   float* lse;
   int* status;

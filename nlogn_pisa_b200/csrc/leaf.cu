@@ -81,6 +81,7 @@ __global__ void family_scatter_kernel(const GroupArgs g, const int32_t* __restri
 // Warp roles of the pipelined tile kernel (one persistent CTA per SM):
 //   warps 0-7   epilogue: warp w reads TMEM lanes 32*(w%4).. (one query-head
 //               row per thread) and handles half of the b children
+//               (warps 0-3 the first ceil(b/2), warps 4-7 the rest)
 //   next kLoadWarps warps  producers: gather the tile's query rows into a
 //               3-stage ring (cp.async), restage the family keys (TMA) when the
 //               bucket changes
@@ -271,7 +272,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t(quarter) * 32) << 16;
     const int r = row >> lgG;
-    const int jn = g.br / 2;                 // children handled by this thread
+    // half 0 scores children [0, ceil(b/2)), half 1 the rest
+    const int j_begin = half == 0 ? 0 : (g.br + 1) / 2, j_end = half == 0 ? (g.br + 1) / 2 : g.br;
     const float l2e = 1.4426950408889634f;
     const float sl = g.scale * l2e;          // exp(scale*x - m) = 2^(x*sl - m*l2e)
     for (int it = 0; it < ntiles; ++it) {
@@ -286,8 +288,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
       const int dst = r < g.RT ? s_dst[it & 7][r] : -1;
       (void)tile;
       const uint32_t acc = tmem + lane_base + a * NK;
-      for (int jj = 0; jj < jn; ++jj) {
-        const int j = half * jn + jj;
+      for (int j = j_begin; j < j_end; ++j) {
         const int64_t key0 = (int64_t(p) * g.br + j) * g.C;
         const int valid_keys = int(min64(g.C, max(int64_t(0), g.N - key0)));
         float score;

@@ -176,8 +176,9 @@ def test_strided_keys_and_pyramid_cache(cuda_device):
             _check_ids(got, want, trace)
 
 
+@pytest.mark.parametrize("branching", [4])
 @pytest.mark.parametrize("method", ["pisa", "pisa2", "pisa1"])
-def test_branching4_matches_oracle(cuda_device, method):
+def test_branching4_matches_oracle(cuda_device, method, branching):
     """The 4-ary extension against the oracle's generalised restatement."""
     import nlogn_pisa_b200 as P
 
@@ -186,13 +187,13 @@ def test_branching4_matches_oracle(cuda_device, method):
     q = torch.randn(B, N, H * G, D, generator=g).to(torch.bfloat16)
     k = torch.randn(B, N, H, D, generator=g).to(torch.bfloat16)
     got = P.select_blocks(q.cuda(), k.cuda(), method=method, block_size=C, topk=K, force_recent=1,
-                          branching=4).cpu().numpy()
+                          branching=branching).cpu().numpy()
     qn, kn = q.float().numpy(), k.float().numpy()
-    levels = O.build_pyramid(kn, C, "bf16", branching=4)
+    levels = O.build_pyramid(kn, C, "bf16", branching=branching)
     rows = np.arange(0, N, 7)
     trace = {}
     want = O.pyramid_select(qn[:, rows], kn, method, C, K, O.query_positions(B, N, N)[:, rows], True, 1,
-                            levels, branching=4, trace=trace)
+                            levels, branching=branching, trace=trace)
     _check_ids(got[:, rows], want, trace, min_exact=0.99)
 
 
