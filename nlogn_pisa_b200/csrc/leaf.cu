@@ -288,7 +288,50 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
       const int dst = r < g.RT ? s_dst[it & 7][r] : -1;
       (void)tile;
       const uint32_t acc = tmem + lane_base + a * NK;
-      for (int j = j_begin; j < j_end; ++j) {
+      int j_first = j_begin;
+      if (g.C == 64 && g.method == PISA_METHOD_PISA && j_end - j_begin >= 2 &&
+          (int64_t(p) * g.br + j_begin + 2) * 64 <= g.N) {
+        // two full 64-key children at once: both TMEM loads in flight, then the
+        // two max / exponential chains interleaved
+        uint32_t r0[64], r1[64];
+        tc::tmem_ld64_nowait(acc + j_begin * 64, r0);
+        tc::tmem_ld64_nowait(acc + (j_begin + 1) * 64, r1);
+        tc::tmem_wait_ld2(r0, r1);
+        // row maxima with four independent three-input chains per child
+        float ma[4], mb[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) { ma[c] = __uint_as_float(r0[c]); mb[c] = __uint_as_float(r1[c]); }
+#pragma unroll
+        for (int i = 4; i < 64; i += 8) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            ma[c] = tc::max3f(ma[c], __uint_as_float(r0[i + 2 * c]), __uint_as_float(r0[i + 2 * c + 1]));
+            mb[c] = tc::max3f(mb[c], __uint_as_float(r1[i + 2 * c]), __uint_as_float(r1[i + 2 * c + 1]));
+          }
+        }
+        const float m0 = fmaxf(tc::max3f(ma[0], ma[1], ma[2]), ma[3]);
+        const float m1 = fmaxf(tc::max3f(mb[0], mb[1], mb[2]), mb[3]);
+        const float2 kk = make_float2(sl, sl), c0 = make_float2(-m0 * sl, -m0 * sl), c1 = make_float2(-m1 * sl, -m1 * sl);
+        float2 s0 = make_float2(0.f, 0.f), s1 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 64; i += 2) {
+          const float2 x0 = tc::fma2(make_float2(__uint_as_float(r0[i]), __uint_as_float(r0[i + 1])), kk, c0);
+          const float2 x1 = tc::fma2(make_float2(__uint_as_float(r1[i]), __uint_as_float(r1[i + 1])), kk, c1);
+          s0 = tc::add2(s0, make_float2(tc::ex2f(x0.x), tc::ex2f(x0.y)));
+          s1 = tc::add2(s1, make_float2(tc::ex2f(x1.x), tc::ex2f(x1.y)));
+        }
+        float sc0 = m0 * g.scale + logf(s0.x + s0.y), sc1 = m1 * g.scale + logf(s1.x + s1.y);
+        for (int o = 1; o < g.G; o <<= 1) {
+          sc0 += __shfl_xor_sync(kFull, sc0, o);
+          sc1 += __shfl_xor_sync(kFull, sc1, o);
+        }
+        if (dst >= 0 && (row & (g.G - 1)) == 0) {
+          g.scores[int64_t(dst) + j_begin] = sc0;
+          g.scores[int64_t(dst) + j_begin + 1] = sc1;
+        }
+        j_first = j_begin + 2;
+      }
+      for (int j = j_first; j < j_end; ++j) {
         const int64_t key0 = (int64_t(p) * g.br + j) * g.C;
         const int valid_keys = int(min64(g.C, max(int64_t(0), g.N - key0)));
         float score;

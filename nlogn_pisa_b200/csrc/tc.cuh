@@ -193,6 +193,23 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
   for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// The same load without waiting: registers are valid after tmem_wait_ld2().
+__device__ __forceinline__ void tmem_ld64_nowait(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Wait for the loads into a and b; the registers pass through the asm
+// statements so no use of them can be scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_ld2(uint32_t (&a)[64], uint32_t (&b)[64]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]), "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15]), "+r"(a[16]), "+r"(a[17]), "+r"(a[18]), "+r"(a[19]), "+r"(a[20]), "+r"(a[21]), "+r"(a[22]), "+r"(a[23]), "+r"(a[24]), "+r"(a[25]), "+r"(a[26]), "+r"(a[27]), "+r"(a[28]), "+r"(a[29]), "+r"(a[30]), "+r"(a[31]), "+r"(a[32]), "+r"(a[33]), "+r"(a[34]), "+r"(a[35]), "+r"(a[36]), "+r"(a[37]), "+r"(a[38]), "+r"(a[39]), "+r"(a[40]), "+r"(a[41]), "+r"(a[42]), "+r"(a[43]), "+r"(a[44]), "+r"(a[45]), "+r"(a[46]), "+r"(a[47]), "+r"(a[48]), "+r"(a[49]), "+r"(a[50]), "+r"(a[51]), "+r"(a[52]), "+r"(a[53]), "+r"(a[54]), "+r"(a[55]), "+r"(a[56]), "+r"(a[57]), "+r"(a[58]), "+r"(a[59]), "+r"(a[60]), "+r"(a[61]), "+r"(a[62]), "+r"(a[63]) :: "memory");
+  asm volatile("" : "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]), "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]), "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15]), "+r"(b[16]), "+r"(b[17]), "+r"(b[18]), "+r"(b[19]), "+r"(b[20]), "+r"(b[21]), "+r"(b[22]), "+r"(b[23]), "+r"(b[24]), "+r"(b[25]), "+r"(b[26]), "+r"(b[27]), "+r"(b[28]), "+r"(b[29]), "+r"(b[30]), "+r"(b[31]), "+r"(b[32]), "+r"(b[33]), "+r"(b[34]), "+r"(b[35]), "+r"(b[36]), "+r"(b[37]), "+r"(b[38]), "+r"(b[39]), "+r"(b[40]), "+r"(b[41]), "+r"(b[42]), "+r"(b[43]), "+r"(b[44]), "+r"(b[45]), "+r"(b[46]), "+r"(b[47]), "+r"(b[48]), "+r"(b[49]), "+r"(b[50]), "+r"(b[51]), "+r"(b[52]), "+r"(b[53]), "+r"(b[54]), "+r"(b[55]), "+r"(b[56]), "+r"(b[57]), "+r"(b[58]), "+r"(b[59]), "+r"(b[60]), "+r"(b[61]), "+r"(b[62]), "+r"(b[63]) :: "memory");
+}
+
 // ---- fp32 helpers on the packed / special-function paths ----
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float r;
