@@ -39,6 +39,7 @@ def parse_args():
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-rows", type=int, default=12, help="sampled rows per CPU worker")
+    p.add_argument("--no-decode", action="store_true", help="skip the decode (configs[3]) measurement")
     return p.parse_args()
 
 
@@ -105,6 +106,82 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": float(self.max_mhz),
                 "reasons": sorted({n for r in self.rows for n in r[2]}), "samples": len(self.rows),
                 "power_w_max": max(r[1] for r in self.rows)}
+
+
+def decode_bench(args, device, world, peaks_hbm):
+    """one decode step for 64 sequences with a 131072-token
+    KV cache (Hq=32, Hkv=8, D=128, block 64, branching 4, top-K 32, forced
+    first + current block).  The pyramid is built once (a PyramidCache keeps it
+    between steps); a step is the fused-schedule selection plus attention over
+    the selected blocks.  Returns the JSON object reported under "decode"."""
+    import torch
+    import torch.distributed as dist
+    from nlogn_pisa_b200 import _lib
+    from nlogn_pisa_b200.selection import _c_array, level_sizes, routing_geometry
+
+    Bd, N, Hq, H, D, C, K, br = 64, 131072, 32, 8, 128, 64, 32, 4
+    lib = _lib.lib()
+    gen = torch.Generator(device=device).manual_seed(3)
+    dt = torch.bfloat16
+    k = torch.randn((Bd, N, H, D), generator=gen, device=device, dtype=dt)
+    v = torch.randn((Bd, N, H, D), generator=gen, device=device, dtype=dt)
+    q = torch.randn((Bd, 1, Hq, D), generator=gen, device=device, dtype=dt)
+    code = _lib.dtype_code(q)
+    sptr = _lib.stream_of(device)
+    stream = torch.cuda.current_stream(device)
+    leaves = N // C
+    top, first_width = routing_geometry(leaves, K, br)
+    sizes = level_sizes(leaves, br, top + 1)
+    offsets = [sum(sizes[:i]) for i in range(len(sizes))]
+    storage = torch.empty((Bd, sum(sizes), H, D), dtype=dt, device=device)
+    _lib.check(lib.pisa_build_pyramid(_lib.ptr(k), code, Bd, N, H, D, *k.stride()[:3], C, br, len(sizes),
+                                      _lib.ptr(storage), storage.stride(0), _c_array(offsets), sptr))
+    method = _lib.METHODS["pisa"]
+    fused = _lib.SCHEDULES["fused"]
+    ws_bytes = lib.pisa_select_workspace_bytes(Bd, 1, Hq, H, D, N, code, method, C, br, K, top, first_width, fused, 0)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=device)
+    ids = torch.empty((Bd, 1, H, K), dtype=torch.int64, device=device)
+    out = torch.empty((Bd, 1, Hq, D), dtype=dt, device=device)
+    lse = torch.empty((Bd, 1, Hq), dtype=torch.float32, device=device)
+
+    def step():
+        _lib.check(lib.pisa_select_blocks(
+            _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3], _lib.ptr(storage), storage.stride(0),
+            _c_array(offsets), _c_array(sizes), len(sizes), None, N - 1, code, Bd, 1, Hq, H, D, N, method, C, br,
+            K, 1, 1, top, first_width, fused, _lib.ptr(ids), _lib.ptr(ws), ws_bytes, sptr))
+        _lib.check(lib.pisa_sparse_attn_fwd(
+            _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3], _lib.ptr(v), *v.stride()[:3],
+            _lib.ptr(ids), 8, None, N - 1, code, Bd, 1, Hq, H, D, D, N, K, C, float(D ** -0.5), 1,
+            _lib.ptr(out), _lib.ptr(lse), None, 0, sptr))
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(args.steps, 5)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record(stream)
+    for _ in range(steps):
+        step()
+    ev[1].record(stream)
+    torch.cuda.synchronize()
+    ms = torch.tensor([ev[0].elapsed_time(ev[1]) / steps], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    step_us = ms.item() * 1000.0
+    # bytes a step must move: the coarse child summaries, the keys of the b*K
+    # leaf candidates (leaf scoring), keys and values of the K selected blocks
+    # (attention), the queries and outputs
+    summaries = sum(sizes[1:]) * br * D * 2 if top > 0 else 0
+    per_head = summaries + br * K * C * D * 2 + 2 * K * C * D * 2
+    step_bytes = Bd * H * per_head + 2 * Bd * Hq * D * 2
+    achieved = step_bytes / (step_us * 1e-6) / 1e9
+    del k, v, storage
+    return {"workload": "decode128k", "batch": Bd, "kv_tokens": N, "q_heads": Hq, "kv_heads": H, "head_dim": D,
+            "block_size": C, "branching": br, "topk": K, "schedule": "fused",
+            "us_per_step": step_us, "us_per_token": step_us / Bd, "steps": steps,
+            "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": step_bytes, "achieved": achieved,
+                         "unit": "GB/s", "peak": peaks_hbm, "frac": achieved / peaks_hbm},
+            "l2": "inputs (34 GB of keys and values) far larger than L2"}
 
 
 def profiled_traffic(kernel, workload):
@@ -367,6 +444,8 @@ def main():
     dominant = max(kernel_report, key=lambda n: kernel_report[n]["ms_per_step"])
     dom = kernel_report[dominant]
 
+    decode = None if args.no_decode else decode_bench(args, device, world, hbm)
+
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -398,6 +477,7 @@ def main():
                          "timing": "CUDA events around each launch on its stream, timed steps only"},
             "kernels": kernel_report,
             "stages": stage_report,
+            "decode": decode,
             "cpu_baseline": cpu,
             "e2e": {"value": world * B * N / (e2e_ms / 1000.0), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},

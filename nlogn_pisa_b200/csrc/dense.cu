@@ -27,13 +27,13 @@ namespace {
 constexpr int kThreads = 128;
 
 template <typename T, int SUP>
-__global__ void __launch_bounds__(kThreads) dense_level_kernel(const DenseArgs a) {
+__global__ void __launch_bounds__(kThreads) dense_level_kernel(const __grid_constant__ DenseArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int qch = a.Dp / 64, vpr = a.Dp / 8;
+  const int qch = a.Dp / 64;
   uint8_t* Qs = smem;                      // [qch][128 rows][128 B]
   uint8_t* Xs = smem + qch * 128 * 128;    // [qch][256 children][128 B]
-  __shared__ uint64_t mbar;
+  __shared__ uint64_t mbar, ld_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ unsigned long long s_maxpos;
 
@@ -48,7 +48,12 @@ __global__ void __launch_bounds__(kThreads) dense_level_kernel(const DenseArgs a
   const bool live = t < t_end;
   const int64_t pos = live ? (a.positions ? a.positions[int64_t(b) * a.T + t] : a.pos_offset + t) : 0;
 
-  if (tid == 0) { tc::mbar_init(&mbar, 1); s_maxpos = 0; }
+  if (tid == 0) {
+    tc::mbar_init(&mbar, 1);
+    tc::mbar_init(&ld_bar, 1);
+    s_maxpos = 0;
+    tc::fence_barrier_init();
+  }
   if (warp == 0) tc::tmem_alloc(&tmem_slot, 256);
   tc::fence_before_sync();
   __syncthreads();
@@ -57,45 +62,36 @@ __global__ void __launch_bounds__(kThreads) dense_level_kernel(const DenseArgs a
   const uint32_t tmem = tmem_slot;
   const uint32_t lane_base = (uint32_t(warp) * 32) << 16;
   const uint32_t qs_addr = tc::smem_u32(Qs), xs_addr = tc::smem_u32(Xs);
-  const T* qbase = static_cast<const T*>(a.q);
-  const T* xbase = static_cast<const T*>(a.summary) + b * a.s_sb + a.child_off * int64_t(a.H) * a.D + int64_t(h) * a.D;
-  const int64_t node_stride = int64_t(a.H) * a.D;
 
-  // the tile's query rows: token t0 + r, head h*G + g
-  {
-    const int c = tid & (vpr - 1);
-    for (int rr = tid / vpr; rr < 128; rr += kThreads / vpr) {
-      const int tok = t0 + (rr >> lgG), gh = rr & (a.G - 1);
-      const uint32_t dst = qs_addr + (c >> 3) * 128 * 128 + tc::swizzle128(rr, c & 7);
-      if (tok < t_end && c * 8 < a.D)
-        cp_async16(dst, qbase + b * a.q_sb + int64_t(tok) * a.q_st + int64_t(h * a.G + gh) * a.q_sh + c * 8);
-      else
-        st_zero16(dst);
-    }
-  }
+  // the tile's query rows (token t0 + r, head h*G + g) arrive by TMA together
+  // with the first child chunk: one box of G heads x 128/G tokens per
+  // 64-dim chunk (dims past D and tokens past the sequence read as zero)
+  const uint32_t q_bytes = uint32_t(qch) * 128 * 128;
+  if (tid == 0)
+    for (int ch = 0; ch < qch; ++ch)
+      tc::tma_load_4d(qs_addr + ch * 128 * 128, &a.tm_q, ch * 64, h * a.G, t0, b, &ld_bar);
   __syncthreads();
   const int64_t maxpos = int64_t(s_maxpos);
-  uint32_t phase = 0;
+  uint32_t phase = 0, ld_phase = 0;
   bool ok = true;
   float* out = a.scores + ((int64_t(b) * a.t_count + (live ? t - a.t_begin : 0)) * a.H + h) * a.row_stride + a.out_off;
   const float l2e = 1.4426950408889634f;
 
   for (int c0 = 0; c0 < a.n_child; c0 += 256) {
-    if (int64_t(c0 / SUP) * a.span > maxpos) break;   // every later node is past every position
+    // every later node is past every position (never at c0 = 0: node 0 starts
+    // at token 0, so the query load issued above is always awaited here)
+    if (int64_t(c0 / SUP) * a.span > maxpos) break;
     const int nc = min(256, a.n_child - c0);
     const int ncp = (nc + 15) / 16 * 16;
-    {
-      const int c = tid & (vpr - 1);
-      for (int rr = tid / vpr; rr < ncp; rr += kThreads / vpr) {
-        const uint32_t dst = xs_addr + (c >> 3) * 256 * 128 + tc::swizzle128(rr, c & 7);
-        if (rr < nc && c * 8 < a.D) cp_async16(dst, xbase + int64_t(c0 + rr) * node_stride + c * 8);
-        else st_zero16(dst);
-      }
+    // 256 child summaries per 64-dim chunk by TMA (rows past the storage
+    // read as zero; rows past the level are ignored by the epilogue)
+    if (tid == 0) {
+      tc::mbar_arrive_expect_tx(&ld_bar, uint32_t(qch) * 256 * 128 + (c0 == 0 ? q_bytes : 0u));
+      for (int ch = 0; ch < qch; ++ch)
+        tc::tma_load_4d(xs_addr + ch * 256 * 128, &a.tm_x, ch * 64, h, int(a.child_off) + c0, b, &ld_bar);
     }
-    cp_async_wait_all();
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
+    if (!tc::mbar_wait(&ld_bar, ld_phase)) ok = false;
+    ld_phase ^= 1;
     tc::fence_after_sync();
     if (tid == 0) {
       const uint32_t idesc = tc::idesc_f16(128, ncp, a.bf16);

@@ -123,6 +123,8 @@ int grouped_leaf(const GroupArgs& g, int dtype, cudaStream_t stream);
 
 // Dense scoring of every node of one coarse level (see dense.cu).
 struct DenseArgs {
+  CUtensorMap tm_q;          // q [B,T,Hq,D], box {64, G, 128/G tokens, 1}
+  CUtensorMap tm_x;          // pyramid storage [B, total, H, D], box {64, 1, 256, 1}
   const void* q;
   int64_t q_sb, q_st, q_sh;
   const void* summary;       // pyramid storage [B, total, H, D]
