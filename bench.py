@@ -137,37 +137,51 @@ def decode_bench(args, device, world, peaks_hbm):
     _lib.check(lib.pisa_build_pyramid(_lib.ptr(k), code, Bd, N, H, D, *k.stride()[:3], C, br, len(sizes),
                                       _lib.ptr(storage), storage.stride(0), _c_array(offsets), sptr))
     method = _lib.METHODS["pisa"]
-    fused = _lib.SCHEDULES["fused"]
+    fused = _lib.SCHEDULES[os.environ.get("PISA_BENCH_DECODE_SCHEDULE", "fused")]
     ws_bytes = lib.pisa_select_workspace_bytes(Bd, 1, Hq, H, D, N, code, method, C, br, K, top, first_width, fused, 0)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=device)
     ids = torch.empty((Bd, 1, H, K), dtype=torch.int64, device=device)
     out = torch.empty((Bd, 1, Hq, D), dtype=dt, device=device)
     lse = torch.empty((Bd, 1, Hq), dtype=torch.float32, device=device)
 
-    def step():
+    def select():
         _lib.check(lib.pisa_select_blocks(
             _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3], _lib.ptr(storage), storage.stride(0),
             _c_array(offsets), _c_array(sizes), len(sizes), None, N - 1, code, Bd, 1, Hq, H, D, N, method, C, br,
             K, 1, 1, top, first_width, fused, _lib.ptr(ids), _lib.ptr(ws), ws_bytes, sptr))
+
+    def attend():
         _lib.check(lib.pisa_sparse_attn_fwd(
             _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3], _lib.ptr(v), *v.stride()[:3],
             _lib.ptr(ids), 8, None, N - 1, code, Bd, 1, Hq, H, D, D, N, K, C, float(D ** -0.5), 1,
             _lib.ptr(out), _lib.ptr(lse), None, 0, sptr))
 
     for _ in range(max(args.warmup, 3)):
-        step()
+        select()
+        attend()
     torch.cuda.synchronize()
     steps = max(args.steps, 5)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    ev[0].record(stream)
-    for _ in range(steps):
-        step()
-    ev[1].record(stream)
+    for name in _lib.KERNELS:
+        _lib.kernel_time(name)
+    _lib.kernel_timing(True)
+    launches0 = lib.pisa_launch_count()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for e in ev:
+        e[0].record(stream)
+        select()
+        e[1].record(stream)
+        attend()
+        e[2].record(stream)
     torch.cuda.synchronize()
-    ms = torch.tensor([ev[0].elapsed_time(ev[1]) / steps], device=device, dtype=torch.float64)
+    _lib.kernel_timing(False)
+    launches = (lib.pisa_launch_count() - launches0) / steps
+    leaf_ms, _ = _lib.kernel_time("leaf_tiles")
+    ms = torch.tensor([sum(e[0].elapsed_time(e[2]) for e in ev) / steps,
+                       sum(e[0].elapsed_time(e[1]) for e in ev) / steps,
+                       sum(e[1].elapsed_time(e[2]) for e in ev) / steps], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    step_us = ms.item() * 1000.0
+    step_us, select_us, attend_us = (x * 1000.0 for x in ms.tolist())
     # bytes a step must move: the coarse child summaries, the keys of the b*K
     # leaf candidates (leaf scoring), keys and values of the K selected blocks
     # (attention), the queries and outputs
@@ -177,8 +191,11 @@ def decode_bench(args, device, world, peaks_hbm):
     achieved = step_bytes / (step_us * 1e-6) / 1e9
     del k, v, storage
     return {"workload": "decode128k", "batch": Bd, "kv_tokens": N, "q_heads": Hq, "kv_heads": H, "head_dim": D,
-            "block_size": C, "branching": br, "topk": K, "schedule": "fused",
+            "block_size": C, "branching": br, "topk": K,
+            "schedule": os.environ.get("PISA_BENCH_DECODE_SCHEDULE", "fused"),
             "us_per_step": step_us, "us_per_token": step_us / Bd, "steps": steps,
+            "select_us": select_us, "attention_us": attend_us, "leaf_tiles_us": 1000.0 * leaf_ms / steps,
+            "launches_per_step": launches,
             "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": step_bytes, "achieved": achieved,
                          "unit": "GB/s", "peak": peaks_hbm, "frac": achieved / peaks_hbm},
             "l2": "inputs (34 GB of keys and values) far larger than L2"}

@@ -174,6 +174,151 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnArgs a)
   }
 }
 
+// Forward for 16-bit inputs with D = Dv in {64, 128, 256} (E = D/16): logits
+// with lane = key (the whole key row per lane, many loads in flight), online
+// softmax with lane = key, then P.V with a half-warp per value row (16 lanes
+// x 2E bytes, two rows per warp instruction, four instructions in flight),
+// lanes owning E columns and the two halves summed at the end.
+template <typename T, int GC, int E>
+__global__ void __launch_bounds__(kWarps * 32) attn_fwd_coop_kernel(const AttnArgs a) {
+  constexpr int D = 16 * E;
+  __shared__ float zs[kWarps][GC][32];
+  __shared__ float mw[kWarps][GC], lw[kWarps][GC];
+  __shared__ float ow[kWarps][GC][D];
+
+  const int chunks = (a.G + GC - 1) / GC;
+  const int chunk = blockIdx.x % chunks;
+  const int64_t item = blockIdx.x / chunks;
+  const int h = int(item % a.H);
+  const int t = int((item / a.H) % a.T);
+  const int b = int(item / (int64_t(a.H) * a.T));
+  const int g0 = chunk * GC;
+  const int gn = min(GC, a.G - g0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int half = lane >> 4, l16 = lane & 15;
+  const int64_t pos = a.positions ? a.positions[int64_t(b) * a.T + t] : a.pos_offset + t;
+
+  // query heads (scaled) in shared memory, read as broadcasts by the logits
+  __shared__ __align__(16) float qsm[GC * D];
+  {
+    const T* qp = static_cast<const T*>(a.q) + b * a.q_sb + t * a.q_st + int64_t(h * a.G + g0) * a.q_sh;
+    for (int i = tid; i < GC * D; i += blockDim.x) {
+      const int g = i / D, d = i % D;
+      qsm[i] = g < gn ? to_f32<T>(qp[g * a.q_sh + d]) * a.scale : 0.f;
+    }
+  }
+  __syncthreads();
+  const T* kfull = static_cast<const T*>(a.k) + b * a.k_sb + int64_t(h) * a.k_sh;
+  const T* vb = static_cast<const T*>(a.v) + b * a.v_sb + int64_t(h) * a.v_sh + l16 * E;
+  float m[GC], l[GC], o[GC][E];
+#pragma unroll
+  for (int g = 0; g < GC; ++g) {
+    m[g] = -INFINITY; l[g] = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) o[g][e] = 0.f;
+  }
+  auto load_row = [&](const T* p, uint32_t (&w)[E / 2]) {
+#pragma unroll
+    for (int c = 0; c < E / 8; ++c) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(p) + c);
+      w[4 * c] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
+    }
+    if constexpr (E == 4) {
+      const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+      w[0] = v.x; w[1] = v.y;
+    }
+  };
+  for (int s = warp; s < a.S; s += kWarps) {
+    int64_t k0, k1;
+    if (!block_range(a, load_index(a.indices, a.index_bytes, item * a.S + s), pos, k0, k1)) continue;
+    for (int64_t base = k0; base < k1; base += 32) {
+      const int nk = int(min64(32, k1 - base));
+      // logits with lane = key: each lane reads its whole key row (D/8
+      // independent 16-byte loads in flight), q from shared memory
+      {
+        const int kk = lane;
+        float z[GC];
+        if (kk < nk) {
+          dots_gc<T, GC>(kfull + (base + kk) * a.k_st, qsm, D, z);
+        } else {
+#pragma unroll
+          for (int g = 0; g < GC; ++g) z[g] = -INFINITY;
+        }
+#pragma unroll
+        for (int g = 0; g < GC; ++g) zs[warp][g][kk] = z[g];
+      }
+      __syncwarp();
+      // online softmax with lane = key
+#pragma unroll
+      for (int g = 0; g < GC; ++g) {
+        const float zv = zs[warp][g][lane];
+        const float mnew = fmaxf(m[g], warp_max(zv));
+        const float alpha = m[g] == -INFINITY ? 0.f : expf(m[g] - mnew);
+        const float pv = zv == -INFINITY ? 0.f : expf(zv - mnew);
+        l[g] = l[g] * alpha + warp_sum(pv);
+        m[g] = mnew;
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[g][e] *= alpha;
+        zs[warp][g][lane] = pv;
+      }
+      __syncwarp();
+      // P.V: value rows base + jj + half
+      for (int j0 = 0; j0 < nk; j0 += 8) {
+        uint32_t w[4][E / 2];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int kk = j0 + 2 * u + half;
+          if (kk < nk) load_row(vb + (base + kk) * a.v_st, w[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int kk = j0 + 2 * u + half;
+          if (kk < nk) {
+            const T* x = reinterpret_cast<const T*>(w[u]);
+#pragma unroll
+            for (int g = 0; g < GC; ++g) {
+              const float pv = zs[warp][g][kk];
+#pragma unroll
+              for (int e = 0; e < E; ++e) o[g][e] = fmaf(pv, to_f32<T>(x[e]), o[g][e]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < GC; ++g) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) o[g][e] += __shfl_xor_sync(kFull, o[g][e], 16);
+    if (lane == 0) { mw[warp][g] = m[g]; lw[warp][g] = l[g]; }
+    if (half == 0) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) ow[warp][g][l16 * E + e] = o[g][e];
+    }
+  }
+  __syncthreads();
+  T* op = static_cast<T*>(a.out) + ((int64_t(b) * a.T + t) * a.Hq + h * a.G + g0) * D;
+  for (int i = tid; i < gn * D; i += blockDim.x) {
+    const int g = i / D, d = i % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mw[w][g]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        if (mw[w][g] == -INFINITY) continue;
+        const float f = expf(mw[w][g] - M);
+        L += lw[w][g] * f;
+        O += ow[w][g][d] * f;
+      }
+    }
+    op[i] = from_f32<T>(L > 0.f ? O / L : 0.f);
+    if (d == 0 && a.lse) a.lse[(int64_t(b) * a.T + t) * a.Hq + h * a.G + g0 + g] = L > 0.f ? M + logf(L) : -INFINITY;
+  }
+}
+
 template <typename T, int GC, int DPL>
 __global__ void __launch_bounds__(kWarps * 32) attn_bwd_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) float sm[];
@@ -346,8 +491,35 @@ int bwd_dpl(const AttnArgs& a, cudaStream_t s) {
   return launch_bwd<T, GC, 8>(a, s);
 }
 
+template <typename T, int GC, int E>
+int fwd_coop_launch(const AttnArgs& a, cudaStream_t stream) {
+  auto kernel = attn_fwd_coop_kernel<T, GC, E>;
+  const int64_t blocks = int64_t(a.B) * a.T * a.H * ((a.G + GC - 1) / GC);
+  if (blocks == 0) return PISA_OK;
+  kernel<<<unsigned(blocks), kWarps * 32, 0, stream>>>(a);
+  PISA_CHECK_LAUNCH();
+  return PISA_OK;
+}
+
+template <typename T, int GC>
+int fwd_coop(const AttnArgs& a, cudaStream_t s) {
+  if (a.D == 64) return fwd_coop_launch<T, GC, 4>(a, s);
+  if (a.D == 128) return fwd_coop_launch<T, GC, 8>(a, s);
+  return fwd_coop_launch<T, GC, 16>(a, s);
+}
+
 template <typename T>
 int fwd_t(const AttnArgs& a, cudaStream_t s) {
+  if constexpr (sizeof(T) == 2) {
+    // rows of 64, 128 or 256 16-bit elements, 16-byte aligned (checked by the caller)
+    const bool coop = a.D == a.Dv && (a.D == 64 || a.D == 128 || a.D == 256) && a.k_st % 8 == 0 &&
+                      a.v_st % 8 == 0 && a.k_sb % 8 == 0 && a.v_sb % 8 == 0 && a.k_sh % 8 == 0 && a.v_sh % 8 == 0;
+    if (coop) {
+      if (a.G == 1) return fwd_coop<T, 1>(a, s);
+      if (a.G == 2) return fwd_coop<T, 2>(a, s);
+      return fwd_coop<T, 4>(a, s);
+    }
+  }
   if (a.G == 1) return fwd_dpl<T, 1>(a, s);
   if (a.G == 2) return fwd_dpl<T, 2>(a, s);
   return fwd_dpl<T, 4>(a, s);

@@ -234,7 +234,12 @@ static SelectPlan plan_select(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int6
     p.dense_off_ws = off;
     off += align_up(B * p.dense_chunk * H * p.dense_row * 4, 256);
   }
-  p.grouped_tc = grouped_tc_eligible(Hq, H, D, dtype, method, C, br, schedule);
+  // The schedule selects an implementation, not a result: both give the same
+  // selection.  The fused single-kernel router gives each (row, KV head) one
+  // CTA, which starves the GPU once there are many rows; from 256 rows on, a
+  // fused request runs the grouped tile pipeline instead.
+  const int eff_schedule = (schedule == PISA_SCHEDULE_FUSED && B * Tq * H >= 256) ? PISA_SCHEDULE_GROUPED : schedule;
+  p.grouped_tc = grouped_tc_eligible(Hq, H, D, dtype, method, C, br, eff_schedule);
   if (p.grouped_tc) {
     p.W0 = top == 0 ? fw : K * br;
     p.NF = p.W0 / br;
