@@ -640,8 +640,8 @@ int attn_tc_typed(AttnTcArgs a, cudaStream_t stream) {
     const unsigned grid = unsigned((reqs + 255) / 256);
     attn_count_kernel<<<grid, 256, 0, stream>>>(a);
     PISA_CHECK_LAUNCH();
-    tile_scan_kernel<<<1, kScanThreads, 0, stream>>>(a.counts, a.offsets, a.total_tiles, a.num_buckets, a.RT);
-    PISA_CHECK_LAUNCH();
+    e = launch_tile_scan(a.counts, a.offsets, a.total_tiles, a.num_buckets, a.RT, stream);
+    if (e != cudaSuccess) return fail_cuda(e, "attention tile scan");
     attn_scatter_kernel<<<grid, 256, 0, stream>>>(a);
     PISA_CHECK_LAUNCH();
     {

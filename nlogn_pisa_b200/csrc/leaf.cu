@@ -456,8 +456,8 @@ int grouped_leaf(const GroupArgs& args, int dtype, cudaStream_t stream) {
   const unsigned grid = unsigned((families + 255) / 256);
   family_count_kernel<<<grid, 256, 0, stream>>>(g, g.counts);
   PISA_CHECK_LAUNCH();
-  tile_scan_kernel<<<1, kScanThreads, 0, stream>>>(g.counts, g.offsets, g.total_tiles_w, g.num_buckets, g.RT);
-  PISA_CHECK_LAUNCH();
+  e = launch_tile_scan(g.counts, g.offsets, g.total_tiles_w, g.num_buckets, g.RT, stream);
+  if (e != cudaSuccess) return fail_cuda(e, "leaf tile scan");
   family_scatter_kernel<<<grid, 256, 0, stream>>>(g, g.offsets, g.cursors, g.tile_owner_w, g.tile_req_w);
   PISA_CHECK_LAUNCH();
 
