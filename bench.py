@@ -3,8 +3,8 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload prefill32k] [--impl ours|reference]
 
-One step = one causal prefill of one synthetic sequence per GPU (BASELINE
-configs[1] by default: B=1, N=32768, Hq=32, Hkv=8, D=128, block 64, branching
+One step = one causal prefill of one synthetic sequence per GPU (the 32K
+benchmark configuration by default: B=1, N=32768, Hq=32, Hkv=8, D=128, block 64, branching
 4, top-K 32, forced first + current block, LSE scoring, bf16): key pyramid,
 coarse-to-fine routing with leaf scoring and top-K, then attention over the
 selected blocks.  Multi-GPU runs (torchrun) give each rank its own sequence
@@ -39,7 +39,7 @@ def parse_args():
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-rows", type=int, default=12, help="sampled rows per CPU worker")
-    p.add_argument("--no-decode", action="store_true", help="skip the decode (configs[3]) measurement")
+    p.add_argument("--no-decode", action="store_true", help="skip the 128K-KV decode measurement")
     return p.parse_args()
 
 
@@ -109,7 +109,7 @@ class ClockSampler:
 
 
 def decode_bench(args, device, world, peaks_hbm):
-    """one decode step for 64 sequences with a 131072-token
+    """The decode benchmark configuration: one decode step for 64 sequences with a 131072-token
     KV cache (Hq=32, Hkv=8, D=128, block 64, branching 4, top-K 32, forced
     first + current block).  The pyramid is built once (a PyramidCache keeps it
     between steps); a step is the fused-schedule selection plus attention over

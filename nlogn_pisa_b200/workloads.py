@@ -40,16 +40,16 @@ class Workload:
 
 
 WORKLOADS = {
-    # 32K causal prefill, GQA 4:1
+    # 32K causal prefill, GQA 4:1 (the headline benchmark)
     "prefill32k": Workload("prefill32k", 1, 32768, 32, 8, 128, 64, 32, 4, True, 1, "pisa", "bf16"),
     # the same with the reference's binary pyramid
     "prefill32k_b2": Workload("prefill32k_b2", 1, 32768, 32, 8, 128, 64, 32, 2, True, 1, "pisa", "bf16"),
     # a smaller case of configs[1] for profiler captures (inputs still larger than L2)
     "prefill8k": Workload("prefill8k", 1, 8192, 32, 8, 128, 64, 32, 4, True, 1, "pisa", "bf16"),
-    # configs[2]: 256K causal prefill with informative block means
+    # 256K causal prefill with informative block means
     "prefill256k": Workload("prefill256k", 1, 262144, 32, 8, 128, 64, 32, 4, True, 1, "pisa", "bf16",
                             key_block_offset_std=0.5),
-    # configs[0]: the reference's CPU-runnable case
+    # the reference's CPU-runnable case
     "config1": Workload("config1", 1, 4096, 4, 4, 64, 64, 16, 4, True, 1, "pisa", "f32"),
 }
 

@@ -46,7 +46,7 @@ CASES = {
                  dtype="f32", seed=7, methods=("pisa", "pisa1", "pisa2"), grads=True),
     "f64": dict(B=1, N=150, T=150, Hq=2, Hkv=1, D=16, C=16, K=4, ff=True, fr=1,
                 dtype="f64", seed=8, methods=("pisa", "pisa2"), grads=True),
-    # the reference's own CPU-runnable case.
+    # the reference's own CPU-runnable benchmark case
     "config1": dict(B=1, N=4096, T=4096, Hq=4, Hkv=4, D=64, C=64, K=16, ff=True, fr=1,
                     dtype="f32", seed=0, methods=("pisa", "pisa1", "pisa2"), grads=False, rows=16),
 }
@@ -122,4 +122,6 @@ def main(root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <path of the NlogN_PISA checkout>")
+    main(sys.argv[1])

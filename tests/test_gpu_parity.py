@@ -198,7 +198,7 @@ def test_branching4_matches_oracle(cuda_device, method, branching):
 
 
 def test_sampled_rows_at_32k(cuda_device):
-    """BASELINE configs[1] shape (N=32768, Hq=32, Hkv=8, D=128, C=64, K=32), sampled query rows."""
+    """The 32K prefill benchmark shape (N=32768, Hq=32, Hkv=8, D=128, C=64, K=32), sampled query rows."""
     import nlogn_pisa_b200 as P
 
     g = torch.Generator().manual_seed(0)

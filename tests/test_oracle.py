@@ -35,7 +35,7 @@ def test_selection_matches_reference(name):
 
 
 def test_config1_selection_matches_reference():
-    """BASELINE configs[0] (N=4096, Hq=Hkv=4, D=64, C=64, K=16, first+recent=1, fp32)."""
+    """The reference's CPU-runnable benchmark case (N=4096, Hq=Hkv=4, D=64, C=64, K=16, first+recent=1, fp32)."""
     case, rec, _, (q, k, v, dout) = np_inputs("config1")
     for method in case["methods"]:
         trace = {}
