@@ -176,12 +176,10 @@ def decode_bench(args, device, world, peaks_hbm):
     _lib.kernel_timing(False)
     launches = (lib.pisa_launch_count() - launches0) / steps
     leaf_ms, _ = _lib.kernel_time("leaf_tiles")
-    ms = torch.tensor([sum(e[0].elapsed_time(e[2]) for e in ev) / steps,
-                       sum(e[0].elapsed_time(e[1]) for e in ev) / steps,
-                       sum(e[1].elapsed_time(e[2]) for e in ev) / steps], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    step_us, select_us, attend_us = (x * 1000.0 for x in ms.tolist())
+    ms = max_over_ranks([sum(e[0].elapsed_time(e[2]) for e in ev) / steps,
+                         sum(e[0].elapsed_time(e[1]) for e in ev) / steps,
+                         sum(e[1].elapsed_time(e[2]) for e in ev) / steps], device, world)
+    step_us, select_us, attend_us = (x * 1000.0 for x in ms)
     # bytes a step must move: the coarse child summaries, the keys of the b*K
     # leaf candidates (leaf scoring), keys and values of the K selected blocks
     # (attention), the queries and outputs
@@ -215,6 +213,19 @@ def profiled_traffic(kernel, workload):
 # ---------------------------------------------------------------------------
 # the reference arm: CPU restatement on a bounded sample
 # ---------------------------------------------------------------------------
+def max_over_ranks(values, device, world):
+    """Element-wise max of per-rank timings over all ranks: the slowest rank
+    sets a multi-GPU step.  One all-reduce (MAX) when world > 1."""
+    import torch
+
+    t = torch.tensor([float(x) for x in values], device=device, dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
 def arm_config(w, world):
     """The `config` object of both arms' JSON lines."""
     return {
@@ -385,11 +396,9 @@ def main():
     kernel_ms = {name: _lib.kernel_time(name) for name in _lib.KERNELS}
     stage_ms = [sum(ev[i].elapsed_time(ev[i + 1]) for ev in events) / args.steps for i in range(len(stages))]
     step_ms = sum(ev[0].elapsed_time(ev[-1]) for ev in events) / args.steps
-    times = torch.tensor([step_ms] + stage_ms, device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    step_ms = times[0].item()
-    stage_ms = times[1:].tolist()
+    times = max_over_ranks([step_ms] + stage_ms, device, world)
+    step_ms = times[0]
+    stage_ms = times[1:]
     value = world * B * N / (step_ms / 1000.0)
 
     # end to end through the public API with pinned host buffers
@@ -414,10 +423,7 @@ def main():
         e2e_step()
     e_end.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e_start.elapsed_time(e_end) / args.steps], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_ms = e2e_ms.item()
+    e2e_ms = max_over_ranks([e_start.elapsed_time(e_end) / args.steps], device, world)[0]
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
     d2h = hout.numel() * hout.element_size()
 
@@ -443,13 +449,11 @@ def main():
     kernel_work = {
         "leaf_tiles": ("leaf_tc_kernel", "tensor", leaf_flops / 1e12, tensor, "TFLOP/s"),
         "attn_tiles": ("attn_tc_kernel", "tensor", attn_flops / 1e12, tensor, "TFLOP/s"),
-        "attn_combine": ("attn_combine_tiles_kernel", "hbm", combine_bytes / 1e9, hbm, "GB/s"),
+        "attn_combine": ("attn_combine_kernel", "hbm", combine_bytes / 1e9, hbm, "GB/s"),
     }
-    kt = torch.tensor([kernel_ms[n][0] for n in _lib.KERNELS], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(kt, op=dist.ReduceOp.MAX)
+    kt = max_over_ranks([kernel_ms[n][0] for n in _lib.KERNELS], device, world)
     kernel_report = {}
-    for (name, (ms_total, count)), ms_max in zip(kernel_ms.items(), kt.tolist()):
+    for (name, (ms_total, count)), ms_max in zip(kernel_ms.items(), kt):
         if count == 0:
             continue
         kname, bound, amount, peak, unit = kernel_work[name]

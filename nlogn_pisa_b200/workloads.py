@@ -44,7 +44,7 @@ WORKLOADS = {
     "prefill32k": Workload("prefill32k", 1, 32768, 32, 8, 128, 64, 32, 4, True, 1, "pisa", "bf16"),
     # the same with the reference's binary pyramid
     "prefill32k_b2": Workload("prefill32k_b2", 1, 32768, 32, 8, 128, 64, 32, 2, True, 1, "pisa", "bf16"),
-    # a smaller case of configs[1] for profiler captures (inputs still larger than L2)
+    # a smaller case of the 32K benchmark for profiler captures (inputs still larger than L2)
     "prefill8k": Workload("prefill8k", 1, 8192, 32, 8, 128, 64, 32, 4, True, 1, "pisa", "bf16"),
     # 256K causal prefill with informative block means
     "prefill256k": Workload("prefill256k", 1, 262144, 32, 8, 128, 64, 32, 4, True, 1, "pisa", "bf16",
