@@ -360,16 +360,22 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
   a.out_ids = out_ids;
   a.coarse_only = plan.grouped_tc ? 1 : 0;
   if (plan.grouped_tc) {
-    // grouped: coarse levels -> leaf candidates + masks, then tensor-core leaf scoring
+    // grouped: coarse levels -> leaf candidates + masks (and, on the warp
+    // router, the leaf bucket counts), then tensor-core leaf scoring
     a.W0 = int(plan.W0);
     a.candidates = reinterpret_cast<int32_t*>(ws + plan.cand_off);
     a.flags = reinterpret_cast<uint8_t*>(ws + plan.flags_off);
+    a.fam_counts = reinterpret_cast<int32_t*>(ws + plan.counts_off);
+    a.NP = int(plan.NP); a.nwin = int(plan.nwin); a.TW = int(plan.TW);
+    cudaError_t e = cudaMemsetAsync(a.fam_counts, 0, sizeof(int32_t) * plan.num_buckets, s);
+    if (e != cudaSuccess) return fail_cuda(e, "bucket counts clear");
   }
+  bool counted = true;
   for (int l = 0; l < kMaxLevels; ++l) a.dense_off[l] = plan.dense_off[l];
   int rc = PISA_OK;
   if (plan.dense_row == 0) {
     a.t_begin = 0; a.t_count = int(Tq);
-    rc = route(a, dtype, s);
+    rc = route(a, dtype, s, &counted);
   } else {
     float* dense = reinterpret_cast<float*>(ws + plan.dense_off_ws);
     a.dense = dense;
@@ -406,7 +412,9 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
       }
       if (rc) break;
       a.t_begin = int(t0); a.t_count = tc;
-      rc = route(a, dtype, s);
+      bool c = false;
+      rc = route(a, dtype, s, &c);
+      counted = counted && c;
     }
   }
   if (rc || !plan.grouped_tc) return rc;
@@ -435,6 +443,7 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
   g.tile_req = g.tile_req_w;
   g.tile_capacity = plan.capacity;
   g.tiles_per_cta = 8;
+  g.counts_ready = counted ? 1 : 0;
   // two accumulators (double buffering) whenever they fit in the 512 TMEM columns
   const int64_t nk = branching * block_size;
   const int64_t want = nk <= 256 ? 2 * nk : nk;

@@ -77,9 +77,16 @@ struct RouteArgs {
   int64_t dense_stride;
   int dense_off[kMaxLevels];  // per level offset in a dense row, -1 = compute here
   FastDiv fbr, fH, ftc;       // branching, KV heads, t_count (set by the launcher)
+  // grouped leaf buckets: when set, the warp router counts each active
+  // (row, family) request into fam_counts (bucket = (b, window, head, family))
+  int32_t* fam_counts;
+  int NP, nwin, TW;
 };
 
-int route(const RouteArgs& a, int dtype, cudaStream_t stream);
+// Routes the rows of a.t_begin .. a.t_begin + a.t_count; `counted` (may be
+// null) reports whether the family buckets were counted on the way.
+
+int route(const RouteArgs& a, int dtype, cudaStream_t stream, bool* counted = nullptr);
 
 // Grouped leaf scoring: requests (row, family) bucketed by (batch, token
 // window, KV head, level-1 survivor), scored on the tensor cores, then the
@@ -113,6 +120,7 @@ struct GroupArgs {
   int tiles_per_cta;
   int tmem_cols;
   int num_sms;
+  int counts_ready;   // bucket counts already produced by the router
   // divisors of the index decodes (set by the launcher from the fields above)
   FastDiv fNF, fH, fT, fNP, fTW, fRT, fbr, fnwin;
   int64_t* out_ids;

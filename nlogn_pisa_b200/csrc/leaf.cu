@@ -447,15 +447,19 @@ int grouped_leaf(const GroupArgs& args, int dtype, cudaStream_t stream) {
   const int64_t families = int64_t(g.B) * g.T * g.H * g.NF;
   const int64_t rows = int64_t(g.B) * g.T * g.H;
   cudaError_t e;
-  e = cudaMemsetAsync(g.counts, 0, sizeof(int32_t) * g.num_buckets, stream);
-  if (e != cudaSuccess) return fail_cuda(e, "bucket counts clear");
+  if (!g.counts_ready) {
+    e = cudaMemsetAsync(g.counts, 0, sizeof(int32_t) * g.num_buckets, stream);
+    if (e != cudaSuccess) return fail_cuda(e, "bucket counts clear");
+  }
   e = cudaMemsetAsync(g.cursors, 0, sizeof(int32_t) * g.num_buckets, stream);
   if (e != cudaSuccess) return fail_cuda(e, "bucket cursors clear");
   e = cudaMemsetAsync(g.tile_req_w, 0xFF, sizeof(int32_t) * g.tile_capacity * g.RT, stream);
   if (e != cudaSuccess) return fail_cuda(e, "tile list clear");
   const unsigned grid = unsigned((families + 255) / 256);
-  family_count_kernel<<<grid, 256, 0, stream>>>(g, g.counts);
-  PISA_CHECK_LAUNCH();
+  if (!g.counts_ready) {
+    family_count_kernel<<<grid, 256, 0, stream>>>(g, g.counts);
+    PISA_CHECK_LAUNCH();
+  }
   e = launch_tile_scan(g.counts, g.offsets, g.total_tiles_w, g.num_buckets, g.RT, stream);
   if (e != cudaSuccess) return fail_cuda(e, "leaf tile scan");
   family_scatter_kernel<<<grid, 256, 0, stream>>>(g, g.offsets, g.cursors, g.tile_owner_w, g.tile_req_w);

@@ -394,13 +394,22 @@ __global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
     if (level == 0 && a.coarse_only) {
       int32_t* dst = a.candidates + item * a.W0;
       uint8_t* fdst = a.flags + item * a.W0;
+      // families are br consecutive slots (br divides 32): the first slot's
+      // lane counts the family's request when any child is scoreable
+      const int bucket0 = a.fam_counts ? ((b * a.nwin + t / a.TW) * a.H + h) * a.NP : 0;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int i = e * 32 + lane;
+        const bool scoreable = i < width && valid[e] && !forced[e] && !identity;
         if (i < width) {
-          const bool scoreable = valid[e] && !forced[e] && !identity;
           dst[i] = id[e];
           fdst[i] = uint8_t((valid[e] ? 1 : 0) | (forced[e] ? 2 : 0) | (scoreable ? 4 : 0));
+        }
+        if (a.fam_counts && e * 32 < width) {
+          const unsigned bits = __ballot_sync(kFull, scoreable);
+          const int q = int(a.fbr.div(uint32_t(lane)));
+          if (lane == q * a.br && ((bits >> lane) & ((1u << a.br) - 1u)) != 0)
+            atomicAdd(a.fam_counts + bucket0 + int(a.fbr.div(uint32_t(id[e]))), 1);
         }
       }
       return;
@@ -477,7 +486,8 @@ int route_t(const RouteArgs& a, cudaStream_t stream) {
 
 }  // namespace
 
-int route(const RouteArgs& a, int dtype, cudaStream_t stream) {
+int route(const RouteArgs& a, int dtype, cudaStream_t stream, bool* counted) {
+  if (counted) *counted = false;
   // every scored level precomputed: the warp-per-item router
   bool all_dense = a.dense != nullptr;
   for (int l = a.top; l >= 0 && all_dense; --l) {
@@ -496,12 +506,15 @@ int route(const RouteArgs& a, int dtype, cudaStream_t stream) {
     w.ftc = FastDiv::make(uint32_t(a.t_count));
     route_warp_kernel<<<unsigned((items + 3) / 4), 128, 0, stream>>>(w);
     PISA_CHECK_LAUNCH();
+    if (counted) *counted = a.fam_counts != nullptr;
     return PISA_OK;
   }
+  RouteArgs plain = a;
+  plain.fam_counts = nullptr;   // the SIMT router leaves the counting to family_count_kernel
   switch (dtype) {
-    case PISA_F32: return route_t<float>(a, stream);
-    case PISA_BF16: return route_t<__nv_bfloat16>(a, stream);
-    case PISA_F16: return route_t<__half>(a, stream);
+    case PISA_F32: return route_t<float>(plain, stream);
+    case PISA_BF16: return route_t<__nv_bfloat16>(plain, stream);
+    case PISA_F16: return route_t<__half>(plain, stream);
   }
   return fail(PISA_ERR_UNSUPPORTED, "unsupported dtype");
 }

@@ -251,3 +251,34 @@ def test_tensor_core_attention_matches_oracle(cuda_device, dtype, shape):
     want, _ = O.sparse_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), ids.numpy(), C,
                                  positions=pos, causal=causal)
     np.testing.assert_allclose(out.float().cpu().numpy(), want, rtol=0, atol=2e-2)
+
+
+def test_packed_documents_match_per_document_oracle(cuda_device):
+    """Packed varlen batch (cu_seqlens): block ids are document-relative and
+    each document is selected and attended on its own, as the reference does
+    (validation.py:59-81, top_k_pyramid.py:73-86, sparse_attn.py:29-55)."""
+    import nlogn_pisa_b200 as P
+
+    g = torch.Generator().manual_seed(41)
+    lengths = [300, 517, 129]
+    Hq, H, D, C, K = 8, 2, 64, 16, 8
+    total = sum(lengths)
+    q = torch.randn(1, total, Hq, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, total, H, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, total, H, D, generator=g).to(torch.bfloat16)
+    cu = torch.tensor([0] + list(np.cumsum(lengths)), dtype=torch.int64)
+    qc, kc, vc = _cuda(q, k, v)
+    ids = P.select_blocks(qc, kc, method="pisa", block_size=C, topk=K, cu_seqlens=cu.cuda(), force_recent=1)
+    out = P.sparse_attention(qc, kc, vc, ids, block_size=C, cu_seqlens=cu.cuda()).float().cpu().numpy()
+    ids = ids.cpu().numpy()
+    start = 0
+    for n in lengths:
+        qd, kd, vd = (x[:, start:start + n].float().numpy() for x in (q, k, v))
+        levels = O.build_pyramid(kd, C, "bf16")
+        trace = {}
+        pos = O.query_positions(1, n, n)
+        want = O.pyramid_select(qd, kd, "pisa", C, K, pos, True, 1, levels, trace=trace)
+        _check_ids(ids[:, start:start + n], want, trace)
+        ref, _ = O.sparse_attention(qd, kd, vd, ids[:, start:start + n], C, positions=pos)
+        np.testing.assert_allclose(out[:, start:start + n], ref, atol=2e-2, rtol=0)
+        start += n
