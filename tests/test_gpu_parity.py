@@ -282,3 +282,29 @@ def test_packed_documents_match_per_document_oracle(cuda_device):
         ref, _ = O.sparse_attention(qd, kd, vd, ids[:, start:start + n], C, positions=pos)
         np.testing.assert_allclose(out[:, start:start + n], ref, atol=2e-2, rtol=0)
         start += n
+
+
+def test_batched_decode_step_matches_oracle(cuda_device):
+    """A decode step for many sequences (Tq=1, fused schedule request, which
+    runs the grouped tile pipeline from 256 rows on) against the oracle, then
+    attention over the selected blocks."""
+    import nlogn_pisa_b200 as P
+
+    g = torch.Generator().manual_seed(43)
+    B, N, Hq, H, D, C, K = 48, 3000, 32, 8, 128, 64, 16
+    q = torch.randn(B, 1, Hq, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, N, H, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, N, H, D, generator=g).to(torch.bfloat16)
+    qc, kc, vc = _cuda(q, k, v)
+    ids = P.select_blocks(qc, kc, method="pisa", block_size=C, topk=K, query_offset=N - 1, force_recent=1,
+                          routing_schedule="fused", branching=4)
+    out = P.sparse_attention(qc, kc, vc, ids, block_size=C, query_offset=N - 1).float().cpu().numpy()
+    ids = ids.cpu().numpy()
+    qn, kn, vn = (x.float().numpy() for x in (q, k, v))
+    levels = O.build_pyramid(kn, C, "bf16", branching=4)
+    pos = O.query_positions(B, 1, N, N - 1)
+    trace = {}
+    want = O.pyramid_select(qn, kn, "pisa", C, K, pos, True, 1, levels, branching=4, trace=trace)
+    _check_ids(ids, want, trace)
+    ref, _ = O.sparse_attention(qn, kn, vn, ids, C, positions=pos)
+    np.testing.assert_allclose(out, ref, atol=2e-2, rtol=0)
