@@ -462,7 +462,7 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
 namespace pisa {
 
 // Workspace layout of the bucketed tensor-core attention forward (one token
-// chunk at a time; the partials of a chunk are bounded to about 2 GiB).
+// chunk at a time; the partials of a chunk are bounded to about 4 GiB: 8192-token chunks at the benchmark shape).
 struct AttnPlan {
   bool tc = false;
   int64_t TW = 4096, chunk = 0, NB = 0, RT = 0, num_buckets = 0, capacity = 0;
@@ -491,7 +491,7 @@ static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t 
          cols <= 512 && smem <= 227 * 1024 && S > 0 && S <= 64 && B * Tq * H * S >= 4096;
   if (!p.tc) return p;
   const int64_t per_token = H * S * G * (Dv * elem_size(dtype) + 8) * 9 / 8;
-  const int64_t fit = ((int64_t(1) << 31) / per_token) / p.TW * p.TW;
+  const int64_t fit = ((int64_t(1) << 32) / per_token) / p.TW * p.TW;
   p.chunk = std::min<int64_t>(Tq, std::max<int64_t>(p.TW, fit));
   p.NB = (N + C - 1) / C;
   p.RT = 128 / G;
