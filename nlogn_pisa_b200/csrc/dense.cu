@@ -7,7 +7,7 @@
 // depends on its descent, but the score of a node does not -- so every node of
 // the level is scored for every row up front, as a GEMM: a tile of 128/G
 // consecutive tokens x G query heads of one KV head (128 rows) against the
-// level's child summaries, 256 children per tcgen05 MMA (N=256, K=head_dim),
+// level's child summaries, kChunk children per tcgen05 MMA (N=kChunk, K=head_dim),
 // accumulators in TMEM.  The epilogue (thread = row) reduces each node's b
 // child columns to its score, sums the G heads with shuffles and writes
 // scores[b, t, h, node].  The router then reads scores instead of computing
@@ -25,6 +25,10 @@ namespace pisa {
 namespace {
 
 constexpr int kThreads = 128;
+// children per MMA chunk: 128 TMEM columns and 16 KB of summaries per 64-dim
+// chunk keep three CTAs resident per SM, so one CTA's loads overlap another's
+// epilogue
+constexpr int kChunk = 128;
 
 template <typename T, int SUP>
 __global__ void __launch_bounds__(kThreads) dense_level_kernel(const __grid_constant__ DenseArgs a) {
@@ -32,7 +36,7 @@ __global__ void __launch_bounds__(kThreads) dense_level_kernel(const __grid_cons
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int qch = a.Dp / 64;
   uint8_t* Qs = smem;                      // [qch][128 rows][128 B]
-  uint8_t* Xs = smem + qch * 128 * 128;    // [qch][256 children][128 B]
+  uint8_t* Xs = smem + qch * 128 * 128;    // [qch][kChunk children][128 B]
   __shared__ uint64_t mbar, ld_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ unsigned long long s_maxpos;
@@ -54,7 +58,7 @@ __global__ void __launch_bounds__(kThreads) dense_level_kernel(const __grid_cons
     s_maxpos = 0;
     tc::fence_barrier_init();
   }
-  if (warp == 0) tc::tmem_alloc(&tmem_slot, 256);
+  if (warp == 0) tc::tmem_alloc(&tmem_slot, kChunk);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -77,18 +81,18 @@ __global__ void __launch_bounds__(kThreads) dense_level_kernel(const __grid_cons
   float* out = a.scores + ((int64_t(b) * a.t_count + (live ? t - a.t_begin : 0)) * a.H + h) * a.row_stride + a.out_off;
   const float l2e = 1.4426950408889634f;
 
-  for (int c0 = 0; c0 < a.n_child; c0 += 256) {
+  for (int c0 = 0; c0 < a.n_child; c0 += kChunk) {
     // every later node is past every position (never at c0 = 0: node 0 starts
     // at token 0, so the query load issued above is always awaited here)
     if (int64_t(c0 / SUP) * a.span > maxpos) break;
-    const int nc = min(256, a.n_child - c0);
+    const int nc = min(kChunk, a.n_child - c0);
     const int ncp = (nc + 15) / 16 * 16;
-    // 256 child summaries per 64-dim chunk by TMA (rows past the storage
+    // kChunk child summaries per 64-dim chunk by TMA (rows past the storage
     // read as zero; rows past the level are ignored by the epilogue)
     if (tid == 0) {
-      tc::mbar_arrive_expect_tx(&ld_bar, uint32_t(qch) * 256 * 128 + (c0 == 0 ? q_bytes : 0u));
+      tc::mbar_arrive_expect_tx(&ld_bar, uint32_t(qch) * kChunk * 128 + (c0 == 0 ? q_bytes : 0u));
       for (int ch = 0; ch < qch; ++ch)
-        tc::tma_load_4d(xs_addr + ch * 256 * 128, &a.tm_x, ch * 64, h, int(a.child_off) + c0, b, &ld_bar);
+        tc::tma_load_4d(xs_addr + ch * kChunk * 128, &a.tm_x, ch * 64, h, int(a.child_off) + c0, b, &ld_bar);
     }
     if (!tc::mbar_wait(&ld_bar, ld_phase)) ok = false;
     ld_phase ^= 1;
@@ -98,7 +102,7 @@ __global__ void __launch_bounds__(kThreads) dense_level_kernel(const __grid_cons
       for (int ks = 0; ks < a.Dp / 16; ++ks) {
         const int ch = ks >> 2, off = (ks & 3) * 32;
         tc::mma_f16(tmem, tc::desc_sw128(qs_addr + ch * 128 * 128 + off),
-                    tc::desc_sw128(xs_addr + ch * 256 * 128 + off), idesc, ks > 0);
+                    tc::desc_sw128(xs_addr + ch * kChunk * 128 + off), idesc, ks > 0);
       }
       tc::mma_commit(&mbar);
     }
@@ -150,15 +154,16 @@ __global__ void __launch_bounds__(kThreads) dense_level_kernel(const __grid_cons
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  if (warp == 0) tc::tmem_free(tmem, 256);
+  if (warp == 0) tc::tmem_free(tmem, kChunk);
 }
 
 }  // namespace
 
 int dense_level(const DenseArgs& a, int dtype, cudaStream_t stream) {
   const int qch = a.Dp / 64;
-  // two CTAs per SM: 2 x 256 TMEM columns
-  const size_t smem = std::max<size_t>(size_t(qch) * 128 * (128 + 256) + 1024, 100 * 1024);
+  // query rows + one chunk of child summaries; TMEM (kChunk columns) allows
+  // four CTAs per SM, shared memory three at D = 128
+  const size_t smem = size_t(qch) * 128 * (128 + kChunk) + 1024;
   void (*kernel)(const DenseArgs);
   if (a.support == 1) kernel = dtype == PISA_BF16 ? dense_level_kernel<__nv_bfloat16, 1> : dense_level_kernel<__half, 1>;
   else if (a.support == 2) kernel = dtype == PISA_BF16 ? dense_level_kernel<__nv_bfloat16, 2> : dense_level_kernel<__half, 2>;
