@@ -91,11 +91,19 @@ __global__ void attn_scatter_kernel(const AttnTcArgs a) {
   if (slot == 0) a.tile_owner[tile] = int32_t(bucket);
 }
 
-// 32-byte streaming store / load (partials are written once and read once)
-__device__ __forceinline__ void st_cs32(void* p, const uint32_t (&w)[8]) {
-  asm volatile("st.global.cs.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
-               :: "l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]),
-                  "r"(w[7]) : "memory");
+// streaming store / load (partials are written once and read once) and the
+// shared-memory staging accesses of the partial readout
+__device__ __forceinline__ void st_cs16(void* p, uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3) {
+  asm volatile("st.global.cs.v4.b32 [%0], {%1,%2,%3,%4};" :: "l"(p), "r"(x0), "r"(x1), "r"(x2), "r"(x3)
+               : "memory");
+}
+__device__ __forceinline__ void st_shared16(uint32_t addr, uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" :: "r"(addr), "r"(x0), "r"(x1), "r"(x2), "r"(x3)
+               : "memory");
+}
+__device__ __forceinline__ void ld_shared16(uint32_t addr, uint32_t& x0, uint32_t& x1, uint32_t& x2, uint32_t& x3) {
+  asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(x0), "=r"(x1), "=r"(x2), "=r"(x3) : "r"(addr)
+               : "memory");
 }
 __device__ __forceinline__ void ld_cs32(const void* p, uint32_t (&w)[8]) {
   asm volatile("ld.global.cs.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
@@ -469,7 +477,13 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
       }
     } else {
       // block-local partial O = sum_k exp(s_k - m) v_k (not divided by l) of
-      // the row's request and head, query-major: row request * G + head
+      // the row's request and head, query-major: row request * G + head.
+      // Thread = row in TMEM, but a warp store of one value slice per row
+      // would touch 32 lines; so each 64-value slice of the warp's 32 rows is
+      // staged in shared memory (16-byte chunks XOR-swizzled by row) and
+      // written back as 8 warp stores of 4 rows x 128 contiguous bytes.
+      const uint32_t stg = tc::smem_u32(smem + nst * q_stage_bytes + 2 * kv_bytes) + quarter * 4096;
+      const int srow = lane >> 3, schunk = lane & 7;  // copy-out: row (of 4) and 16-byte chunk
       for (int it = 0; it < ntiles; ++it) {
         const int ab = acc_of(it), rnd = round_of(it);
         const bool got = tc::mbar_wait(&o_full[ab], rnd & 1);
@@ -478,23 +492,40 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
         if (!tc::mbar_wait(&meta_full[it & (kMeta - 1)], (it >> 4) & 1)) s_fail = 1;
         const int req = r < a.RT ? s_req[it & (kMeta - 1)][r] : -1;
         const uint32_t obase = tmem + lane_base + nacc * a.sp_cols + ab * a.o_cols;
-        T* pbase = part_o + (int64_t(req) * a.G + (row & (a.G - 1))) * a.Dv;
-        for (int c0 = 0; c0 < a.Dv; c0 += 32) {
-          float v[32];
-          tc::tmem_ld32(obase + c0, v);
-          if (req >= 0) {
+        // this lane's partial row, or null (request without a visible block)
+        T* prow = req >= 0 ? part_o + (int64_t(req) * a.G + (row & (a.G - 1))) * a.Dv : nullptr;
+        for (int c0 = 0; c0 < a.Dv; c0 += 64) {
+          const int ncol = min(64, a.Dv - c0);     // 32 or 64 (Dv % 32 == 0)
+          // stage: row = lane, 16-byte chunk c at (c ^ (lane & 7)); 32 values at a time
+          for (int half = 0; half < ncol / 32; ++half) {
+            float v[32];
+            tc::tmem_ld32(obase + c0 + 32 * half, v);
+            if (c0 + 32 * half + 32 >= a.Dv) {
+              // every TMEM load of this tile has completed: release the O buffer
+              tc::fence_before_sync();
+              __syncwarp();
+              if (lane == 0) tc::mbar_arrive(&o_empty[ab]);
+            }
 #pragma unroll
-            for (int hgrp = 0; hgrp < 2; ++hgrp) {
-              uint32_t w[8];
+            for (int c = 0; c < 4; ++c)
+              st_shared16(stg + lane * 128 + (((4 * half + c) ^ (lane & 7)) << 4), pack2<T>(v[8 * c], v[8 * c + 1]),
+                          pack2<T>(v[8 * c + 2], v[8 * c + 3]), pack2<T>(v[8 * c + 4], v[8 * c + 5]),
+                          pack2<T>(v[8 * c + 6], v[8 * c + 7]));
+          }
+          __syncwarp();
+          // copy out: warp store k covers rows 4k..4k+3, lane -> (row, chunk)
 #pragma unroll
-              for (int i = 0; i < 8; ++i) w[i] = pack2<T>(v[16 * hgrp + 2 * i], v[16 * hgrp + 2 * i + 1]);
-              st_cs32(pbase + c0 + 16 * hgrp, w);
+          for (int k = 0; k < 8; ++k) {
+            const int rr = 4 * k + srow;
+            const T* dst = reinterpret_cast<const T*>(__shfl_sync(kFull, reinterpret_cast<uintptr_t>(prow), rr));
+            if (dst != nullptr && schunk * 8 < ncol) {
+              uint32_t x0, x1, x2, x3;
+              ld_shared16(stg + rr * 128 + ((schunk ^ (rr & 7)) << 4), x0, x1, x2, x3);
+              st_cs16(const_cast<T*>(dst) + c0 + schunk * 8, x0, x1, x2, x3);
             }
           }
+          __syncwarp();
         }
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&o_empty[ab]);
         if (!got) break;
       }
     }
@@ -615,7 +646,8 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnTcArgs a) {
 template <typename T>
 int attn_tc_typed(AttnTcArgs a, cudaStream_t stream) {
   const int qch = a.Dp / 64, vch = a.Dvp / 64;
-  const size_t smem = size_t(a.nstages) * 128 * 128 * qch + size_t(2) * a.C * 128 * (qch + vch) + 1024;
+  // query stages, two K/V buffers, the readout's staging (4 warps x 32 rows x 128 B)
+  const size_t smem = size_t(a.nstages) * 128 * 128 * qch + size_t(2) * a.C * 128 * (qch + vch) + 16384 + 1024;
   cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return fail_cuda(e, "attention smem attribute");
   a.fS = FastDiv::make(uint32_t(a.S));

@@ -483,7 +483,8 @@ static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t 
   const int64_t cols = p.nacc * (p.sp_cols + p.o_cols);
   p.tmem_cols = cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
   const int64_t Dp = D <= 64 ? 64 : D <= 128 ? 128 : 256, Dvp = Dv <= 64 ? 64 : Dv <= 128 ? 128 : 256;
-  const int64_t kv_smem = 2 * C * 2 * (Dp + Dvp) + 1024 + 12288;
+  // K/V buffers, alignment slack, readout staging (16 KB) and static shared memory
+  const int64_t kv_smem = 2 * C * 2 * (Dp + Dvp) + 1024 + 16384 + 17408;
   p.nstages = 3 * 128 * 2 * Dp + kv_smem <= 227 * 1024 ? 3 : 2;
   const int64_t smem = p.nstages * 128 * 2 * Dp + kv_smem;
   p.tc = (dtype == PISA_BF16 || dtype == PISA_F16) && is_pow2(G) && G <= 32 && D % 16 == 0 &&
