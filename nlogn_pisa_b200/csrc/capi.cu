@@ -393,7 +393,7 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
     for (int l = 0; l <= top; ++l) total_nodes = std::max<int64_t>(total_nodes, a.levels.offset[l] + a.levels.size[l]);
     rc = make_tensor_map(&d.tm_q, q, dtype, B, Tq, Hq, D, q_sb, q_st, q_sh, uint32_t(d.G), uint32_t(128 / d.G));
     if (rc == PISA_OK)
-      rc = make_tensor_map(&d.tm_x, a.summary, dtype, B, total_nodes, H, D, a.s_sb, H * D, D, 1, 128);
+      rc = make_tensor_map(&d.tm_x, a.summary, dtype, B, total_nodes, H, D, a.s_sb, H * D, D, 1, 64);
     for (int64_t t0 = 0; t0 < Tq && rc == PISA_OK; t0 += plan.dense_chunk) {
       const int tc = int(std::min<int64_t>(plan.dense_chunk, Tq - t0));
       d.t_begin = int(t0); d.t_count = tc;

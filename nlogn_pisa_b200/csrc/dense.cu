@@ -25,10 +25,10 @@ namespace pisa {
 namespace {
 
 constexpr int kThreads = 128;
-// children per MMA chunk: 128 TMEM columns and 16 KB of summaries per 64-dim
-// chunk keep three CTAs resident per SM, so one CTA's loads overlap another's
-// epilogue
-constexpr int kChunk = 128;
+// children per MMA chunk: 64 TMEM columns and 8 KB of summaries per 64-dim
+// chunk keep four CTAs resident per SM at D = 128, so some CTAs load while
+// others run their epilogue, and the causal cut-off skips work in steps of 64
+constexpr int kChunk = 64;
 
 template <typename T, int SUP>
 __global__ void __launch_bounds__(kThreads) dense_level_kernel(const __grid_constant__ DenseArgs a) {
@@ -161,8 +161,8 @@ __global__ void __launch_bounds__(kThreads) dense_level_kernel(const __grid_cons
 
 int dense_level(const DenseArgs& a, int dtype, cudaStream_t stream) {
   const int qch = a.Dp / 64;
-  // query rows + one chunk of child summaries; TMEM (kChunk columns) allows
-  // four CTAs per SM, shared memory three at D = 128
+  // query rows + one chunk of child summaries (49 KB at D = 128: four CTAs
+  // per SM; TMEM, kChunk columns each, allows eight)
   const size_t smem = size_t(qch) * 128 * (128 + kChunk) + 1024;
   void (*kernel)(const DenseArgs);
   if (a.support == 1) kernel = dtype == PISA_BF16 ? dense_level_kernel<__nv_bfloat16, 1> : dense_level_kernel<__half, 1>;
