@@ -462,7 +462,7 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
 namespace pisa {
 
 // Workspace layout of the bucketed tensor-core attention forward (one token
-// chunk at a time; the partials of a chunk are bounded to about 4 GiB: 8192-token chunks at the benchmark shape).
+// chunk at a time; the partials of a chunk are bounded to about 4 GiB: 12288-token chunks at the benchmark shape).
 struct AttnPlan {
   bool tc = false;
   int64_t TW = 4096, chunk = 0, NB = 0, RT = 0, num_buckets = 0, capacity = 0;
