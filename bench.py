@@ -411,8 +411,11 @@ def main():
     hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
     dq, dk, dv = (torch.empty_like(x) for x in (q, k, v))
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    e2e_chunk = min(N, 4096)
-    bounds = [(a, min(a + e2e_chunk, N)) for a in range(0, N, e2e_chunk)]
+    # short first and last chunks (the copy in of the first and the copy out
+    # of the last are not overlapped with compute), long chunks between:
+    # cuts at 1/16, 1/4, 1/2, 3/4 and 15/16 of the tokens, on block boundaries
+    cuts = sorted({0, N} | {min(N, int(N * f) // C * C) for f in (1 / 16, 1 / 4, 1 / 2, 3 / 4, 15 / 16)})
+    bounds = [(a, b) for a, b in zip(cuts[:-1], cuts[1:]) if b > a]
     ev_in = [torch.cuda.Event() for _ in bounds]
     ev_out = [torch.cuda.Event() for _ in bounds]
 
@@ -526,7 +529,7 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": world * B * N / (e2e_ms / 1000.0), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                    "mode": f"incremental prefill in {e2e_chunk}-token chunks through select_blocks / "
+                    "mode": f"incremental prefill in token chunks {[b - a for a, b in bounds]} through select_blocks / "
                             "sparse_attention; host-to-device, compute and device-to-host on three streams"},
             "gpu_launches": launches,
             "clocks": clock_info,
