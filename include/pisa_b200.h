@@ -152,7 +152,8 @@ PISA_API int64_t pisa_select_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, 
  *   whose output is 0).  lse may be NULL.
  * workspace: pisa_sparse_attn_fwd_workspace_bytes(...) bytes enable the
  *   block-bucketed tensor-core path for fp16/bf16 prefill; with NULL (or when
- *   that size is 0) the per-query gather kernels run.
+ *   that size is 0, as it is below 64 query rows per sequence, e.g. batched
+ *   decode) the per-query gather kernels run.
  */
 PISA_API int pisa_sparse_attn_fwd(const void *q, int64_t q_sb, int64_t q_st, int64_t q_sh, const void *k,
                          int64_t k_sb, int64_t k_st, int64_t k_sh, const void *v, int64_t v_sb,
