@@ -38,8 +38,10 @@ def parse_args():
     p.add_argument("--workload", default="prefill32k")
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--cpu-rows", type=int, default=12, help="sampled rows per CPU worker")
+    p.add_argument("--cpu-rows", type=int, default=16, help="sampled rows per CPU worker (cpu_baseline leg)")
+    p.add_argument("--ref-rows", type=int, default=48, help="sampled rows per CPU worker (reference arm)")
     p.add_argument("--no-decode", action="store_true", help="skip the 128K-KV decode measurement")
+    p.add_argument("--no-extra", action="store_true", help="skip the binary-pyramid and 256K lines")
     return p.parse_args()
 
 
@@ -117,7 +119,7 @@ def decode_bench(args, device, world, peaks_hbm):
     import torch
     import torch.distributed as dist
     from nlogn_pisa_b200 import _lib
-    from nlogn_pisa_b200.selection import _c_array, level_sizes, routing_geometry
+    from nlogn_pisa_b200.selection import _c_array, level_sizes, routing_geometry  # noqa: F401
 
     Bd, N, Hq, H, D, C, K, br = 64, 131072, 32, 8, 128, 64, 32, 4
     lib = _lib.lib()
@@ -242,15 +244,17 @@ def run_reference(args, workload):
     if rank != 0:
         return 0
     sys.path.insert(0, str(ROOT / "oracle"))
-    from cpu_sample import time_sample
+    from cpu_sample import reference_available, time_sample
 
-    samples = []
-    for _ in range(args.warmup):
-        time_sample(workload, rows_per_worker=2)
-    for _ in range(max(1, args.steps)):
-        samples.append(time_sample(workload, rows_per_worker=args.cpu_rows))
-    value = statistics.median(s["value"] for s in samples)
-    base = samples[0]
+    # The reference's own CPU implementation of the path (its torch backend,
+    # from the offline install under baseline/_ref) when present, else the
+    # oracle port of it.  One process pool on all host cores; warm-up and
+    # timed repeats of the same bounded sample of query rows.
+    impl = "reference" if reference_available() else "port"
+    repeats = max(1, args.steps) + max(0, args.warmup)
+    base = time_sample(workload, rows_per_worker=args.ref_rows, impl=impl, repeats=repeats)
+    timed = base["values"][max(0, args.warmup):]
+    value = statistics.median(timed)
     line = {
         "impl": "reference",
         "metric": "prefill tokens/s (select+attend)",
@@ -260,12 +264,18 @@ def run_reference(args, workload):
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": 1000.0 * workload.tokens / value,
+        "extrapolated": True,
+        "step": (f"one step = {base['rows_sampled']} sampled query rows timed on {base['cores']} host processes, "
+                 f"extrapolated to the {workload.tokens}-token sequence; ms_per_step is that extrapolation, "
+                 f"sample wall time {1000.0 * base['seconds']:.0f} ms"),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": workload.dtype,
         "data": "synthetic",
-        "config": arm_config(workload, int(os.environ.get("WORLD_SIZE", "1"))),
+        "config": arm_config(workload, int(os.environ.get("WORLD_SIZE", "1")))
+        | ({"branching": 2, "branching_note": "the reference implements only a binary pyramid"}
+           if base["kind"] == "reference" else {}),
         "cpu_baseline": {k: base[k] for k in ("unit", "cores", "kind", "sample")} | {"value": value},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -276,32 +286,16 @@ def run_reference(args, workload):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
-def main():
-    args = parse_args()
-    from nlogn_pisa_b200.workloads import WORKLOADS
-
-    workload = WORKLOADS[args.workload]
-    if args.impl == "reference":
-        return run_reference(args, workload)
-
+def prefill_measure(w, device, rank, steps, warmup, world, kernel_timing=True, sample_clocks=None):
+    """Time the pyramid -> selection -> attention step of workload `w` through
+    the C ABI with inputs resident in HBM.  Returns per-stage device times
+    (max over ranks), per-kernel device times and the step's algorithmic work."""
     import torch
-    import torch.distributed as dist
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
-
-    import nlogn_pisa_b200 as P
     from nlogn_pisa_b200 import _lib
-    from nlogn_pisa_b200.selection import _c_array, level_sizes, routing_geometry
+    from nlogn_pisa_b200.selection import _c_array, level_sizes, routing_geometry  # noqa: F401
     from nlogn_pisa_b200.workloads import make_inputs
 
-    w = workload
     q, k, v = make_inputs(w, device, seed=w.seed + rank)
     B, N, Hq, H, D = w.batch, w.tokens, w.q_heads, w.kv_heads, w.head_dim
     G, C, K, br = Hq // H, w.block_size, w.topk, w.branching
@@ -318,17 +312,17 @@ def main():
     out = torch.empty((B, N, Hq, D), dtype=q.dtype, device=device)
     lse = torch.empty((B, N, Hq), dtype=torch.float32, device=device)
     method = _lib.METHODS[w.method]
-    scale = D ** -0.5
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    sel_ws_bytes = lib.pisa_select_workspace_bytes(B, N, Hq, H, D, N, code, method, C, br, K, top,
+                                                   first_width, _lib.SCHEDULES["grouped"], 0)
+    sel_ws = torch.empty(max(sel_ws_bytes, 1), dtype=torch.uint8, device=device)
+    attn_ws_bytes = lib.pisa_sparse_attn_fwd_workspace_bytes(B, N, Hq, H, D, D, N, K, C, code)
+    attn_ws = torch.empty(max(attn_ws_bytes, 1), dtype=torch.uint8, device=device)
 
     def pyramid():
         _lib.check(lib.pisa_build_pyramid(
             _lib.ptr(k), code, B, N, H, D, *k.stride()[:3], C, br, len(sizes), _lib.ptr(storage),
             storage.stride(0), _c_array(offsets), sptr))
-
-    sel_ws_bytes = lib.pisa_select_workspace_bytes(B, N, Hq, H, D, N, code, method, C, br, K, top,
-                                                   first_width, _lib.SCHEDULES["grouped"], 0)
-    sel_ws = torch.empty(max(sel_ws_bytes, 1), dtype=torch.uint8, device=device)
 
     def select():
         _lib.check(lib.pisa_select_blocks(
@@ -337,50 +331,62 @@ def main():
             Hq, H, D, N, method, C, br, K, int(w.force_first), w.force_recent, top, first_width,
             _lib.SCHEDULES["grouped"], _lib.ptr(ids), _lib.ptr(sel_ws), sel_ws_bytes, sptr))
 
-    attn_ws_bytes = lib.pisa_sparse_attn_fwd_workspace_bytes(B, N, Hq, H, D, D, N, K, C, code)
-    attn_ws = torch.empty(max(attn_ws_bytes, 1), dtype=torch.uint8, device=device)
-
     def attend():
         _lib.check(lib.pisa_sparse_attn_fwd(
             _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3], _lib.ptr(v), *v.stride()[:3],
-            _lib.ptr(ids), 8, None, 0, code, B, N, Hq, H, D, D, N, K, C, float(scale), 1,
+            _lib.ptr(ids), 8, None, 0, code, B, N, Hq, H, D, D, N, K, C, float(D ** -0.5), 1,
             _lib.ptr(out), _lib.ptr(lse), _lib.ptr(attn_ws), attn_ws_bytes, sptr))
 
     stages = (("pyramid", pyramid), ("select", select), ("attention", attend))
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(max(warmup, 3)):
         for _, fn in stages:
             fn()
     torch.cuda.synchronize()
+    _lib.check(lib.pisa_workspace_status(_lib.ptr(sel_ws), sptr))
+    if attn_ws_bytes:
+        _lib.check(lib.pisa_workspace_status(_lib.ptr(attn_ws), sptr))
 
-    # algorithmic work of one step (outside the timed region)
+    # algorithmic work of one step (outside the timed region), from the actual selections
     pos = torch.arange(N, device=device)
     valid_ids = (ids >= 0) & (ids * C <= pos[None, :, None, None])
     key_count = torch.clamp(torch.minimum(pos[None, :, None, None] + 1, torch.full_like(ids, N)) - ids * C, 0, C)
     attn_keys = torch.where(valid_ids, key_count, 0).sum().item()
-    attn_flops = attn_keys * G * (2 * D + 2 * D)
     leaf = pos // C
-    valid_leaves = leaf + 1
     cand = torch.full_like(leaf, br * K)
     forced = 1 + (leaf > 0).long()          # first block + current block (force_recent = 1)
     invalid = (br - 1) - (leaf % br)        # siblings of the current leaf past the causal edge
-    scored = torch.where(valid_leaves > K, cand - forced - invalid, 0)
-    leaf_flops = scored.sum().item() * H * B * 2 * D * G * C
-    pyramid_bytes = (B * N * H * D + B * sum(sizes) * H * D) * q.element_size()
+    scored = torch.where(leaf + 1 > K, cand - forced - invalid, 0)
+    es = q.element_size()
+    dense_nodes = sum(sizes[lv] for lv in range(1, top + 1) if sizes[lv] > K)   # scored coarse nodes per row
+    work = {
+        "attn_flops": attn_keys * G * 4 * D,
+        "leaf_flops": scored.sum().item() * H * B * 2 * D * G * C,
+        "pyramid_bytes": (B * N * H * D + B * sum(sizes) * H * D) * es,
+        # combine: read every visible request's G partial rows, write the output
+        "combine_bytes": valid_ids.sum().item() * G * (D * es + 8) + B * N * Hq * D * es,
+        # router: read the dense coarse scores, write the leaf candidates (int32) and masks (u8)
+        "router_bytes": B * N * H * (dense_nodes * 4 + br * K * 5),
+        # dense coarse levels: children of every scored coarse node, G query rows of D
+        "dense_flops": B * N * H * G * 2 * D * sum(sizes[lv - 1] for lv in range(1, top + 1) if sizes[lv] > K),
+        # final top-K: read candidates, masks and scores of the b*K leaf slots, write K int64 ids
+        "final_bytes": B * N * H * (br * K * 9 + K * 8),
+        "selected_flops": attn_keys * G * 4 * D,
+    }
+    del valid_ids, key_count
 
-    # combine kernel: read every visible request's G partial rows, write the output
-    combine_bytes = valid_ids.sum().item() * G * (D * q.element_size() + 8) + B * N * Hq * D * q.element_size()
-
-    clocks = ClockSampler(local)
     if world > 1:
+        import torch.distributed as dist
         dist.barrier()
     torch.cuda.synchronize()
     for name in _lib.KERNELS:
         _lib.kernel_time(name)            # drop warm-up records
-    _lib.kernel_timing(True)
+    if kernel_timing:
+        _lib.kernel_timing(True)
     launches0 = lib.pisa_launch_count()
-    clocks.start()
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)] for _ in range(args.steps)]
-    for step in range(args.steps):
+    if sample_clocks:
+        sample_clocks.start()
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)] for _ in range(steps)]
+    for step in range(steps):
         flush.zero_()
         ev = events[step]
         ev[0].record(stream)
@@ -390,30 +396,84 @@ def main():
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clock_info = clocks.stop()
+    clock_info = sample_clocks.stop() if sample_clocks else None
     launches = lib.pisa_launch_count() - launches0
     _lib.kernel_timing(False)
     kernel_ms = {name: _lib.kernel_time(name) for name in _lib.KERNELS}
-    stage_ms = [sum(ev[i].elapsed_time(ev[i + 1]) for ev in events) / args.steps for i in range(len(stages))]
-    step_ms = sum(ev[0].elapsed_time(ev[-1]) for ev in events) / args.steps
+    stage_ms = [sum(ev[i].elapsed_time(ev[i + 1]) for ev in events) / steps for i in range(len(stages))]
+    step_ms = sum(ev[0].elapsed_time(ev[-1]) for ev in events) / steps
     times = max_over_ranks([step_ms] + stage_ms, device, world)
-    step_ms = times[0]
-    stage_ms = times[1:]
-    value = world * B * N / (step_ms / 1000.0)
+    kt = max_over_ranks([kernel_ms[n][0] for n in _lib.KERNELS], device, world)
+    _lib.check(lib.pisa_workspace_status(_lib.ptr(sel_ws), sptr))
+    if attn_ws_bytes:
+        _lib.check(lib.pisa_workspace_status(_lib.ptr(attn_ws), sptr))
+    return {
+        "tensors": (q, k, v), "step_ms": times[0], "stage_ms": dict(zip((s for s, _ in stages), times[1:])),
+        "kernel_ms": {n: (ms, kernel_ms[n][1]) for n, ms in zip(_lib.KERNELS, kt)},
+        "launches": launches, "work": work, "clocks": clock_info, "steps": steps,
+        "value": world * B * N / (times[0] / 1000.0),
+    }
 
-    # End to end through the public API with pinned host buffers, as an
-    # incremental prefill: token chunks of the sequence are copied in on one
-    # stream while earlier chunks are selected and attended on the compute
-    # stream (select_blocks / sparse_attention with query_offset on the key
-    # prefix, which gives the same result as one call over the whole
-    # sequence), and each chunk's output is copied back on a third stream.
+
+def kernel_report(m, hbm, tensor):
+    """Per-kernel roofline entries: algorithmic work per step over device time per step."""
+    w = m["work"]
+    table = {
+        "leaf_tiles": ("leaf_tc_kernel", "tensor", w["leaf_flops"] / 1e12, tensor, "TFLOP/s"),
+        "attn_tiles": ("attn_tc_kernel", "tensor", w["attn_flops"] / 1e12, tensor, "TFLOP/s"),
+        "attn_combine": ("attn_combine_kernel", "hbm", w["combine_bytes"] / 1e9, hbm, "GB/s"),
+        "pyramid": ("pyramid kernels", "hbm", w["pyramid_bytes"] / 1e9, hbm, "GB/s"),
+        "dense_level": ("dense_level_kernel", "tensor", w["dense_flops"] / 1e12, tensor, "TFLOP/s"),
+        "router": ("route_warp_kernel", "hbm", w["router_bytes"] / 1e9, hbm, "GB/s"),
+        "leaf_final": ("leaf_final_kernel", "hbm", w["final_bytes"] / 1e9, hbm, "GB/s"),
+    }
+    report = {}
+    for name, (ms_total, count) in m["kernel_ms"].items():
+        if count == 0:
+            continue
+        kname, bound, amount, peak, unit = table[name]
+        per_step_ms = ms_total / m["steps"]
+        achieved = amount / (per_step_ms / 1000.0)
+        report[name] = {"kernel": kname, "bound": bound, "ms_per_step": per_step_ms,
+                        "launches_per_step": count / m["steps"], "ms_per_launch": ms_total / count,
+                        "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak}
+    return report
+
+
+def stage_report(m, hbm, tensor):
+    w = m["work"]
+    work = {"pyramid": ("hbm", w["pyramid_bytes"] / 1e9, hbm, "GB/s"),
+            "select": ("tensor", (w["leaf_flops"] + w["dense_flops"]) / 1e12, tensor, "TFLOP/s"),
+            "attention": ("tensor", w["attn_flops"] / 1e12, tensor, "TFLOP/s")}
+    out = {}
+    for name, ms in m["stage_ms"].items():
+        bound, amount, peak, unit = work[name]
+        achieved = amount / (ms / 1000.0)
+        out[name] = {"ms": ms, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                     "frac": achieved / peak}
+    return out
+
+
+def e2e_prefill(w, tensors, device, world, steps):
+    """The same step end to end through the public API with pinned host buffers,
+    as an incremental prefill: token chunks of the sequence are copied in on
+    one stream while earlier chunks are selected and attended on the compute
+    stream (select_blocks / sparse_attention with query_offset on the key
+    prefix, which gives the same result as one call over the whole sequence),
+    and each chunk's output is copied back on a third stream."""
+    import torch
+
+    import nlogn_pisa_b200 as P
+
+    q, k, v = tensors
+    B, N, C, K, br = w.batch, w.tokens, w.block_size, w.topk, w.branching
+    stream = torch.cuda.current_stream(device)
     hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
-    hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    hout = torch.empty((B, N, w.q_heads, w.head_dim), dtype=q.dtype, pin_memory=True)
     dq, dk, dv = (torch.empty_like(x) for x in (q, k, v))
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     # short first and last chunks (the copy in of the first and the copy out
-    # of the last are not overlapped with compute), long chunks between:
-    # cuts at 1/16, 1/4, 1/2, 3/4 and 15/16 of the tokens, on block boundaries
+    # of the last are not overlapped with compute), long chunks between
     cuts = sorted({0, N} | {min(N, int(N * f) // C * C) for f in (1 / 16, 1 / 4, 1 / 2, 3 / 4, 15 / 16)})
     bounds = [(a, b) for a, b in zip(cuts[:-1], cuts[1:]) if b > a]
     ev_in = [torch.cuda.Event() for _ in bounds]
@@ -443,16 +503,51 @@ def main():
         e2e_step()
     torch.cuda.synchronize()
     if world > 1:
+        import torch.distributed as dist
         dist.barrier()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         e2e_step()
     e_end.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = max_over_ranks([e_start.elapsed_time(e_end) / args.steps], device, world)[0]
+    e2e_ms = max_over_ranks([e_start.elapsed_time(e_end) / steps], device, world)[0]
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
     d2h = hout.numel() * hout.element_size()
+    return {"value": world * B * N / (e2e_ms / 1000.0), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+            "mode": f"incremental prefill in token chunks {[b - a for a, b in bounds]} through select_blocks / "
+                    "sparse_attention; host-to-device, compute and device-to-host on three streams"}
+
+
+def compact_line(w, m, hbm, tensor):
+    """A secondary workload's measurement: throughput, stages and kernels."""
+    return {"workload": w.name, "tokens": w.tokens, "branching": w.branching, "topk": w.topk,
+            "value": m["value"], "unit": "tokens/s", "ms_per_step": m["step_ms"], "steps": m["steps"],
+            "stages": stage_report(m, hbm, tensor), "kernels": kernel_report(m, hbm, tensor)}
+
+
+def main():
+    args = parse_args()
+    from nlogn_pisa_b200.workloads import WORKLOADS
+
+    workload = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return run_reference(args, workload)
+
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    from nlogn_pisa_b200 import _lib
 
     peaks = {}
     peaks_file = ROOT / "MEASURED_PEAKS.json"
@@ -461,37 +556,27 @@ def main():
     hbm = peaks.get("hbm_gbs", 6650.0)
     tensor = peaks.get("bf16_tflops", 1590.0)
     src = "measured" if peaks else "fallback"
-    stage_work = {
-        "pyramid": ("hbm", pyramid_bytes / 1e9, hbm, "GB/s"),
-        "select": ("tensor", leaf_flops / 1e12, tensor, "TFLOP/s"),
-        "attention": ("tensor", attn_flops / 1e12, tensor, "TFLOP/s"),
-    }
-    stage_report = {}
-    for (name, _), ms in zip(stages, stage_ms):
-        bound, amount, peak, unit = stage_work[name]
-        achieved = amount / (ms / 1000.0)
-        stage_report[name] = {"ms": ms, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
-                              "frac": achieved / peak}
-    # the dominant kernel: largest device time per step among the timed tile kernels
-    kernel_work = {
-        "leaf_tiles": ("leaf_tc_kernel", "tensor", leaf_flops / 1e12, tensor, "TFLOP/s"),
-        "attn_tiles": ("attn_tc_kernel", "tensor", attn_flops / 1e12, tensor, "TFLOP/s"),
-        "attn_combine": ("attn_combine_kernel", "hbm", combine_bytes / 1e9, hbm, "GB/s"),
-    }
-    kt = max_over_ranks([kernel_ms[n][0] for n in _lib.KERNELS], device, world)
-    kernel_report = {}
-    for (name, (ms_total, count)), ms_max in zip(kernel_ms.items(), kt):
-        if count == 0:
-            continue
-        kname, bound, amount, peak, unit = kernel_work[name]
-        per_step_ms = ms_max / args.steps
-        achieved = amount / (per_step_ms / 1000.0)
-        kernel_report[name] = {"kernel": kname, "bound": bound, "ms_per_step": per_step_ms,
-                               "launches_per_step": count / args.steps, "ms_per_launch": ms_max / count,
-                               "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak}
-    dominant = max(kernel_report, key=lambda n: kernel_report[n]["ms_per_step"])
-    dom = kernel_report[dominant]
 
+    w = workload
+    clocks = ClockSampler(local)
+    m = prefill_measure(w, device, rank, args.steps, args.warmup, world, sample_clocks=clocks)
+    e2e = e2e_prefill(w, m["tensors"], device, world, args.steps)
+    m["tensors"] = None
+    torch.cuda.empty_cache()
+    kernels = kernel_report(m, hbm, tensor)
+    dominant = max((n for n in kernels if n in ("leaf_tiles", "attn_tiles", "attn_combine")),
+                   key=lambda n: kernels[n]["ms_per_step"])
+    dom = kernels[dominant]
+
+    extra = {}
+    if world == 1 and not args.no_extra:
+        for name, steps in (("prefill32k_b2", 5), ("prefill256k", 3)):
+            if name == w.name:
+                continue
+            mx = prefill_measure(WORKLOADS[name], device, rank, steps, 3, world)
+            mx["tensors"] = None
+            extra[name] = compact_line(WORKLOADS[name], mx, hbm, tensor)
+            torch.cuda.empty_cache()
     decode = None if args.no_decode else decode_bench(args, device, world, hbm)
 
     if rank == 0:
@@ -501,15 +586,16 @@ def main():
             from cpu_sample import time_sample
 
             cpu = time_sample(w, rows_per_worker=args.cpu_rows)
-            cpu.pop("seconds", None)
+            for key in ("seconds", "values", "rows_sampled"):
+                cpu.pop(key, None)
         line = {
             "metric": "prefill tokens/s (select+attend)",
-            "value": value,
+            "value": m["value"],
             "unit": "tokens/s",
             "n_gpus": world,
             "steps": args.steps,
             "warmup": max(args.warmup, 3),
-            "ms_per_step": step_ms,
+            "ms_per_step": m["step_ms"],
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
@@ -523,16 +609,16 @@ def main():
                          "launches_per_step": dom["launches_per_step"],
                          "work_per_launch": dom["achieved"] * dom["ms_per_launch"] / 1000.0,
                          "timing": "CUDA events around each launch on its stream, timed steps only"},
-            "kernels": kernel_report,
-            "stages": stage_report,
+            "kernels": kernels,
+            "stages": stage_report(m, hbm, tensor),
+            "select_attend_tensor_frac": (m["work"]["leaf_flops"] + m["work"]["attn_flops"])
+            / 1e12 / (m["step_ms"] / 1000.0) / tensor,
+            "workloads": extra,
             "decode": decode,
             "cpu_baseline": cpu,
-            "e2e": {"value": world * B * N / (e2e_ms / 1000.0), "unit": "tokens/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                    "mode": f"incremental prefill in token chunks {[b - a for a, b in bounds]} through select_blocks / "
-                            "sparse_attention; host-to-device, compute and device-to-host on three streams"},
-            "gpu_launches": launches,
-            "clocks": clock_info,
+            "e2e": e2e,
+            "gpu_launches": m["launches"],
+            "clocks": m["clocks"],
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -140,6 +140,35 @@ PISA_API int64_t pisa_select_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, 
                                              int64_t first_width, int schedule, int build_summary);
 
 /*
+ * Leaf scores of arbitrary candidate lists.  Replaces grouped_leaf_scores
+ * (pisa/pisa/ops/flash_sparse_attn/top_k_pyramid/leaf_triton.py:144-232)
+ * with its masks (leaf_scoreable_mask, leaf_triton.py:23-60).
+ * candidates: [B,Tq,H,W] int32 (cand_bytes 4) or int64 (8), contiguous.
+ * out_scores: [B,Tq,H,W] fp32 in candidate order: the score summed over the
+ *   G query heads (pisa: LSE over the block's keys; pisa2: scale*mean +
+ *   0.5*scale^2*var of the logits; pisa1: q . leaf mean, scale 1), or -inf
+ *   for an id outside [0, ceil(N/block_size)) and, when `positions` ([B,Tq]
+ *   int64) is given, for ids past the query's position, forced ids (block 0
+ *   with force_first, the force_recent most recent blocks) and every id of a
+ *   row whose valid ids all fit in `topk` (pisa / pisa2).
+ * leaf_means: [B, blocks, H, D] (node stride H*D, batch stride means_sb) for
+ *   pisa1, or NULL to pool them from `keys` inside the workspace.
+ * workspace: pisa_leaf_scores_workspace_bytes(...) bytes (have_means != 0
+ *   when leaf_means will be passed).
+ */
+PISA_API int pisa_leaf_scores(const void *q, int64_t q_sb, int64_t q_st, int64_t q_sh, const void *keys,
+                              int64_t key_sb, int64_t key_st, int64_t key_sh, const void *leaf_means,
+                              int64_t means_sb, const void *candidates, int cand_bytes,
+                              const int64_t *positions, int dtype, int64_t B, int64_t Tq, int64_t Hq,
+                              int64_t H, int64_t D, int64_t N, int64_t W, int method, int64_t block_size,
+                              int64_t topk, int force_first, int64_t force_recent, float *out_scores,
+                              void *workspace, int64_t workspace_bytes, pisa_stream_t stream);
+
+PISA_API int64_t pisa_leaf_scores_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D,
+                                                  int64_t N, int64_t W, int dtype, int method,
+                                                  int64_t block_size, int have_means);
+
+/*
  * Attention over selected key blocks with one softmax over their union
  * (causal inside blocks), forward.  Replaces sparse_attention's CUDA branch
  * (pisa/pisa/ops/flash_sparse_attn/sparse_attn/sparse_attn.py:10-61 ->
@@ -192,14 +221,16 @@ PISA_API int64_t pisa_sparse_attn_bwd_workspace_bytes(int64_t B, int64_t Tq, int
  * the tensors it passes, or a framework whose device memory is planned in
  * advance).  No counterpart in the reference.  The fp32 dK/dV accumulators
  * live in a fixed device array inside the library:
- * pisa_sparse_attn_bwd_noalloc_max_bytes() bytes (32 MiB) on every GPU that
- * loads the library, held until the process exits; shapes needing more
- * (B*N*H*(D+Dv) above 8M values) return PISA_ERR_UNSUPPORTED.  The first call
- * on a device looks up the array's device address (set-up); make that first
- * call before any stream capture.  Every call uses the same array and clears
- * it on `stream` first, so calls that overlap on the GPU (other streams,
- * other host threads) race.  Arguments as pisa_sparse_attn_bwd.  Allocates
- * nothing.
+ * pisa_sparse_attn_bwd_noalloc_max_bytes() bytes (32 MiB) per GPU, held until
+ * the process exits.  Shapes whose pisa_sparse_attn_bwd_workspace_bytes(...)
+ * exceeds that return PISA_ERR_UNSUPPORTED.  The first call on a device looks
+ * up the array's device address (set-up); under lazy module loading (the CUDA
+ * default) that is also when the 32 MiB are reserved on the device, so make
+ * that first call before fixing a memory plan and before any stream capture.
+ * The current device must be the device of `stream` (PISA_ERR_INVALID
+ * otherwise).  Every call uses the same array and clears it on `stream`
+ * first, so calls that overlap on the GPU (other streams, other host
+ * threads) race.  Arguments as pisa_sparse_attn_bwd.  Allocates nothing.
  */
 PISA_API int pisa_sparse_attn_bwd_noalloc(const void *q, const void *k, const void *v, const void *out,
                                           const void *dout, const float *lse, const void *indices,
@@ -212,6 +243,24 @@ PISA_API int pisa_sparse_attn_bwd_noalloc(const void *q, const void *k, const vo
 /* Size of the fixed scratch of pisa_sparse_attn_bwd_noalloc, in bytes. */
 PISA_API int64_t pisa_sparse_attn_bwd_noalloc_max_bytes(void);
 
+/* ---- device status (no counterpart in the reference, whose Triton kernels never wait) ----
+ * Every kernel that waits on another part of the GPU waits a bounded number
+ * of tries.  A wait that expires records PISA_ERR_TIMEOUT in the 4-byte
+ * status word at byte offset 0 of the call's workspace (pisa_select_blocks,
+ * pisa_leaf_scores, and pisa_sparse_attn_fwd when it takes the tensor-core
+ * path); the entry point clears that word on `stream` before its kernels run.
+ *
+ * pisa_workspace_status copies the word back and synchronises `stream`:
+ * PISA_OK, or PISA_ERR_TIMEOUT (the call's outputs are not valid). */
+PISA_API int pisa_workspace_status(const void *workspace, pisa_stream_t stream);
+
+/* Exercises the timeout path without touching any operand: one warp waits up
+ * to `max_tries` tries on an mbarrier that it arrives on first (arrive != 0)
+ * or that nothing ever arrives on (arrive == 0), and records the outcome in
+ * workspace[0..3] (256 bytes, cleared first) for pisa_workspace_status. */
+PISA_API int pisa_wait_selftest(int arrive, int64_t max_tries, void *workspace, int64_t workspace_bytes,
+                                pisa_stream_t stream);
+
 /* ---- per-kernel device timing (profiling aid; the reference has no counterpart) ----
  * With timing on, the library records a pair of CUDA events on the launch
  * stream around every launch of the kernels below.  Reading returns the summed
@@ -221,7 +270,11 @@ PISA_API int64_t pisa_sparse_attn_bwd_noalloc_max_bytes(void);
 #define PISA_KERNEL_LEAF_TILES 0    /* tensor-core leaf scoring tiles */
 #define PISA_KERNEL_ATTN_TILES 1    /* tensor-core attention tiles */
 #define PISA_KERNEL_ATTN_COMBINE 2  /* merge of the attention block partials */
-#define PISA_KERNEL_COUNT 3
+#define PISA_KERNEL_PYRAMID 3       /* key pyramid build (all its launches) */
+#define PISA_KERNEL_DENSE_LEVEL 4   /* tensor-core scoring of whole coarse levels */
+#define PISA_KERNEL_ROUTER 5        /* coarse-to-fine router (warp-per-row or per-item form) */
+#define PISA_KERNEL_LEAF_FINAL 6    /* final top-K over the leaf candidates */
+#define PISA_KERNEL_COUNT 7
 
 /* Kernels this library has launched in this process so far. */
 PISA_API int64_t pisa_launch_count(void);

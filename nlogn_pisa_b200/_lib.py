@@ -8,6 +8,7 @@ ValueError.  There is no CPU or Triton fallback.
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
 import torch
@@ -46,6 +47,11 @@ SIGNATURES = {
     "pisa_sparse_attn_bwd_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _L, _I, _L, _L, _L, _L, _L,
                                           _L, _L, _L, _L, _F, _I, _P, _P, _P, _P]),
     "pisa_sparse_attn_bwd_noalloc_max_bytes": (_L, []),
+    "pisa_leaf_scores": (_I, [_P, _L, _L, _L, _P, _L, _L, _L, _P, _L, _P, _I, _P, _I, _L, _L, _L, _L,
+                              _L, _L, _L, _I, _L, _L, _I, _L, _P, _P, _L, _P]),
+    "pisa_leaf_scores_workspace_bytes": (_L, [_L, _L, _L, _L, _L, _L, _L, _I, _I, _L, _I]),
+    "pisa_workspace_status": (_I, [_P, _P]),
+    "pisa_wait_selftest": (_I, [_I, _L, _P, _L, _P]),
     "pisa_launch_count": (_L, []),
     "pisa_kernel_timing": (_I, [_I]),
     "pisa_kernel_time": (_I, [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
@@ -80,8 +86,39 @@ def check(status):
     raise RuntimeError(f"libpisa_b200: {message}")
 
 
+_checked = os.environ.get("PISA_CHECK_STATUS", "0") not in ("", "0")
+
+
+def set_status_checks(enabled):
+    """With checks on, every operator that ran a waiting kernel reads its
+    device status word back (one 4-byte copy and a stream synchronisation)
+    and raises RuntimeError when a bounded device wait expired.  Off by
+    default: the common path never synchronises the host.  The environment
+    variable PISA_CHECK_STATUS=1 turns checks on at import."""
+    global _checked
+    _checked = bool(enabled)
+
+
+def status_checks():
+    return _checked
+
+
+def check_workspace(workspace, device):
+    """Raise RuntimeError if the call that used ``workspace`` hit an expired wait."""
+    if workspace is None:
+        return
+    with torch.cuda.device(device):
+        check(lib().pisa_workspace_status(ptr(workspace), stream_of(device)))
+
+
 def ptr(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def int64_array(values):
+    """A host int64[] for the ABI's level tables."""
+    values = [int(v) for v in values]
+    return (ctypes.c_int64 * max(1, len(values)))(*values)
 
 
 def stream_of(device):
@@ -95,7 +132,8 @@ def dtype_code(t):
         raise ValueError("the CUDA kernels support FP16, BF16 and FP32") from None
 
 
-KERNELS = {"leaf_tiles": 0, "attn_tiles": 1, "attn_combine": 2}
+KERNELS = {"leaf_tiles": 0, "attn_tiles": 1, "attn_combine": 2, "pyramid": 3, "dense_level": 4, "router": 5,
+           "leaf_final": 6}
 
 
 def kernel_timing(enable):

@@ -43,6 +43,8 @@ def attention_forward(q, k, v, indices, block_size, scale, positions, offset, ca
             tokens, q_heads, heads, dim, dim_v, length, indices.shape[-1], block_size, float(scale),
             int(bool(causal)), _lib.ptr(out), _lib.ptr(lse), _lib.ptr(workspace), ws_bytes,
             _lib.stream_of(q.device)))
+    if _lib.status_checks():
+        _lib.check_workspace(workspace, q.device)
     return out, lse
 
 

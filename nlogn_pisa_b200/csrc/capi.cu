@@ -197,7 +197,7 @@ static SelectPlan plan_select(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int6
   SelectPlan p;
   p.geo = level_geometry(N, C, br, top + 1);
   int64_t off = 0;
-  p.status_off = off;  // device status word (timeouts of bounded waits)
+  p.status_off = off;  // device status word (timeouts of bounded waits) at offset 0
   off += 256;
   if (build_summary) {
     p.pyramid_off = off;
@@ -315,6 +315,24 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
   if (!rows_aligned(q, dtype, q_sb, q_st, q_sh) || !rows_aligned(keys, dtype, key_sb, key_st, key_sh))
     return fail(PISA_ERR_UNSUPPORTED, "q and key rows must be 16-byte aligned");
 
+  if (summary != nullptr) {
+    if (!level_offsets || !level_sizes || num_levels < 1) return fail(PISA_ERR_INVALID, "pyramid level tables are required");
+    if (!rows_aligned(summary, dtype, summary_sb, H * D, D)) return fail(PISA_ERR_UNSUPPORTED, "summary rows must be 16-byte aligned");
+    // The tables must describe the pyramid of these keys for this block size
+    // and branching: ceil(N / C) leaves, then ceil(n / b) per level.  A table
+    // may end early only at a single node (it stays that node above).
+    {
+      const Geometry want = level_geometry(N, block_size, branching, std::min<int64_t>(num_levels, kMaxLevels));
+      for (int64_t l = 0; l < std::min<int64_t>(num_levels, kMaxLevels); ++l) {
+        if (level_sizes[l] != want.sizes[l])
+          return fail(PISA_ERR_INVALID, "pyramid level sizes do not match the keys, block_size and branching");
+        if (level_offsets[l] < 0) return fail(PISA_ERR_INVALID, "pyramid level offsets must be nonnegative");
+      }
+      if (num_levels < top + 1 && level_sizes[num_levels - 1] != 1)
+        return fail(PISA_ERR_INVALID, "pyramid has fewer levels than the routing depth");
+    }
+  }
+
   const SelectPlan plan = plan_select(B, Tq, Hq, H, D, N, dtype, method, block_size, branching,
                                       topk, top, first_width, schedule, summary == nullptr);
   if (plan.total > 0 && (!workspace || workspace_bytes < plan.total))
@@ -335,8 +353,6 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
     a.s_sb = g.total * H * D;
     for (int l = 0; l <= top; ++l) { a.levels.offset[l] = g.offsets[l]; a.levels.size[l] = int32_t(g.sizes[l]); }
   } else {
-    if (!level_offsets || !level_sizes || num_levels < 1) return fail(PISA_ERR_INVALID, "pyramid level tables are required");
-    if (!rows_aligned(summary, dtype, summary_sb, H * D, D)) return fail(PISA_ERR_UNSUPPORTED, "summary rows must be 16-byte aligned");
     a.summary = summary;
     a.s_sb = summary_sb;
     // A one-node local pyramid remains that node at additional common levels
@@ -461,13 +477,170 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
 
 namespace pisa {
 
+// Workspace layout of pisa_leaf_scores: status word, int32 ids, masks, then
+// either the leaf means (pisa1 without caller means) or the buckets and tile
+// list of the grouped tensor-core scorer (one family per candidate block).
+struct LeafPlan {
+  bool tc = false;
+  int64_t rows = 0, blocks = 0, nwin = 0, TW = 4096, RT = 0, num_buckets = 0, capacity = 0;
+  int64_t status_off = 0, cand_off = 0, flags_off = 0, means_off = -1, counts_off = 0, cursors_off = 0,
+          offsets_off = 0, misc_off = 0, owner_off = 0, req_off = 0, total = 0;
+};
+
+static LeafPlan plan_leaf(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t N, int64_t W,
+                          int dtype, int method, int64_t C, bool have_means) {
+  LeafPlan p;
+  p.rows = B * Tq * H;
+  p.blocks = (N + C - 1) / C;
+  int64_t off = 0;
+  p.status_off = off; off += 256;
+  p.cand_off = off; off += align_up(p.rows * W * 4, 256);
+  p.flags_off = off; off += align_up(p.rows * W, 256);
+  p.tc = grouped_tc_eligible(Hq, H, D, dtype, method, C, 1, PISA_SCHEDULE_GROUPED) && C <= 256;
+  if (p.tc) {
+    p.RT = 128 / (Hq / H);
+    p.nwin = (Tq + p.TW - 1) / p.TW;
+    p.num_buckets = B * p.nwin * H * p.blocks;
+    p.capacity = (p.rows * W + p.RT - 1) / p.RT + p.num_buckets;
+    if (p.rows * W >= (int64_t(1) << 31) || p.capacity * p.RT >= (int64_t(1) << 31) ||
+        p.num_buckets >= (int64_t(1) << 31))
+      p.tc = false;
+  }
+  if (p.tc) {
+    p.counts_off = off; off += align_up(p.num_buckets * 4, 256);
+    p.cursors_off = off; off += align_up(p.num_buckets * 4, 256);
+    p.offsets_off = off; off += align_up(p.num_buckets * 4, 256);
+    p.misc_off = off; off += 256;
+    p.owner_off = off; off += align_up(p.capacity * 4, 256);
+    p.req_off = off; off += align_up(p.capacity * p.RT * 4, 256);
+  } else if (method == PISA_METHOD_PISA1 && !have_means) {
+    p.means_off = off; off += align_up(B * p.blocks * H * D * elem_size(dtype), 256);
+  }
+  p.total = off;
+  return p;
+}
+
+}  // namespace pisa
+
+extern "C" {
+
+int64_t pisa_leaf_scores_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t N,
+                                         int64_t W, int dtype, int method, int64_t block_size,
+                                         int have_means) {
+  if (B <= 0 || Tq <= 0 || Hq <= 0 || H <= 0 || D <= 0 || N <= 0 || W < 0 || block_size < 1 || Hq % H) return 0;
+  return plan_leaf(B, Tq, Hq, H, D, N, W, dtype, method, block_size, have_means != 0).total;
+}
+
+int pisa_leaf_scores(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, const void* keys,
+                     int64_t key_sb, int64_t key_st, int64_t key_sh, const void* leaf_means,
+                     int64_t means_sb, const void* candidates, int cand_bytes, const int64_t* positions,
+                     int dtype, int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t N,
+                     int64_t W, int method, int64_t block_size, int64_t topk, int force_first,
+                     int64_t force_recent, float* out_scores, void* workspace, int64_t workspace_bytes,
+                     pisa_stream_t stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype < PISA_F32 || dtype > PISA_F16) return fail(PISA_ERR_UNSUPPORTED, "grouped leaf scoring supports FP16, BF16 and FP32");
+  if (method < PISA_METHOD_PISA1 || method > PISA_METHOD_PISA) return fail(PISA_ERR_INVALID, "expected method pisa1/pisa2/pisa");
+  if (block_size <= 0) return fail(PISA_ERR_INVALID, "block_size must be positive");
+  if (B <= 0 || Tq <= 0 || Hq <= 0 || H <= 0 || D <= 0 || N <= 0 || W < 0) return fail(PISA_ERR_INVALID, "nonempty tensors are required");
+  if (Hq % H) return fail(PISA_ERR_INVALID, "a whole number of query heads per KV head is required");
+  if (Hq / H > 32) return fail(PISA_ERR_UNSUPPORTED, "at most 32 query heads per KV head");
+  if (D % 8 || D > 256) return fail(PISA_ERR_UNSUPPORTED, "head_dim must be a multiple of 8 and at most 256");
+  if (cand_bytes != 4 && cand_bytes != 8) return fail(PISA_ERR_INVALID, "candidates must be int32 or int64");
+  if (positions && method != PISA_METHOD_PISA1 && topk < 0) return fail(PISA_ERR_INVALID, "topk is required with positions");
+  if (positions && force_recent < 0) return fail(PISA_ERR_INVALID, "force_recent must be nonnegative");
+  if (!out_scores || (W > 0 && !candidates)) return fail(PISA_ERR_INVALID, "candidates and out_scores are required");
+  if (!rows_aligned(q, dtype, q_sb, q_st, q_sh) || !rows_aligned(keys, dtype, key_sb, key_st, key_sh))
+    return fail(PISA_ERR_UNSUPPORTED, "q and key rows must be 16-byte aligned");
+  if (leaf_means && !rows_aligned(leaf_means, dtype, means_sb, H * D, D))
+    return fail(PISA_ERR_UNSUPPORTED, "leaf mean rows must be 16-byte aligned");
+  if (W == 0) return PISA_OK;
+  const LeafPlan plan = plan_leaf(B, Tq, Hq, H, D, N, W, dtype, method, block_size, leaf_means != nullptr);
+  if (!workspace || workspace_bytes < plan.total) return fail(PISA_ERR_INVALID, "workspace too small");
+  char* ws = static_cast<char*>(workspace);
+  cudaError_t e = cudaMemsetAsync(ws + plan.status_off, 0, 256, s);
+  if (e != cudaSuccess) return fail_cuda(e, "status clear");
+
+  LeafPrepArgs p{};
+  p.cand = candidates; p.cand_bytes = cand_bytes; p.positions = positions;
+  p.B = int(B); p.T = int(Tq); p.H = int(H); p.W = int(W); p.C = int(block_size);
+  p.K = int(topk); p.method = method; p.force_first = force_first ? 1 : 0; p.force_recent = int(force_recent);
+  p.blocks = plan.blocks;
+  p.cand_out = reinterpret_cast<int32_t*>(ws + plan.cand_off);
+  p.flags = reinterpret_cast<uint8_t*>(ws + plan.flags_off);
+  p.scores = out_scores;
+  int rc = leaf_prepare(p, s);
+  if (rc) return rc;
+  const double scale = 1.0 / std::sqrt(double(D));
+
+  if (!plan.tc) {
+    RouteArgs a{};
+    a.q = q; a.q_sb = q_sb; a.q_st = q_st; a.q_sh = q_sh;
+    a.keys = keys; a.k_sb = key_sb; a.k_st = key_st; a.k_sh = key_sh;
+    a.B = int(B); a.T = int(Tq); a.H = int(H); a.G = int(Hq / H); a.D = int(D); a.N = int(N);
+    a.C = int(block_size); a.method = method; a.scale = float(scale); a.c2 = float(0.5 * scale * scale);
+    a.levels.size[0] = int32_t(plan.blocks);
+    const void* means = leaf_means;
+    int64_t msb = means_sb;
+    if (method == PISA_METHOD_PISA1 && !means) {
+      // leaf means of these keys (fp32 accumulation), as mean_pool(k, block_size)
+      const int64_t zero = 0;
+      rc = build_pyramid(keys, dtype, B, N, H, D, key_sb, key_st, key_sh, block_size, 2, 1,
+                         ws + plan.means_off, plan.blocks * H * D, &zero, 0, s);
+      if (rc) return rc;
+      means = ws + plan.means_off;
+      msb = plan.blocks * H * D;
+    }
+    return leaf_scores_simt(a, p.cand_out, p.flags, int(W), out_scores, means, msb, dtype, s);
+  }
+
+  GroupArgs g{};
+  g.q = q; g.q_sb = q_sb; g.q_st = q_st; g.q_sh = q_sh;
+  g.keys = keys; g.k_sb = key_sb; g.k_st = key_st; g.k_sh = key_sh;
+  g.B = int(B); g.T = int(Tq); g.H = int(H); g.G = int(Hq / H); g.D = int(D);
+  g.Dp = int(D <= 64 ? 64 : D <= 128 ? 128 : 256); g.N = int(N); g.C = int(block_size); g.K = int(topk);
+  // one family per candidate block: W slots of one child each, bucketed by block id
+  g.br = 1; g.W0 = int(W); g.NF = int(W); g.NP = int(plan.blocks);
+  g.nwin = int(plan.nwin); g.TW = int(plan.TW); g.RT = int(plan.RT);
+  g.method = method; g.bf16 = dtype == PISA_BF16 ? 1 : 0;
+  g.scale = float(scale); g.c2 = float(0.5 * scale * scale);
+  g.cand = p.cand_out; g.flags = p.flags; g.scores = out_scores;
+  g.counts = reinterpret_cast<int32_t*>(ws + plan.counts_off);
+  g.cursors = reinterpret_cast<int32_t*>(ws + plan.cursors_off);
+  g.offsets = reinterpret_cast<int32_t*>(ws + plan.offsets_off);
+  g.num_buckets = plan.num_buckets;
+  g.total_tiles_w = reinterpret_cast<int32_t*>(ws + plan.misc_off);
+  g.total_tiles = g.total_tiles_w;
+  g.status = reinterpret_cast<int*>(ws + plan.status_off);
+  g.tile_owner_w = reinterpret_cast<int32_t*>(ws + plan.owner_off);
+  g.tile_owner = g.tile_owner_w;
+  g.tile_req_w = reinterpret_cast<int32_t*>(ws + plan.req_off);
+  g.tile_req = g.tile_req_w;
+  g.tile_capacity = plan.capacity;
+  g.tiles_per_cta = 8;
+  g.counts_ready = 0;
+  g.skip_final = 1;
+  const int64_t nk = block_size;
+  const int64_t want = 2 * nk;
+  g.tmem_cols = want <= 32 ? 32 : want <= 64 ? 64 : want <= 128 ? 128 : want <= 256 ? 256 : 512;
+  g.num_sms = num_sms();
+  rc = make_tensor_map(&g.tm_q, q, dtype, B, Tq, Hq, D, q_sb, q_st, q_sh, uint32_t(g.G), 1);
+  if (rc == PISA_OK) rc = make_tensor_map(&g.tm_k, keys, dtype, B, N, H, D, key_sb, key_st, key_sh, 1, uint32_t(nk));
+  if (rc) return rc;
+  return grouped_leaf(g, dtype, s);
+}
+
+}  // extern "C"
+
+namespace pisa {
+
 // Workspace layout of the bucketed tensor-core attention forward (one token
 // chunk at a time; the partials of a chunk are bounded to about 4 GiB: 12288-token chunks at the benchmark shape).
 struct AttnPlan {
   bool tc = false;
   int64_t TW = 4096, chunk = 0, NB = 0, RT = 0, num_buckets = 0, capacity = 0;
   int64_t sp_cols = 0, o_cols = 0, tmem_cols = 0, nacc = 1, nstages = 2;
-  int64_t counts_off = 0, cursors_off = 0, offsets_off = 0, misc_off = 0, owner_off = 0,
+  int64_t status_off = 0, counts_off = 0, cursors_off = 0, offsets_off = 0, misc_off = 0, owner_off = 0,
           req_off = 0, po_off = 0, pml_off = 0, total = 0;
 };
 
@@ -509,6 +682,7 @@ static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t 
   // tile slots (tile * RT + slot) are decoded as 31-bit numbers
   if (p.capacity * p.RT >= (int64_t(1) << 31)) { p.tc = false; return p; }
   int64_t off = 0;
+  p.status_off = off; off += 256;  // device status word (timeouts of bounded waits) at offset 0
   p.counts_off = off; off += align_up(p.num_buckets * 4, 256);
   p.cursors_off = off; off += align_up(p.num_buckets * 4, 256);
   p.offsets_off = off; off += align_up(p.num_buckets * 4, 256);
@@ -571,7 +745,11 @@ int pisa_sparse_attn_fwd(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh
     a.cursors = reinterpret_cast<int32_t*>(ws + plan.cursors_off);
     a.offsets = reinterpret_cast<int32_t*>(ws + plan.offsets_off);
     a.total_tiles = reinterpret_cast<int32_t*>(ws + plan.misc_off);
-    a.status = reinterpret_cast<int*>(ws + plan.misc_off + 4);
+    a.status = reinterpret_cast<int*>(ws + plan.status_off);
+    {
+      cudaError_t e = cudaMemsetAsync(ws + plan.status_off, 0, 256, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return fail_cuda(e, "status clear");
+    }
     a.tile_owner = reinterpret_cast<int32_t*>(ws + plan.owner_off);
     a.tile_req = reinterpret_cast<int32_t*>(ws + plan.req_off);
     a.part_o = ws + plan.po_off;

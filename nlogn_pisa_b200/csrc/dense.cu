@@ -172,6 +172,7 @@ int dense_level(const DenseArgs& a, int dtype, cudaStream_t stream) {
   if (e != cudaSuccess) return fail_cuda(e, "dense level smem attribute");
   const int tt = 128 / a.G;
   dim3 grid(unsigned((a.t_count + tt - 1) / tt), unsigned(a.H), unsigned(a.B));
+  TimedLaunch timed(PISA_KERNEL_DENSE_LEVEL, stream);
   kernel<<<grid, kThreads, smem, stream>>>(a);
   PISA_CHECK_LAUNCH();
   return PISA_OK;

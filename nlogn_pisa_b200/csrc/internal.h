@@ -125,9 +125,29 @@ struct GroupArgs {
   FastDiv fNF, fH, fT, fNP, fTW, fRT, fbr, fnwin;
   int64_t* out_ids;
   int* status;
+  int skip_final;     // 1: stop after the tile kernel (scores only, no top-K)
 };
 
 int grouped_leaf(const GroupArgs& g, int dtype, cudaStream_t stream);
+
+// Masks, int32 ids and -inf fills of the standalone leaf scorer (leafscore.cu).
+struct LeafPrepArgs {
+  const void* cand;            // [B, T, H, W] int32 or int64, contiguous
+  int cand_bytes;
+  const int64_t* positions;    // [B, T] or null (no causal / forced masks)
+  int B, T, H, W, C, K, method, force_first, force_recent;
+  int64_t blocks;
+  int32_t* cand_out;           // [B, T, H, W]
+  uint8_t* flags;              // bit0 valid, bit1 forced, bit2 scoreable
+  float* scores;               // [B, T, H, W]: -inf written for unscored slots
+};
+
+int leaf_prepare(const LeafPrepArgs& p, cudaStream_t stream);
+
+// SIMT scores of the scoreable slots (any dtype, all three methods); `means`
+// ([B, blocks, H, D], node stride H*D, batch stride means_sb) for pisa1.
+int leaf_scores_simt(const RouteArgs& a, const int32_t* cand, const uint8_t* flags, int W, float* scores,
+                     const void* means, int64_t means_sb, int dtype, cudaStream_t stream);
 
 // Dense scoring of every node of one coarse level (see dense.cu).
 struct DenseArgs {

@@ -476,7 +476,9 @@ int grouped_leaf(const GroupArgs& args, int dtype, cudaStream_t stream) {
     PISA_CHECK_LAUNCH();
   }
 
+  if (g.skip_final) return PISA_OK;
   const unsigned fgrid = unsigned((rows + 3) / 4);
+  TimedLaunch timed(PISA_KERNEL_LEAF_FINAL, stream);
   switch (g.W0) {
     case 16: leaf_final_kernel<16><<<fgrid, 128, 0, stream>>>(g); break;
     case 32: leaf_final_kernel<32><<<fgrid, 128, 0, stream>>>(g); break;

@@ -8,8 +8,10 @@
 // whose device memory is fully planned in advance, where an extra
 // cudaMalloc would fail or break the plan.  For them this file keeps the
 // accumulators in one fixed device array that lives in the library image:
-// kScratchBytes (32 MiB) on every GPU that loads the library, held until the
-// process exits.  The entry point itself calls no allocator.
+// kScratchBytes (32 MiB) per GPU, held until the process exits.  With lazy
+// module loading (the CUDA default since 12.2) the array is reserved on a
+// device when the first call there looks up its address, not when the
+// library is loaded.  The entry point itself calls no allocator.
 #include <cstdio>
 #include <mutex>
 
@@ -64,11 +66,21 @@ int pisa_sparse_attn_bwd_noalloc(const void* q, const void* k, const void* v, co
   if (need > pisa::kScratchBytes) {
     char msg[200];
     snprintf(msg, sizeof msg,
-             "pisa_sparse_attn_bwd_noalloc: these shapes need %lld bytes of dK/dV accumulators, above the "
-             "fixed %lld-byte scratch (B*N*H*(D+Dv) at most %lld values); use pisa_sparse_attn_bwd",
-             static_cast<long long>(need), static_cast<long long>(pisa::kScratchBytes),
-             static_cast<long long>(pisa::kScratchBytes / 4));
+             "pisa_sparse_attn_bwd_noalloc: these shapes need %lld bytes of dK/dV accumulators "
+             "(pisa_sparse_attn_bwd_workspace_bytes), above the fixed %lld-byte scratch "
+             "(pisa_sparse_attn_bwd_noalloc_max_bytes); use pisa_sparse_attn_bwd",
+             static_cast<long long>(need), static_cast<long long>(pisa::kScratchBytes));
     return pisa::fail(PISA_ERR_UNSUPPORTED, msg);
+  }
+  // The array is looked up for the current device while the kernels run on
+  // the stream's device: the two must be the same GPU.
+  {
+    int cur = 0, sdev = 0;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e == cudaSuccess) e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev);
+    if (e != cudaSuccess) return pisa::fail_cuda(e, "pisa_sparse_attn_bwd_noalloc: stream device");
+    if (cur != sdev)
+      return pisa::fail(PISA_ERR_INVALID, "pisa_sparse_attn_bwd_noalloc: the current device must be the stream's device");
   }
   void* scratch = nullptr;
   const int rc = pisa::scratch_address(&scratch);

@@ -93,6 +93,7 @@ static int pyramid_impl(const void* keys, int64_t B, int64_t N, int64_t H, int64
                         void* storage, int64_t ssb, const int64_t* offs, int64_t first_token,
                         cudaStream_t stream) {
   const int threads = 128;
+  TimedLaunch timed(PISA_KERNEL_PYRAMID, stream);
   int64_t n = (N + C - 1) / C;
   int64_t first = first_token / C;
   if (n - first > 0) {

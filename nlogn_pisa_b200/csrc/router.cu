@@ -18,6 +18,7 @@
 // per-lane running max / sum of exponentials).  Warp 0 runs the network in
 // registers (element i in lane i%32, slot i/32).
 #include "internal.h"
+#include "score.cuh"
 
 namespace pisa {
 
@@ -25,152 +26,6 @@ namespace {
 
 constexpr int kThreads = 128;
 constexpr int kMaxWidth = 256;
-
-template <typename T, int GMAX>
-__device__ __forceinline__ void row_dots(const T* __restrict__ row, const float* __restrict__ qs,
-                                         int G, int D, float (&acc)[GMAX]) {
-  constexpr int V = Vec<T>::N;
-#pragma unroll
-  for (int g = 0; g < GMAX; ++g) acc[g] = 0.f;
-  for (int d = 0; d < D; d += V) {
-    float x[V];
-    load_vec<T>(row + d, x);
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-      if (g < G) {
-        const float* qg = qs + g * D + d;
-#pragma unroll
-        for (int i = 0; i < V; i += 4) {
-          const float4 qv = *reinterpret_cast<const float4*>(qg + i);
-          acc[g] = fmaf(qv.x, x[i + 0], acc[g]);
-          acc[g] = fmaf(qv.y, x[i + 1], acc[g]);
-          acc[g] = fmaf(qv.z, x[i + 2], acc[g]);
-          acc[g] = fmaf(qv.w, x[i + 3], acc[g]);
-        }
-      }
-    }
-  }
-}
-
-// Score of one coarse candidate (level >= 1) from its `br` child summaries,
-// or of one node (pisa1, support 1).  Thread-local.
-template <typename T, int GMAX>
-__device__ float coarse_score(const RouteArgs& a, const T* level_base, int child_len, int id,
-                              const float* qs) {
-  const int64_t node_stride = int64_t(a.H) * a.D;
-  float acc[GMAX];
-  if (a.method == PISA_METHOD_PISA1) {
-    row_dots<T, GMAX>(level_base + int64_t(id) * node_stride, qs, a.G, a.D, acc);
-    float score = 0.f;
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g)
-      if (g < a.G) score += acc[g];
-    return score;
-  }
-  // pisa: running max m / scaled sum s; pisa2 binary: z0, z1; pisa2 general:
-  // sum of products s1 and of squares s2.
-  float m[GMAX], s[GMAX], z0[GMAX], z1[GMAX], s1[GMAX], s2[GMAX];
-#pragma unroll
-  for (int g = 0; g < GMAX; ++g) {
-    m[g] = -INFINITY; s[g] = 0.f; z0[g] = 0.f; z1[g] = 0.f; s1[g] = 0.f; s2[g] = 0.f;
-  }
-  int count = 0;
-  const bool binary = a.br == 2;
-  float score = 0.f;
-  for (int j = 0; j < a.br; ++j) {
-    const int c = id * a.br + j;
-    if (c >= child_len) break;
-    row_dots<T, GMAX>(level_base + int64_t(c) * node_stride, qs, a.G, a.D, acc);
-    ++count;
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-      if (g >= a.G) continue;
-      if (a.method == PISA_METHOD_PISA) {
-        const float z = acc[g] * a.scale;
-        if (z > m[g]) { s[g] = s[g] * expf(m[g] - z) + 1.f; m[g] = z; }
-        else { s[g] += expf(z - m[g]); }
-      } else if (binary) {
-        const float z = acc[g] * a.scale;
-        if (j == 0) z0[g] = z; else z1[g] = z;
-      } else {
-        s1[g] += acc[g];
-        s2[g] += acc[g] * acc[g];
-      }
-    }
-  }
-  const float cnt = float(count > 0 ? count : 1);
-#pragma unroll
-  for (int g = 0; g < GMAX; ++g) {
-    if (g >= a.G) continue;
-    if (a.method == PISA_METHOD_PISA) {
-      score += m[g] + logf(s[g]);
-    } else if (binary) {
-      const float total = z0[g] + z1[g];
-      const float diff = z0[g] - z1[g];
-      score += count == 2 ? 0.5f * total + 0.125f * diff * diff : total;
-    } else {
-      const float mean = s1[g] / cnt;
-      const float second = s2[g] / cnt;
-      const float var = fmaxf(second - mean * mean, 0.f);
-      score += a.scale * mean + a.c2 * var;
-    }
-  }
-  return score;
-}
-
-// Score of one leaf candidate from its C raw keys; executed by a whole warp.
-template <typename T, int GMAX>
-__device__ float leaf_score_warp(const RouteArgs& a, const T* key_base, int id, const float* qs,
-                                 int lane) {
-  float m[GMAX], s[GMAX], s2[GMAX], acc[GMAX];
-#pragma unroll
-  for (int g = 0; g < GMAX; ++g) { m[g] = -INFINITY; s[g] = 0.f; s2[g] = 0.f; }
-  int count = 0;
-  const int64_t first = int64_t(id) * a.C;
-  for (int kk = lane; kk < a.C; kk += 32) {
-    const int64_t tok = first + kk;
-    if (tok >= a.N) break;
-    row_dots<T, GMAX>(key_base + tok * a.k_st, qs, a.G, a.D, acc);
-    ++count;
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-      if (g >= a.G) continue;
-      if (a.method == PISA_METHOD_PISA) {
-        const float z = acc[g] * a.scale;
-        if (z > m[g]) { s[g] = s[g] * expf(m[g] - z) + 1.f; m[g] = z; }
-        else { s[g] += expf(z - m[g]); }
-      } else {
-        s[g] += acc[g];
-        s2[g] += acc[g] * acc[g];
-      }
-    }
-  }
-  float score = 0.f;
-  if (a.method == PISA_METHOD_PISA) {
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-      if (g >= a.G) continue;
-      const float M = warp_max(m[g]);
-      const float part = m[g] == -INFINITY ? 0.f : s[g] * expf(m[g] - M);
-      const float S = warp_sum(part);
-      score += M + logf(S);
-    }
-  } else {
-    int total = count;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(kFull, total, o);
-    const float cnt = float(total > 0 ? total : 1);
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-      if (g >= a.G) continue;
-      const float mean = warp_sum(s[g]) / cnt;
-      const float second = warp_sum(s2[g]) / cnt;
-      const float var = fmaxf(second - mean * mean, 0.f);
-      score += a.scale * mean + a.c2 * var;
-    }
-  }
-  return score;
-}
 
 template <int WP>
 __device__ __forceinline__ void network_step(float* sc, int* ids, int width, int K, int br,
@@ -469,6 +324,7 @@ int launch_route(const RouteArgs& a, cudaStream_t stream) {
   }
   const int64_t items = int64_t(a.B) * a.t_count * a.H;
   if (items == 0) return PISA_OK;
+  TimedLaunch timed(PISA_KERNEL_ROUTER, stream);
   kernel<<<unsigned(items), kThreads, smem, stream>>>(a);
   PISA_CHECK_LAUNCH();
   return PISA_OK;
@@ -504,6 +360,7 @@ int route(const RouteArgs& a, int dtype, cudaStream_t stream, bool* counted) {
     w.fbr = FastDiv::make(uint32_t(a.br));
     w.fH = FastDiv::make(uint32_t(a.H));
     w.ftc = FastDiv::make(uint32_t(a.t_count));
+    TimedLaunch timed(PISA_KERNEL_ROUTER, stream);
     route_warp_kernel<<<unsigned((items + 3) / 4), 128, 0, stream>>>(w);
     PISA_CHECK_LAUNCH();
     if (counted) *counted = a.fam_counts != nullptr;

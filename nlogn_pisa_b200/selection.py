@@ -12,14 +12,11 @@ reference's only value) additionally allows a 4-ary pyramid.
 
 from __future__ import annotations
 
-import ctypes
-
 import torch
 
 from . import _lib
+from .layout import check_level_sizes, full_level_sizes, level_sizes
 from .validation import packed_queries, query_positions, require_cuda, validate_qkv
-
-_INT64_ARRAY = ctypes.c_int64 * 32
 
 
 def routing_geometry(blocks, topk, branching=2):
@@ -34,14 +31,6 @@ def routing_geometry(blocks, topk, branching=2):
     return top, max(16, 1 << (max(blocks, topk) - 1).bit_length())
 
 
-def level_sizes(leaves, branching, levels):
-    sizes, n = [], leaves
-    for _ in range(levels):
-        sizes.append(n)
-        n = -(-n // branching)
-    return sizes
-
-
 def _rows16(t):
     """t itself when its rows are 16-byte aligned with a unit last stride, else a contiguous copy."""
     vec = 16 // t.element_size()
@@ -50,11 +39,7 @@ def _rows16(t):
     return t if ok else t.contiguous()
 
 
-def _c_array(values):
-    arr = _INT64_ARRAY()
-    for i, v in enumerate(values):
-        arr[i] = int(v)
-    return arr
+_c_array = _lib.int64_array
 
 
 def mean_pool(keys, size, *, backend="auto", fp32_accumulation=False):
@@ -103,9 +88,9 @@ def build_pyramid(keys, block_size, *, backend="auto", max_level=None, branching
     code = _lib.dtype_code(keys)
     keys = _rows16(keys)
     batch, length, heads, dim = keys.shape
-    sizes = [-(-length // block_size)]
-    while sizes[-1] > 1 and (max_level is None or len(sizes) <= max_level):
-        sizes.append(-(-sizes[-1] // branching))
+    sizes = full_level_sizes(-(-length // block_size), branching)
+    if max_level is not None:
+        sizes = sizes[:max_level + 1]
     offsets = [0]
     for s in sizes[:-1]:
         offsets.append(offsets[-1] + s)
@@ -166,16 +151,31 @@ def select_blocks(q, k, method="pisa", block_size=64, topk=8, cu_seqlens=None, q
 
 
 def _pyramid_tables(pyramid, k, block_size, top, branching):
-    """(storage, batch_stride, offsets, sizes) for a caller-supplied pyramid, or Nones."""
+    """(storage, batch_stride, offsets, sizes) for a caller-supplied pyramid, or Nones.
+
+    The level sizes must be those of ``k``'s keys for this block size and
+    branching (a binary pyramid queried with branching 4, or a pyramid of
+    other keys, raises ValueError instead of routing over the wrong tree).
+    """
     if pyramid is None:
         return None, 0, None, None
     if hasattr(pyramid, "storage"):
         storage = pyramid.storage
-        sizes = list(pyramid.level_sizes)
+        sizes = [int(x) for x in pyramid.level_sizes]
         starts = getattr(pyramid, "starts", None)
         offsets = list(starts) if starts is not None else [int(x) for x in pyramid.offsets.tolist()]
+        if len(offsets) < len(sizes):
+            raise ValueError("pyramid offsets must cover every level")
+        _check_summary(storage, k)
+        check_level_sizes(sizes, k.shape[1], block_size, branching, top + 1)
         return _rows16_storage(storage), storage.stride(0), offsets[:len(sizes)], sizes
     levels = list(pyramid.levels if hasattr(pyramid, "levels") else pyramid)
+    if not levels:
+        raise ValueError("pyramid has no levels")
+    for level in levels:
+        _check_summary(level, k)
+    sizes = [x.shape[1] for x in levels]
+    check_level_sizes(sizes, k.shape[1], block_size, branching, top + 1)
     levels = levels + [levels[-1]] * max(0, top + 1 - len(levels))
     summary = torch.cat(levels, dim=1).contiguous()
     sizes = [x.shape[1] for x in levels]
@@ -185,10 +185,10 @@ def _pyramid_tables(pyramid, k, block_size, top, branching):
     return summary, summary.stride(0), offsets, sizes
 
 
-def _rows16_storage(storage):
-    if storage.stride(-1) != 1 or storage.stride(-2) != storage.shape[-1] or storage.stride(1) != storage.shape[-1] * storage.shape[-2]:
-        raise ValueError("pyramid storage must be contiguous per node ([B, total, H, D])")
-    return storage
+def _check_summary(t, k):
+    if (t.ndim != 4 or t.shape[0] != k.shape[0] or t.shape[2:] != k.shape[2:] or t.dtype != k.dtype
+            or t.device != k.device):
+        raise ValueError("pyramid levels must be [B, nodes, Hkv, D] tensors like the keys")
 
 
 def _select_unpacked(q, k, method, block_size, topk, query_offset, force_first, force_recent,
@@ -223,6 +223,71 @@ def _select_unpacked(q, k, method, block_size, topk, query_offset, force_first, 
             heads, dim, length, _lib.METHODS[method], block_size, branching, topk,
             int(bool(force_first)), force_recent, top, first_width, schedule, _lib.ptr(out),
             _lib.ptr(workspace), ws_bytes, _lib.stream_of(q.device)))
+    if _lib.status_checks():
+        _lib.check_workspace(workspace, q.device)
+    return out
+
+
+@torch.no_grad()
+def grouped_leaf_scores(q, k, candidates, block_size, method, tile_size=4, *, positions=None, topk=None,
+                        force_first=True, force_recent=2, leaf_means=None, num_warps=None,
+                        num_stages=None):
+    """FP32 leaf scores [B,Tq,Hkv,W] in the order of ``candidates`` (-inf where unscored).
+
+    Arguments as the reference's grouped_leaf_scores.  ``tile_size``,
+    ``num_warps`` and ``num_stages`` are accepted for compatibility (the
+    bucketed tensor-core scorer packs 128/G requests per tile whatever they
+    are).  With ``positions`` ([B,Tq] or broadcastable int64), ids past the
+    query's position, forced ids and rows whose valid ids all fit in
+    ``topk`` are not scored.
+    """
+    validate_qkv(q, k)
+    require_cuda(q, k)
+    if q.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        raise ValueError("grouped leaf scoring supports FP16, BF16 and FP32")
+    if method not in ("pisa1", "pisa2", "pisa") or tile_size not in (1, 2, 4):
+        raise ValueError("expected method pisa1/pisa2/pisa and tile_size 1/2/4")
+    if block_size <= 0:
+        raise ValueError("block_size must be positive")
+    if candidates.ndim != 4 or candidates.shape[:3] != (*q.shape[:2], k.shape[2]):
+        raise ValueError("candidates must have shape [B,Tq,Hkv,W]")
+    if candidates.dtype not in (torch.int32, torch.int64) or candidates.device != q.device:
+        raise ValueError("candidates must use an integer dtype on the query device")
+    if positions is not None:
+        if method != "pisa1" and topk is None:
+            raise ValueError("topk is required with positions for pisa and pisa2")
+        positions = torch.broadcast_to(positions.to(device=q.device, dtype=torch.int64),
+                                       q.shape[:2]).contiguous()
+    code = _lib.dtype_code(q)
+    q, k = _rows16(q), _rows16(k)
+    candidates = candidates.contiguous()
+    batch, tokens, q_heads, dim = q.shape
+    heads, length, width = k.shape[2], k.shape[1], candidates.shape[-1]
+    means_sb = 0
+    if leaf_means is not None and method == "pisa1":
+        blocks = -(-length // block_size)
+        if (leaf_means.shape[0] != batch or leaf_means.shape[1] < blocks or leaf_means.shape[2:] != k.shape[2:]
+                or leaf_means.dtype != q.dtype or leaf_means.device != q.device):
+            raise ValueError("leaf_means must be [B, blocks, Hkv, D] like the keys")
+        if leaf_means.stride(-1) != 1 or leaf_means.stride(-2) != dim or leaf_means.stride(1) != heads * dim:
+            leaf_means = leaf_means.contiguous()
+        means_sb = leaf_means.stride(0)
+    else:
+        leaf_means = None
+    library = _lib.lib()
+    ws_bytes = library.pisa_leaf_scores_workspace_bytes(batch, tokens, q_heads, heads, dim, length, width, code,
+                                                        _lib.METHODS[method], block_size, int(leaf_means is not None))
+    workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+    out = torch.empty(candidates.shape, dtype=torch.float32, device=q.device)
+    with torch.cuda.device(q.device):
+        _lib.check(library.pisa_leaf_scores(
+            _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3], _lib.ptr(leaf_means), means_sb,
+            _lib.ptr(candidates), candidates.element_size(), _lib.ptr(positions), code, batch, tokens,
+            q_heads, heads, dim, length, width, _lib.METHODS[method], block_size,
+            -1 if topk is None else int(topk), int(bool(force_first)), int(force_recent), _lib.ptr(out),
+            _lib.ptr(workspace), ws_bytes, _lib.stream_of(q.device)))
+    if _lib.status_checks():
+        _lib.check_workspace(workspace, q.device)
     return out
 
 

@@ -12,6 +12,7 @@ Every function restates the reference algorithm of Aphelios-Tang/NlogN_PISA
                              pisa/pisa/ops/compress/mean_pooling/mean_pooling.py:45-52
 * routing geometry/masks  -> pisa/pisa/ops/flash_sparse_attn/top_k_pyramid/top_k_pyramid_torch.py:6-14,114-133
 * candidate scoring       -> top_k_pyramid_torch.py:48-80
+* leaf scores of arbitrary candidates -> pisa/pisa/ops/flash_sparse_attn/top_k_pyramid/leaf_triton.py:23-60,144-232
 * bitonic top-K network   -> top_k_pyramid_torch.py:84-110
 * coarse-to-fine descent  -> top_k_pyramid_torch.py:137-177
 * query positions         -> pisa/pisa/utils/validation.py:38-56
@@ -205,6 +206,50 @@ def block_scores(query, source, ids, support, method, scale):
                 variance = np.maximum(second - mean * mean, 0)
                 score = sc * mean + acc(0.5 * scale * scale) * variance
     return score.sum(2).astype(acc)
+
+
+def leaf_scores(q, k, candidates, block_size, method, positions=None, topk=None, force_first=True,
+                force_recent=2, leaf_means=None, dtype="f32"):
+    """grouped_leaf_scores (leaf_triton.py:144-232): fp32 scores of arbitrary
+    leaf candidates in candidate order, -inf where a slot is not scored.
+
+    Slots with ids outside [0, blocks) are not scored (bucket_kernel,
+    grouping_triton.py:34-36).  With ``positions`` [B, T] the level-0 masks of
+    leaf_scoreable_mask (leaf_triton.py:23-60 -> score_masks,
+    top_k_pyramid_triton.py:105-122) also drop ids past the position, forced
+    ids and, for pisa / pisa2, rows whose valid ids all fit in ``topk``.
+    Scores are block_scores (top_k_pyramid_torch.py:48-80) over the C raw keys
+    (pisa, pisa2; scale D^-0.5) or over the leaf mean (pisa1; scale 1).
+    """
+    batch, tokens, q_heads, dim = q.shape
+    heads, length = k.shape[2], k.shape[1]
+    groups = q_heads // heads
+    blocks = -(-length // block_size)
+    ids = candidates.astype(np.int64)
+    in_range = (ids >= 0) & (ids < blocks)
+    if positions is None:
+        scoreable = in_range
+    else:
+        pos = np.broadcast_to(np.asarray(positions, np.int64), (batch, tokens))
+        pos = np.broadcast_to(pos[..., None], (batch, tokens, heads))
+        valid = in_range & (ids * block_size <= pos[..., None])
+        forced = force_mask(np.where(in_range, ids, -1), pos, block_size, force_first, force_recent) & valid
+        scoreable = valid & ~forced
+        if method != "pisa1":
+            scoreable &= (valid.sum(-1) > topk)[..., None]
+    acc = np.float64 if q.dtype == np.float64 else np.float32
+    out = np.full(ids.shape, -np.inf, acc)
+    if method == "pisa1":
+        means = mean_pool(k, block_size, dtype) if leaf_means is None else leaf_means
+        source, support, sc = means, 1, 1.0
+    else:
+        source, support, sc = k, block_size, dim ** -0.5
+    for b in range(batch):
+        query = q[b].reshape(tokens, heads, groups, dim)
+        src = np.broadcast_to(source[b][None], (tokens,) + source[b].shape)
+        score = block_scores(query, src, np.where(scoreable[b], ids[b], -1), support, method, sc)
+        out[b] = np.where(scoreable[b], score, -np.inf)
+    return out
 
 
 def network_topk(scores, ids, topk, return_scores=False):

@@ -8,7 +8,10 @@ It imports the reference package ``pisa`` from ``<root>/pisa`` and calls
 ``select_blocks(..., backend="torch")`` (top_k_pyramid.py:11-122),
 ``sparse_attention(..., backend="torch")`` with autograd
 (sparse_attn.py:10-61, sparse_attn_torch.py:6-35) and ``build_pyramid``
-(mean_pooling.py:45-52).  Inputs are regenerated from their seed by
+(mean_pooling.py:45-52), and the leaf scores of random candidate lists with
+the reference's ``block_scores`` / ``routing_masks``
+(top_k_pyramid_torch.py:48-80,114-120; the grouped_leaf_scores semantics of
+leaf_triton.py:144-232).  Inputs are regenerated from their seed by
 :func:`inputs` (torch's CPU generator, fp32 normal draws in q, k, v, dout
 order, then a cast), so the fixtures hold only outputs plus input checksums.
 The reference is not needed to *read* the fixtures.
@@ -79,14 +82,84 @@ def as_np(t):
     return t.detach().to(torch.float64 if t.dtype == torch.float64 else torch.float32).numpy()
 
 
-def main(root):
+# Leaf scores of arbitrary candidate lists (grouped_leaf_scores semantics),
+# computed with the reference's torch scoring and masks.
+LEAF_CASES = {
+    "leaf_bf16": dict(B=2, T=40, N=300, Hq=8, Hkv=2, D=64, C=16, W=16, K=8, ff=True, fr=2,
+                      dtype="bf16", seed=12),
+    "leaf_f32": dict(B=1, T=30, N=200, Hq=4, Hkv=4, D=32, C=32, W=10, K=4, ff=False, fr=1,
+                     dtype="f32", seed=13),
+}
+
+
+def leaf_inputs(case):
+    """Seeded q, k, candidates (distinct ids per row in [-2, blocks + 2)) and positions."""
+    g = torch.Generator().manual_seed(case["seed"])
+    dt = DTYPES[case["dtype"]]
+    q = torch.randn(case["B"], case["T"], case["Hq"], case["D"], generator=g).to(dt)
+    k = torch.randn(case["B"], case["N"], case["Hkv"], case["D"], generator=g).to(dt)
+    blocks = -(-case["N"] // case["C"])
+    rows = case["B"] * case["T"] * case["Hkv"]
+    cand = torch.stack([torch.randperm(blocks + 4, generator=g)[:case["W"]] - 2 for _ in range(rows)])
+    cand = cand.reshape(case["B"], case["T"], case["Hkv"], case["W"])
+    positions = torch.randint(0, case["N"], (case["B"], case["T"]), generator=g)
+    return q, k, cand, positions
+
+
+def leaf_reference(root_modules, q, k, cand, positions, case, method):
+    """The reference's block_scores / routing_masks / mean_pool on one case."""
+    block_scores, routing_masks, mean_pool = root_modules
+    C, K = case["C"], case["K"]
+    blocks = -(-case["N"] // C)
+    in_range = (cand >= 0) & (cand < blocks)
+    ids = torch.where(in_range, cand, -1)
+    out = {}
+    for masked in (False, True):
+        if masked:
+            pos = positions[..., None].expand(*cand.shape[:3])
+            valid, forced, scoreable = routing_masks(ids, pos, C, K, case["ff"], case["fr"])
+            if method == "pisa1":
+                scoreable = valid & ~forced
+        else:
+            scoreable = in_range
+        if method == "pisa1":
+            source, support, scale = mean_pool(k, C, backend="torch"), 1, 1.0
+        else:
+            source, support, scale = k, C, case["D"] ** -0.5
+        result = torch.full(cand.shape, -torch.inf)
+        for b in range(case["B"]):
+            src = source[b:b + 1].expand(case["T"], *source.shape[1:])
+            sc = block_scores(q[b], src, torch.where(scoreable[b], ids[b], -1), support, method, scale)
+            result[b] = torch.where(scoreable[b], sc.float(), -torch.inf)
+        out["masked" if masked else "plain"] = result.numpy()
+    return out
+
+
+def main(root, which=None):
     sys.path.insert(0, str(Path(root) / "pisa"))
-    from pisa.ops.compress.mean_pooling import build_pyramid
+    from pisa.ops.compress.mean_pooling import build_pyramid, mean_pool
     from pisa.ops.flash_sparse_attn.sparse_attn import sparse_attention
     from pisa.ops.flash_sparse_attn.top_k_pyramid import select_blocks
+    from pisa.ops.flash_sparse_attn.top_k_pyramid.top_k_pyramid_torch import block_scores, routing_masks
 
     torch.set_num_threads(max(1, torch.get_num_threads()))
+    for name, case in LEAF_CASES.items():
+        if which and name not in which:
+            continue
+        q, k, cand, positions = leaf_inputs(case)
+        rec = {"q_sum": checksum(q), "k_sum": checksum(k), "cand_sum": checksum(cand),
+               "positions_sum": checksum(positions)}
+        for method in ("pisa", "pisa1", "pisa2"):
+            for tag, arr in leaf_reference((block_scores, routing_masks, mean_pool), q, k, cand, positions,
+                                           case, method).items():
+                rec[f"{method}_{tag}"] = arr
+        np.savez_compressed(HERE / f"{name}.npz", **rec)
+        print(name, {k: v.shape for k, v in rec.items()})
+    if which and not (set(which) & (set(CASES) | {"pyramid"})):
+        return
     for name, case in CASES.items():
+        if which and name not in which:
+            continue
         q, k, v, dout = inputs(case)
         rec = {
             "q_sum": checksum(q), "k_sum": checksum(k), "v_sum": checksum(v), "dout_sum": checksum(dout),
@@ -109,6 +182,8 @@ def main(root):
         np.savez_compressed(HERE / f"{name}.npz", **rec)
         print(name, {k: v.shape for k, v in rec.items()})
 
+    if which and "pyramid" not in which:
+        return
     # Pyramid levels with a tail block, bf16 and f32 (mean_pooling_torch.py:7-14).
     g = torch.Generator().manual_seed(11)
     keys = torch.randn(2, 1000, 3, 40, generator=g)
@@ -122,6 +197,6 @@ def main(root):
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: make_golden.py <path of the NlogN_PISA checkout>")
-    main(sys.argv[1])
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <path of the NlogN_PISA checkout> [fixture names...]")
+    main(sys.argv[1], set(sys.argv[2:]) or None)

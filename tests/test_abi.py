@@ -1,5 +1,6 @@
 """CPU-side checks of the C ABI and the host logic (no compute calls)."""
 
+import ctypes
 import re
 from pathlib import Path
 
@@ -112,3 +113,31 @@ def test_kernel_timer_without_launches():
     lib = _lib.lib()
     assert lib.pisa_kernel_time(7, None, None) == _lib.ERR_INVALID
     _lib.kernel_timing(False)
+
+
+def test_caller_pyramid_tables_are_validated_without_gpu():
+    """Level tables that do not describe the keys' pyramid (another branching,
+    other keys, too shallow) are rejected before any device work."""
+    from nlogn_pisa_b200 import _lib
+
+    lib = _lib.lib()
+    N, C, K = 4096, 64, 16                      # 64 leaves: top 2 (b=2), 1 (b=4)
+    binary = [64, 32, 16, 8, 4, 2, 1]
+    offsets = np.cumsum([0] + binary[:-1]).tolist()
+
+    def call(sizes, branching, top, first_width):
+        rc = lib.pisa_select_blocks(
+            None, 0, 0, 0, None, 0, 0, 0, ctypes.c_void_p(256), 0, _lib.int64_array(offsets),
+            _lib.int64_array(sizes), len(sizes), None, 0, 1, 1, 64, 4, 1, 64, N, 2, C, branching, K, 1, 1,
+            top, first_width, 0, ctypes.c_void_p(256), None, 0, None)
+        return rc, _lib.lib().pisa_last_error().decode()
+
+    # a binary pyramid read with branching 4
+    rc, msg = call(binary, 4, 1, 16)
+    assert rc == _lib.ERR_INVALID and "level sizes" in msg
+    # sizes of other keys
+    rc, msg = call([63, 32, 16, 8, 4, 2, 1], 2, 2, 16)
+    assert rc == _lib.ERR_INVALID and "level sizes" in msg
+    # shallower than the routing depth without reaching a single node
+    rc, msg = call([64, 32], 2, 2, 16)
+    assert rc == _lib.ERR_INVALID and "fewer levels" in msg

@@ -1,0 +1,128 @@
+"""Parity at the benchmarked configurations, on sampled query rows.
+
+The selection of every benchmarked configuration (branching 4, top-K 32 over
+b*K = 128 leaf candidates; the 256K sequence with per-block key offsets; the
+64-sequence decode step over a 131072-token cache; top-K 64 over 256 leaf
+candidates) is checked against the oracle's descent on rows spread over the
+sequence (query rows are independent given the keys, validation.py:38-47),
+then attention over the GPU's own ids against the oracle's attention.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import pisa_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _check_ids(got, want, trace, min_exact):
+    rows, exact, tie, bad = O.compare_selection(got, want, trace["min_gap"])
+    assert len(bad) == 0, f"{len(bad)} rows differ beyond near-ties, e.g. rows {bad[:5]}"
+    assert exact >= min_exact * rows, (exact, tie, rows)
+
+
+def _sampled_parity(q, k, v, ids, out, rows, C, K, branching, method="pisa", min_exact=0.95):
+    """Oracle descent + attention on `rows` of one sequence (batch 0)."""
+    qn = q[:, rows].float().cpu().numpy()
+    kn = k.float().cpu().numpy()
+    vn = v.float().cpu().numpy()
+    levels = O.build_pyramid(kn, C, "bf16", branching=branching)
+    pos = np.broadcast_to(rows[None], (1, len(rows)))
+    trace = {}
+    want = O.pyramid_select(qn, kn, method, C, K, pos, True, 1, levels, branching=branching, trace=trace)
+    got = ids[:, rows].cpu().numpy()
+    _check_ids(got, want, trace, min_exact)
+    ref, _ = O.sparse_attention(qn, kn, vn, got, C, positions=pos)
+    np.testing.assert_allclose(out[:, rows].float().cpu().numpy(), ref, rtol=0, atol=2e-2)
+
+
+def _rows(n, count, seed):
+    rng = np.random.default_rng(seed)
+    edges = [0, 1, 63, 64, n // 2, n - 65, n - 64, n - 2, n - 1]
+    return np.unique(np.concatenate([edges, rng.integers(0, n, count)]))
+
+
+def test_prefill32k_branching4_topk32(cuda_device):
+    """The headline benchmark workload itself (prefill32k: B=1, N=32768,
+    Hq=32, Hkv=8, D=128, C=64, b=4, K=32, forced first + current block): the
+    grouped pipeline with its 128-candidate leaf level and final network."""
+    import nlogn_pisa_b200 as P
+    from nlogn_pisa_b200.workloads import WORKLOADS, make_inputs
+
+    w = WORKLOADS["prefill32k"]
+    q, k, v = make_inputs(w, cuda_device)
+    ids = P.select_blocks(q, k, method=w.method, block_size=w.block_size, topk=w.topk,
+                          force_first=w.force_first, force_recent=w.force_recent, branching=w.branching)
+    out = P.sparse_attention(q, k, v, ids, block_size=w.block_size)
+    assert ids.shape == (1, w.tokens, w.kv_heads, w.topk)
+    _sampled_parity(q, k, v, ids, out, _rows(w.tokens, 20, 1), w.block_size, w.topk, w.branching)
+
+
+def test_prefill32k_binary_pyramid(cuda_device):
+    """prefill32k_b2: the same workload with the reference's binary pyramid."""
+    import nlogn_pisa_b200 as P
+    from nlogn_pisa_b200.workloads import WORKLOADS, make_inputs
+
+    w = WORKLOADS["prefill32k_b2"]
+    q, k, v = make_inputs(w, cuda_device)
+    ids = P.select_blocks(q, k, method=w.method, block_size=w.block_size, topk=w.topk,
+                          force_first=w.force_first, force_recent=w.force_recent, branching=w.branching)
+    out = P.sparse_attention(q, k, v, ids, block_size=w.block_size)
+    _sampled_parity(q, k, v, ids, out, _rows(w.tokens, 12, 2), w.block_size, w.topk, w.branching)
+
+
+def test_prefill256k_block_offsets(cuda_device):
+    """The 262144-token workload (keys with per-block N(0, 0.5^2) mean offsets)."""
+    import nlogn_pisa_b200 as P
+    from nlogn_pisa_b200.workloads import WORKLOADS, make_inputs
+
+    w = WORKLOADS["prefill256k"]
+    q, k, v = make_inputs(w, cuda_device)
+    ids = P.select_blocks(q, k, method=w.method, block_size=w.block_size, topk=w.topk,
+                          force_first=w.force_first, force_recent=w.force_recent, branching=w.branching)
+    out = P.sparse_attention(q, k, v, ids, block_size=w.block_size)
+    _sampled_parity(q, k, v, ids, out, _rows(w.tokens, 10, 3), w.block_size, w.topk, w.branching)
+
+
+def test_topk64_branching4(cuda_device):
+    """Top-K 64 with branching 4: 256 leaf candidates per row (the widest network)."""
+    import nlogn_pisa_b200 as P
+
+    g = torch.Generator(device=cuda_device).manual_seed(7)
+    B, N, Hq, H, D, C, K, br = 1, 16384, 32, 8, 128, 64, 64, 4
+    q = torch.randn(B, N, Hq, D, generator=g, device=cuda_device).to(torch.bfloat16)
+    k = torch.randn(B, N, H, D, generator=g, device=cuda_device).to(torch.bfloat16)
+    v = torch.randn(B, N, H, D, generator=g, device=cuda_device).to(torch.bfloat16)
+    ids = P.select_blocks(q, k, block_size=C, topk=K, force_recent=1, branching=br)
+    out = P.sparse_attention(q, k, v, ids, block_size=C)
+    _sampled_parity(q, k, v, ids, out, _rows(N, 16, 4), C, K, br)
+
+
+def test_decode_step_128k_cache_64_sequences(cuda_device):
+    """The benchmarked decode step: 64 sequences, one query token each, a
+    131072-token cache, Hq=32, Hkv=8, D=128, C=64, b=4, K=32 (fused request,
+    run as the grouped pipeline at this many rows), with a prebuilt pyramid;
+    four sequences checked in full against the oracle."""
+    import nlogn_pisa_b200 as P
+
+    Bd, N, Hq, H, D, C, K, br = 64, 131072, 32, 8, 128, 64, 32, 4
+    gen = torch.Generator(device=cuda_device).manual_seed(3)
+    k = torch.randn((Bd, N, H, D), generator=gen, device=cuda_device, dtype=torch.bfloat16)
+    v = torch.randn((Bd, N, H, D), generator=gen, device=cuda_device, dtype=torch.bfloat16)
+    q = torch.randn((Bd, 1, Hq, D), generator=gen, device=cuda_device, dtype=torch.bfloat16)
+    levels = P.build_pyramid(k, C, branching=br)
+    ids = P.select_blocks(q, k, block_size=C, topk=K, query_offset=N - 1, force_recent=1, pyramid=levels,
+                          routing_schedule="fused", branching=br)
+    out = P.sparse_attention(q, k, v, ids, block_size=C, query_offset=N - 1)
+    for b in (0, 17, 42, 63):
+        qn, kn, vn = (x[b:b + 1].float().cpu().numpy() for x in (q, k, v))
+        lv = O.build_pyramid(kn, C, "bf16", branching=br)
+        pos = O.query_positions(1, 1, N, N - 1)
+        trace = {}
+        want = O.pyramid_select(qn, kn, "pisa", C, K, pos, True, 1, lv, branching=br, trace=trace)
+        got = ids[b:b + 1].cpu().numpy()
+        _check_ids(got, want, trace, 1.0)
+        ref, _ = O.sparse_attention(qn, kn, vn, got, C, positions=pos)
+        np.testing.assert_allclose(out[b:b + 1].float().cpu().numpy(), ref, rtol=0, atol=2e-2)

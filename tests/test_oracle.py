@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 
 import pisa_oracle as O
-from golden_cases import CASES, load, np_inputs, offset_arg
+from golden_cases import CASES, LEAF_CASES, leaf_case, load, np_inputs, offset_arg
 
 SELECT_CASES = [n for n in CASES if n != "config1"]
 
@@ -123,3 +123,20 @@ def test_forced_count_raises():
     pos = np.array([[255]])
     with pytest.raises(ValueError):
         O.routing_masks(ids, pos, 64, 1, True, 2)
+
+
+@pytest.mark.parametrize("name", sorted(LEAF_CASES))
+@pytest.mark.parametrize("method", ["pisa", "pisa1", "pisa2"])
+def test_leaf_scores_match_reference(name, method):
+    """grouped_leaf_scores semantics: the reference's block_scores and masks on
+    random candidate lists (ids out of range, past the position, forced)."""
+    case, rec, (q, k, cand, positions) = leaf_case(name)
+    qn, kn = (x.float().numpy() for x in (q, k))
+    for tag, pos in (("plain", None), ("masked", positions.numpy())):
+        got = O.leaf_scores(qn, kn, cand.numpy(), case["C"], method, positions=pos, topk=case["K"],
+                            force_first=case["ff"], force_recent=case["fr"], dtype=case["dtype"])
+        want = rec[f"{method}_{tag}"]
+        assert (np.isinf(got) == np.isinf(want)).all(), (method, tag)
+        fin = np.isfinite(want)
+        assert fin.any() and (~fin).any()
+        np.testing.assert_allclose(got[fin], want[fin], rtol=1e-5, atol=1e-5)

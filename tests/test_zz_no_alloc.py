@@ -25,12 +25,19 @@ def _noalloc_backward(q, k, v, out, dout, lse, ids, block_size, scale):
     B, T, Hq, D = q.shape
     H, N, Dv = k.shape[2], k.shape[1], v.shape[-1]
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    rc = lib.pisa_sparse_attn_bwd_noalloc(
-        _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out), _lib.ptr(dout), _lib.ptr(lse), _lib.ptr(ids),
-        ids.element_size(), None, 0, _lib.dtype_code(q), B, T, Hq, H, D, Dv, N, ids.shape[-1], block_size,
-        float(scale), 1, _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv), _lib.stream_of(q.device))
-    _lib.check(rc)
-    return dq, dk, dv
+    torch.cuda.synchronize(q.device)
+    free0, allocated0 = torch.cuda.mem_get_info(q.device)[0], torch.cuda.memory_allocated(q.device)
+    with torch.cuda.device(q.device):
+        rc = lib.pisa_sparse_attn_bwd_noalloc(
+            _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out), _lib.ptr(dout), _lib.ptr(lse), _lib.ptr(ids),
+            ids.element_size(), None, 0, _lib.dtype_code(q), B, T, Hq, H, D, Dv, N, ids.shape[-1], block_size,
+            float(scale), 1, _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv), _lib.stream_of(q.device))
+        _lib.check(rc)
+        torch.cuda.synchronize(q.device)
+    # device memory (the process-wide free count and torch's allocator) is
+    # unchanged across the call, apart from the one-time set-up of a first call
+    memory = (torch.cuda.mem_get_info(q.device)[0] - free0, torch.cuda.memory_allocated(q.device) - allocated0)
+    return (dq, dk, dv), memory
 
 
 @pytest.mark.gpu
@@ -52,9 +59,10 @@ def test_noalloc_backward_matches_workspace_backward(cuda_device):
     out, lse = attention_forward(q, k, v, ids, C, scale, None, 0, True)
     ref = attention_backward(q, k, v, out, dout, lse, ids, C, scale, None, 0, True)
     # two calls in a row: the second sees the first call's leftovers in the shared array
-    for _ in range(2):
-        got = _noalloc_backward(q, k, v, out, dout, lse, ids, C, scale)
-        torch.cuda.synchronize()
+    for call in range(2):
+        got, memory = _noalloc_backward(q, k, v, out, dout, lse, ids, C, scale)
+        if call == 1:
+            assert memory == (0, 0), memory
         for name, g, r in zip(("dq", "dk", "dv"), got, ref):
             assert torch.isfinite(g.float()).all(), name
             torch.testing.assert_close(g.float(), r.float(), atol=ATOL, rtol=0, msg=name)
@@ -72,3 +80,12 @@ def test_noalloc_backward_rejects_shapes_above_its_scratch(cuda_device):
                                           ctypes.c_void_p(0))
     assert rc == _lib.ERR_UNSUPPORTED
     assert "scratch" in lib.pisa_last_error().decode()
+    # the limit is pisa_sparse_attn_bwd_workspace_bytes <= the scratch size, exactly
+    per_token = lib.pisa_sparse_attn_bwd_workspace_bytes(1, 1, 32, 8, 128, 128, 1024) // 1024
+    fits = cap // per_token
+    assert lib.pisa_sparse_attn_bwd_workspace_bytes(1, 1, 32, 8, 128, 128, fits) <= cap
+    assert lib.pisa_sparse_attn_bwd_workspace_bytes(1, 1, 32, 8, 128, 128, fits + 1) > cap
+    rc = lib.pisa_sparse_attn_bwd_noalloc(None, None, None, None, None, None, None, 8, None, 0, _lib.BF16,
+                                          1, 1, 32, 8, 128, 128, fits + 1, 32, 64, 0.1, 1, None, None, None,
+                                          ctypes.c_void_p(0))
+    assert rc == _lib.ERR_UNSUPPORTED
