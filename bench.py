@@ -286,18 +286,23 @@ def run_reference(args, workload):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
-def prefill_measure(w, device, rank, steps, warmup, world, kernel_timing=True, sample_clocks=None):
+def prefill_measure(w, device, rank, steps, warmup, world, kernel_timing=True, sample_clocks=None,
+                    heads=None, seed=None):
     """Time the pyramid -> selection -> attention step of workload `w` through
     the C ABI with inputs resident in HBM.  Returns per-stage device times
-    (max over ranks), per-kernel device times and the step's algorithmic work."""
+    (max over ranks), per-kernel device times and the step's algorithmic work.
+    `heads` = (kv_slice, q_slice) runs one KV-head group of the sequence."""
     import torch
 
     from nlogn_pisa_b200 import _lib
     from nlogn_pisa_b200.selection import _c_array, level_sizes, routing_geometry  # noqa: F401
     from nlogn_pisa_b200.workloads import make_inputs
 
-    q, k, v = make_inputs(w, device, seed=w.seed + rank)
-    B, N, Hq, H, D = w.batch, w.tokens, w.q_heads, w.kv_heads, w.head_dim
+    q, k, v = make_inputs(w, device, seed=w.seed + rank if seed is None else seed)
+    if heads is not None:
+        kv, qh = heads
+        q, k, v = q[:, :, qh].contiguous(), k[:, :, kv].contiguous(), v[:, :, kv].contiguous()
+    B, N, Hq, H, D = w.batch, w.tokens, q.shape[2], k.shape[2], w.head_dim
     G, C, K, br = Hq // H, w.block_size, w.topk, w.branching
     code = _lib.dtype_code(q)
     lib = _lib.lib()
@@ -520,6 +525,65 @@ def e2e_prefill(w, tensors, device, world, steps):
                     "sparse_attention; host-to-device, compute and device-to-host on three streams"}
 
 
+def long_context_bench(device, world, rank, hbm, tensor, steps=3):
+    """The 262144-token configuration split over the ranks of this run, both ways
+    (nlogn_pisa_b200/sharding.py):
+      kv_heads  each rank runs its group of Hkv/world KV heads (and their query
+                heads) of the one sequence; no collective;
+      sequence  each rank owns 1/world of the query rows and of the keys/values,
+                pools its leaf blocks, all-gathers leaf means, keys and values
+                over NCCL and rebuilds the upper levels locally (world > 1).
+    value = the sequence's tokens / the slowest rank's device time per step."""
+    import torch
+    import torch.distributed as dist
+
+    import nlogn_pisa_b200 as P
+    from nlogn_pisa_b200.sharding import head_groups, sequence_shards, sequence_sharded_prefill
+    from nlogn_pisa_b200.workloads import WORKLOADS, make_inputs
+
+    w = WORKLOADS["prefill256k"]
+    out = {"workload": w.name, "tokens": w.tokens, "ranks": world}
+    kv, qh = head_groups(w.q_heads, w.kv_heads, rank, world)
+    m = prefill_measure(w, device, rank, steps, 3, world, heads=(kv, qh), seed=w.seed)
+    m["tensors"] = None
+    torch.cuda.empty_cache()
+    out["kv_heads"] = {"value": w.tokens / (m["step_ms"] / 1000.0), "unit": "tokens/s", "ms_per_step": m["step_ms"],
+                       "kv_heads_per_rank": kv.stop - kv.start, "scaling": "strong", "collective": "none",
+                       "stages": stage_report(m, hbm, tensor)}
+    if world > 1:
+        q, k, v = make_inputs(w, device, seed=w.seed)
+        shards = sequence_shards(w.tokens, w.block_size, world)
+        a, b = shards[rank]
+        ql, kl, vl = (x[:, a:b].contiguous() for x in (q, k, v))
+        del q, k, v
+        torch.cuda.empty_cache()
+        stream = torch.cuda.current_stream(device)
+
+        def step():
+            return sequence_sharded_prefill(ql, kl, vl, shards, rank, method=w.method, block_size=w.block_size,
+                                            topk=w.topk, force_first=w.force_first, force_recent=w.force_recent,
+                                            branching=w.branching)
+
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks([e0.elapsed_time(e1) / steps], device, world)[0]
+        out["sequence"] = {"value": w.tokens / (ms / 1000.0), "unit": "tokens/s", "ms_per_step": ms,
+                           "tokens_per_rank": b - a, "scaling": "strong",
+                           "collective": "NCCL all-gather of leaf means, keys and values; upper levels rebuilt locally",
+                           "api": "public Python API (select_blocks / sparse_attention with pyramid=)"}
+        del ql, kl, vl
+        torch.cuda.empty_cache()
+    return out
+
+
 def compact_line(w, m, hbm, tensor):
     """A secondary workload's measurement: throughput, stages and kernels."""
     return {"workload": w.name, "tokens": w.tokens, "branching": w.branching, "topk": w.topk,
@@ -570,13 +634,14 @@ def main():
 
     extra = {}
     if world == 1 and not args.no_extra:
-        for name, steps in (("prefill32k_b2", 5), ("prefill256k", 3)):
+        for name, steps in (("prefill32k_b2", 5),):
             if name == w.name:
                 continue
             mx = prefill_measure(WORKLOADS[name], device, rank, steps, 3, world)
             mx["tensors"] = None
             extra[name] = compact_line(WORKLOADS[name], mx, hbm, tensor)
             torch.cuda.empty_cache()
+    long_ctx = None if args.no_extra else long_context_bench(device, world, rank, hbm, tensor)
     decode = None if args.no_decode else decode_bench(args, device, world, hbm)
 
     if rank == 0:
@@ -614,6 +679,7 @@ def main():
             "select_attend_tensor_frac": (m["work"]["leaf_flops"] + m["work"]["attn_flops"])
             / 1e12 / (m["step_ms"] / 1000.0) / tensor,
             "workloads": extra,
+            "long_context": long_ctx,
             "decode": decode,
             "cpu_baseline": cpu,
             "e2e": e2e,

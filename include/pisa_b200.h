@@ -243,6 +243,20 @@ PISA_API int pisa_sparse_attn_bwd_noalloc(const void *q, const void *k, const vo
 /* Size of the fixed scratch of pisa_sparse_attn_bwd_noalloc, in bytes. */
 PISA_API int64_t pisa_sparse_attn_bwd_noalloc_max_bytes(void);
 
+/*
+ * Split-half rotary position encoding of the token mixer's q and k before
+ * selection.  Replaces rotary_fn / rotary_torch
+ * (pisa/pisa/ops/lrpe/rotary.py:9-17, rotary_torch.py:5-9) as called by
+ * xmixers' RotaryEmbedding (xmixers/xmixers/modules/pes/lrpe.py:29-33).
+ * x, out: [B,T,H,D] (element strides; out may equal x); frequency: D/2 fp32;
+ * positions: int64 with batch stride positions_sb (0 broadcasts one row) and
+ * unit token stride, or NULL for position_offset + token.
+ */
+PISA_API int pisa_rotary(const void *x, int64_t x_sb, int64_t x_st, int64_t x_sh, void *out, int64_t out_sb,
+                         int64_t out_st, int64_t out_sh, const int64_t *positions, int64_t positions_sb,
+                         int64_t position_offset, const float *frequency, int dtype, int64_t B, int64_t T,
+                         int64_t H, int64_t D, pisa_stream_t stream);
+
 /* ---- device status (no counterpart in the reference, whose Triton kernels never wait) ----
  * Every kernel that waits on another part of the GPU waits a bounded number
  * of tries.  A wait that expires records PISA_ERR_TIMEOUT in the 4-byte
@@ -260,6 +274,11 @@ PISA_API int pisa_workspace_status(const void *workspace, pisa_stream_t stream);
  * workspace[0..3] (256 bytes, cleared first) for pisa_workspace_status. */
 PISA_API int pisa_wait_selftest(int arrive, int64_t max_tries, void *workspace, int64_t workspace_bytes,
                                 pisa_stream_t stream);
+
+/* Accuracy check of the leaf epilogue's two exponential forms (no
+ * counterpart in the reference): poly[i] = the FMA-pipe polynomial 2^x[i],
+ * mufu[i] = ex2.approx.ftz.f32 of x[i]; device arrays of n floats. */
+PISA_API int pisa_ex2_selftest(const float *x, float *poly, float *mufu, int64_t n, pisa_stream_t stream);
 
 /* ---- per-kernel device timing (profiling aid; the reference has no counterpart) ----
  * With timing on, the library records a pair of CUDA events on the launch

@@ -50,8 +50,10 @@ SIGNATURES = {
     "pisa_leaf_scores": (_I, [_P, _L, _L, _L, _P, _L, _L, _L, _P, _L, _P, _I, _P, _I, _L, _L, _L, _L,
                               _L, _L, _L, _I, _L, _L, _I, _L, _P, _P, _L, _P]),
     "pisa_leaf_scores_workspace_bytes": (_L, [_L, _L, _L, _L, _L, _L, _L, _I, _I, _L, _I]),
+    "pisa_rotary": (_I, [_P, _L, _L, _L, _P, _L, _L, _L, _P, _L, _L, _P, _I, _L, _L, _L, _L, _P]),
     "pisa_workspace_status": (_I, [_P, _P]),
     "pisa_wait_selftest": (_I, [_I, _L, _P, _L, _P]),
+    "pisa_ex2_selftest": (_I, [_P, _P, _P, _L, _P]),
     "pisa_launch_count": (_L, []),
     "pisa_kernel_timing": (_I, [_I]),
     "pisa_kernel_time": (_I, [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),

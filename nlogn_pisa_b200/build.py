@@ -30,19 +30,24 @@ def needs_build():
     return any(p.stat().st_mtime > stamp for p in deps)
 
 
-def build(force=False, verbose=False, jobs=None):
-    """Compile every .cu into objects in parallel, then link the shared library."""
-    if not force and not needs_build():
+def build(force=False, verbose=False, jobs=None, out=None, defines=()):
+    """Compile every .cu into objects in parallel, then link the shared library.
+
+    `out` and `defines` (e.g. ["PISA_LEAF_POLY_PAIRS=0"]) build a variant of
+    the library elsewhere, for side-by-side measurements."""
+    target = LIB if out is None else Path(out)
+    if out is None and not force and not needs_build():
         return LIB
     nvcc = os.environ.get("NVCC", "nvcc")
-    objdir = ROOT / "_build"
-    objdir.mkdir(exist_ok=True)
+    objdir = ROOT / "_build" if out is None else target.parent / (target.stem + "_obj")
+    objdir.mkdir(parents=True, exist_ok=True)
     procs = []
     objs = []
     for src in sources():
         obj = objdir / (src.stem + ".o")
         objs.append(obj)
-        cmd = [nvcc, *ARCH, *FLAGS, "-I", str(INCLUDE), "-I", str(CSRC), "-c", str(src), "-o", str(obj)]
+        cmd = [nvcc, *ARCH, *FLAGS, *(f"-D{d}" for d in defines), "-I", str(INCLUDE), "-I", str(CSRC), "-c",
+               str(src), "-o", str(obj)]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         procs.append((src, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT)))
@@ -56,14 +61,14 @@ def build(force=False, verbose=False, jobs=None):
             print(f"== {src.name}\n{text}")
     if failed:
         raise RuntimeError("nvcc failed:\n" + "\n".join(failed))
-    tmp = LIB.with_suffix(".so.tmp")
+    tmp = target.with_suffix(".so.tmp")
     # cudart is linked statically: the library then works beside whichever
     # libcudart the host process (torch) has loaded, sharing the primary context.
     cmd = [nvcc, *ARCH, "-shared", "-cudart", "static", "-Xcompiler", "-fPIC", *map(str, objs),
            "-o", str(tmp)]
     subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, target)
+    return target
 
 
 if __name__ == "__main__":

@@ -89,9 +89,21 @@ __global__ void family_scatter_kernel(const GroupArgs g, const int32_t* __restri
 // mbarriers: full_q/empty_q guard the query stages, full_acc/empty_acc the
 // accumulators; the parity of round r is r & 1 (empty waits start at 1, so the
 // first round passes).  Every wait is bounded and records a timeout status.
-constexpr int kEpiWarps = 8, kLoadWarps = 4, kMmaWarp = kEpiWarps + kLoadWarps, kStages = 3, kGroup = 8;
+// Epilogue warps come in groups of four (one per TMEM lane quarter); group g
+// scores children [g*b/groups, (g+1)*b/groups) of every tile.
+#ifndef PISA_LEAF_EPI_GROUPS
+#define PISA_LEAF_EPI_GROUPS 4
+#endif
+constexpr int kEpiGroups = PISA_LEAF_EPI_GROUPS;
+constexpr int kEpiWarps = 4 * kEpiGroups, kLoadWarps = 4, kMmaWarp = kEpiWarps + kLoadWarps, kStages = 3, kGroup = 8;
 constexpr int kRowsPerLoader = 128 / kLoadWarps;  // tile rows per producer warp
 constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
+// Of every four pairs of LSE exponentials in the two-children epilogue, this
+// many are evaluated by tc::ex2_poly2 on the FMA pipe, the rest by ex2.approx.
+#ifndef PISA_LEAF_POLY_PAIRS
+#define PISA_LEAF_POLY_PAIRS 0
+#endif
+constexpr int kPolyPairs = PISA_LEAF_POLY_PAIRS;
 
 template <typename T>
 __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_constant__ GroupArgs g) {
@@ -268,12 +280,11 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
     __syncwarp();
   } else {
     // ---------------- epilogue ----------------
-    const int quarter = warp & 3, half = warp >> 2;
+    const int quarter = warp & 3, group = warp >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t(quarter) * 32) << 16;
     const int r = row >> lgG;
-    // half 0 scores children [0, ceil(b/2)), half 1 the rest
-    const int j_begin = half == 0 ? 0 : (g.br + 1) / 2, j_end = half == 0 ? (g.br + 1) / 2 : g.br;
+    const int j_begin = group * g.br / kEpiGroups, j_end = (group + 1) * g.br / kEpiGroups;
     const float l2e = 1.4426950408889634f;
     const float sl = g.scale * l2e;          // exp(scale*x - m) = 2^(x*sl - m*l2e)
     for (int it = 0; it < ntiles; ++it) {
@@ -289,7 +300,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
       (void)tile;
       const uint32_t acc = tmem + lane_base + a * NK;
       int j_first = j_begin;
-      if (g.C == 64 && g.method == PISA_METHOD_PISA && j_end - j_begin >= 2 &&
+      if (kEpiGroups < 4 && g.C == 64 && g.method == PISA_METHOD_PISA && j_end - j_begin >= 2 &&
           (int64_t(p) * g.br + j_begin + 2) * 64 <= g.N) {
         // two full 64-key children at once: both TMEM loads in flight, then the
         // two max / exponential chains interleaved
@@ -317,8 +328,14 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
         for (int i = 0; i < 64; i += 2) {
           const float2 x0 = tc::fma2(make_float2(__uint_as_float(r0[i]), __uint_as_float(r0[i + 1])), kk, c0);
           const float2 x1 = tc::fma2(make_float2(__uint_as_float(r1[i]), __uint_as_float(r1[i + 1])), kk, c1);
-          s0 = tc::add2(s0, make_float2(tc::ex2f(x0.x), tc::ex2f(x0.y)));
-          s1 = tc::add2(s1, make_float2(tc::ex2f(x1.x), tc::ex2f(x1.y)));
+          if (((i >> 1) & 3) < kPolyPairs) {
+            // this pair on the FMA pipe (the MUFU unit bounds the epilogue)
+            s0 = tc::add2(s0, tc::ex2_poly2(x0));
+            s1 = tc::add2(s1, tc::ex2_poly2(x1));
+          } else {
+            s0 = tc::add2(s0, make_float2(tc::ex2f(x0.x), tc::ex2f(x0.y)));
+            s1 = tc::add2(s1, make_float2(tc::ex2f(x1.x), tc::ex2f(x1.y)));
+          }
         }
         float sc0 = m0 * g.scale + logf(s0.x + s0.y), sc1 = m1 * g.scale + logf(s1.x + s1.y);
         for (int o = 1; o < g.G; o <<= 1) {
@@ -335,7 +352,35 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
         const int64_t key0 = (int64_t(p) * g.br + j) * g.C;
         const int valid_keys = int(min64(g.C, max(int64_t(0), g.N - key0)));
         float score;
-        if (g.C == 64 && valid_keys == 64) {
+        if (kEpiGroups == 4 && g.C == 64 && valid_keys == 64) {
+          // full 64-key block in two 32-column halves (32 live values: the
+          // 16 epilogue warps leave at most 80 registers a thread); the LSE
+          // merges the halves' maxima, the moments simply add
+          float v[32];
+          tc::tmem_ld32(acc + j * 64, v);
+          if (g.method == PISA_METHOD_PISA) {
+            const float m1 = tc::max32(v);
+            const float s1 = tc::sum_ex2_32(v, sl, m1 * sl);
+            tc::tmem_ld32(acc + j * 64 + 32, v);
+            const float mx = fmaxf(m1, tc::max32(v));
+            const float sum = fmaf(s1, tc::ex2f((m1 - mx) * sl), tc::sum_ex2_32(v, sl, mx * sl));
+            score = mx * g.scale + logf(sum);
+          } else {
+            float2 a1 = make_float2(0.f, 0.f), a2 = make_float2(0.f, 0.f);
+            for (int hh = 0; hh < 2; ++hh) {
+              if (hh) tc::tmem_ld32(acc + j * 64 + 32, v);
+#pragma unroll
+              for (int i = 0; i < 32; i += 2) {
+                const float2 pv = make_float2(v[i], v[i + 1]);
+                a1 = tc::add2(a1, pv);
+                a2 = tc::fma2(pv, pv, a2);
+              }
+            }
+            const float mean = (a1.x + a1.y) / 64.f;
+            const float var = fmaxf((a2.x + a2.y) / 64.f - mean * mean, 0.f);
+            score = g.scale * mean + g.c2 * var;
+          }
+        } else if (kEpiGroups < 4 && g.C == 64 && valid_keys == 64) {
           // full 64-key block: one TMEM load, packed arithmetic, no masks
           float v[64];
           tc::tmem_ld64(acc + j * 64, v);

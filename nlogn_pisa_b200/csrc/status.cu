@@ -36,11 +36,36 @@ __global__ void wait_selftest_kernel(int arrive, uint32_t max_tries, int* status
   if (!ok) atomicExch(status, PISA_ERR_TIMEOUT);
 }
 
+// Both exponentials of the leaf epilogue on the same inputs: the polynomial
+// form (tc::ex2_poly2) and ex2.approx.
+__global__ void ex2_selftest_kernel(const float* x, float* poly, float* mufu, int64_t n) {
+  const int64_t i = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) * 2;
+  if (i >= n) return;
+  const float2 v = make_float2(x[i], i + 1 < n ? x[i + 1] : 0.f);
+  const float2 p = tc::ex2_poly2(v);
+  poly[i] = p.x;
+  mufu[i] = tc::ex2f(v.x);
+  if (i + 1 < n) {
+    poly[i + 1] = p.y;
+    mufu[i + 1] = tc::ex2f(v.y);
+  }
+}
+
 }  // namespace
 
 }  // namespace pisa
 
 extern "C" {
+
+int pisa_ex2_selftest(const float* x, float* poly, float* mufu, int64_t n, pisa_stream_t stream) {
+  if (n < 0 || (n > 0 && (!x || !poly || !mufu))) return pisa::fail(PISA_ERR_INVALID, "x, poly and mufu are required");
+  if (n == 0) return PISA_OK;
+  const int64_t pairs = (n + 1) / 2;
+  pisa::ex2_selftest_kernel<<<unsigned((pairs + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, poly, mufu, n);
+  PISA_CHECK_LAUNCH();
+  return PISA_OK;
+}
 
 int pisa_workspace_status(const void* workspace, pisa_stream_t stream) {
   if (!workspace) return pisa::fail(PISA_ERR_INVALID, "workspace is required");

@@ -243,6 +243,60 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
 }
 
 // Max of 64 values with four independent 3-input max chains.
+// 2^x for a pair of fp32 values on the FMA and integer pipes, leaving the
+// MUFU unit (ex2.approx) free for the other exponentials of an epilogue.
+// Range reduction: adding 1.5 * 2^23 rounds x to the nearest integer j, which
+// lands in the low mantissa bits of the sum; f = x - j lies in [-0.5, 0.5].
+// 2^f is a degree-5 polynomial whose coefficients were fitted for minimum
+// maximum relative error on [-0.5, 0.5] (Lawson-weighted least squares;
+// 2.3e-7 maximum relative error with fp32 Horner evaluation, the size of
+// ex2.approx.f32's error); 2^j is applied by adding j to the exponent field
+// (j << 23 equals the sum's bits << 23, since the constant's low 9 bits are 0).
+// Inputs are clamped at -125: results below 2^-125 are not exact.
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 magic = make_float2(12582912.f, 12582912.f);
+  const float2 t = add2(x, magic);
+  const float2 j = add2(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = fma2(j, make_float2(-1.f, -1.f), x);
+  float2 p = fma2(make_float2(1.3276325771585107e-3f, 1.3276325771585107e-3f), f,
+                  make_float2(9.675491601228714e-3f, 9.675491601228714e-3f));
+  p = fma2(p, f, make_float2(5.550713092088699e-2f, 5.550713092088699e-2f));
+  p = fma2(p, f, make_float2(2.4022120237350464e-1f, 2.4022120237350464e-1f));
+  p = fma2(p, f, make_float2(6.931469440460205e-1f, 6.931469440460205e-1f));
+  p = fma2(p, f, make_float2(1.0000001192092896f, 1.0000001192092896f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
+__device__ __forceinline__ float max32(const float (&v)[32]) {
+  float m0 = v[0], m1 = v[1], m2 = v[2], m3 = v[3];
+#pragma unroll
+  for (int i = 4; i < 32; i += 8) {
+    m0 = max3f(m0, v[i], v[i + 1]);
+    m1 = max3f(m1, v[i + 2], v[i + 3]);
+    m2 = max3f(m2, v[i + 4], v[i + 5]);
+    m3 = max3f(m3, v[i + 6], v[i + 7]);
+  }
+  return fmaxf(max3f(m0, m1, m2), m3);
+}
+
+// sum_i 2^(v_i * k - c) over 32 values, packed pairs, two accumulators
+__device__ __forceinline__ float sum_ex2_32(const float (&v)[32], float k, float c) {
+  float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+  const float2 kk = make_float2(k, k), cc = make_float2(-c, -c);
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    float2 x0 = fma2(make_float2(v[i], v[i + 1]), kk, cc);
+    float2 x1 = fma2(make_float2(v[i + 2], v[i + 3]), kk, cc);
+    acc0 = add2(acc0, make_float2(ex2f(x0.x), ex2f(x0.y)));
+    acc1 = add2(acc1, make_float2(ex2f(x1.x), ex2f(x1.y)));
+  }
+  const float2 t = add2(acc0, acc1);
+  return t.x + t.y;
+}
+
 __device__ __forceinline__ float max64(const float (&v)[64]) {
   float m0 = v[0], m1 = v[1], m2 = v[2], m3 = v[3];
 #pragma unroll

@@ -185,6 +185,13 @@ def _pyramid_tables(pyramid, k, block_size, top, branching):
     return summary, summary.stride(0), offsets, sizes
 
 
+def _rows16_storage(storage):
+    if (storage.stride(-1) != 1 or storage.stride(-2) != storage.shape[-1]
+            or storage.stride(1) != storage.shape[-1] * storage.shape[-2]):
+        raise ValueError("pyramid storage must be contiguous per node ([B, total, H, D])")
+    return storage
+
+
 def _check_summary(t, k):
     if (t.ndim != 4 or t.shape[0] != k.shape[0] or t.shape[2:] != k.shape[2:] or t.dtype != k.dtype
             or t.device != k.device):

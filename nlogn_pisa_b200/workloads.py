@@ -44,8 +44,10 @@ WORKLOADS = {
     "prefill32k": Workload("prefill32k", 1, 32768, 32, 8, 128, 64, 32, 4, True, 1, "pisa", "bf16"),
     # the same with the reference's binary pyramid
     "prefill32k_b2": Workload("prefill32k_b2", 1, 32768, 32, 8, 128, 64, 32, 2, True, 1, "pisa", "bf16"),
-    # a smaller case of the 32K benchmark for profiler captures (inputs still larger than L2)
+    # smaller cases of the 32K benchmark for profiler captures (inputs still larger than L2);
+    # 16K is the smallest length at which the coarse level is scored densely and routed by warps
     "prefill8k": Workload("prefill8k", 1, 8192, 32, 8, 128, 64, 32, 4, True, 1, "pisa", "bf16"),
+    "prefill16k": Workload("prefill16k", 1, 16384, 32, 8, 128, 64, 32, 4, True, 1, "pisa", "bf16"),
     # 256K causal prefill with informative block means
     "prefill256k": Workload("prefill256k", 1, 262144, 32, 8, 128, 64, 32, 4, True, 1, "pisa", "bf16",
                             key_block_offset_std=0.5),

@@ -72,6 +72,25 @@ def test_expired_wait_surfaces_as_runtime_error(cuda_device):
     _lib.check_workspace(ws, cuda_device)
 
 
+def test_polynomial_exp2_matches_ex2_approx_error(cuda_device):
+    """The FMA-pipe 2^x of the leaf epilogue stays within 4e-7 relative of the
+    exact value over the inputs the epilogue gives it (x <= 0, down to the
+    -125 clamp), the size of ex2.approx.f32's own error."""
+    from nlogn_pisa_b200 import _lib
+
+    x = torch.cat([torch.linspace(-125.0, 0.0, 1_000_001), -torch.rand(100_000) * 3,
+                   torch.tensor([0.0, -0.5, -0.49999997, -1.5, -124.5, -125.0])]).to(cuda_device)
+    poly, mufu = torch.empty_like(x), torch.empty_like(x)
+    _lib.check(_lib.lib().pisa_ex2_selftest(_lib.ptr(x), _lib.ptr(poly), _lib.ptr(mufu), x.numel(),
+                                            _lib.stream_of(cuda_device)))
+    exact = torch.exp2(x.double())
+    rel_poly = ((poly.double() - exact).abs() / exact).max().item()
+    rel_mufu = ((mufu.double() - exact).abs() / exact).max().item()
+    assert rel_poly < 4e-7, rel_poly
+    assert rel_poly < 4 * max(rel_mufu, 1e-7), (rel_poly, rel_mufu)
+    assert (poly > 0).all()
+
+
 def test_checked_mode_reads_status_of_real_calls(cuda_device):
     """With status checks on, select_blocks / sparse_attention read their
     status words back (OK on a normal run) and give the same results."""
