@@ -584,6 +584,95 @@ def long_context_bench(device, world, rank, hbm, tensor, steps=3):
     return out
 
 
+def training_bench(device, world, rank, tensor, steps=5, warmup=3, batch=4, tokens=16384):
+    """The training configuration: fwd + bwd + AdamW step of one random-init
+    LLaMA-style block (d_model 1024, Hq = Hkv = 16, D = 64, SwiGLU 2816,
+    RMSNorm, RoPE 1e4, pisa2, block 64, branching 4, top-K 16) on `batch`
+    sequences of `tokens` uniform random token ids per GPU, bf16 autocast with
+    fp32 master weights, data-parallel over the run's ranks (DDP: NCCL
+    all-reduce of the gradients inside the timed step).  Loss: mean square of
+    the block's normalised output.  value = tokens of all ranks / step time
+    (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from nlogn_pisa_b200.model import BlockConfig, DecoderBlock
+
+    cfg = BlockConfig()
+    torch.manual_seed(1234)
+    model = DecoderBlock(cfg).to(device)
+    if world > 1:
+        model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[device.index])
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+    g = torch.Generator(device=device).manual_seed(4321 + rank)
+    ids = torch.randint(0, cfg.vocab_size, (batch, tokens), generator=g, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            h = model(ids)
+            loss = h.float().square().mean()
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        loss = step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks([e0.elapsed_time(e1) / steps], device, world)[0]
+    # the attention layer alone (selection + attention fwd + bwd) on this shape
+    import nlogn_pisa_b200 as P
+
+    Hq, D = cfg.num_attention_heads, cfg.head_dim
+    q = torch.randn(batch, tokens, Hq, D, device=device, dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(batch, tokens, cfg.num_key_value_heads, D, device=device, dtype=torch.bfloat16,
+                    requires_grad=True)
+    v = torch.randn_like(k, requires_grad=True)
+    dout = torch.randn(batch, tokens, Hq, D, device=device, dtype=torch.bfloat16)
+    ids_sel = P.select_blocks(q.detach(), k.detach(), method=cfg.attention_method, block_size=cfg.block_size,
+                              topk=cfg.topk, force_recent=cfg.force_recent, branching=cfg.branching)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    for i in range(warmup + steps):
+        if i == warmup:
+            ev[0].record(stream)
+        P.select_blocks(q.detach(), k.detach(), method=cfg.attention_method, block_size=cfg.block_size,
+                        topk=cfg.topk, force_recent=cfg.force_recent, branching=cfg.branching)
+        if i == warmup:
+            ev[1].record(stream)
+        out = P.sparse_attention(q, k, v, ids_sel, block_size=cfg.block_size)
+        if i == warmup:
+            ev[2].record(stream)
+        out.backward(dout)
+        if i == warmup:
+            ev[3].record(stream)
+        q.grad = k.grad = v.grad = None
+    torch.cuda.synchronize()
+    sel_ms, fwd_ms, bwd_ms = (ev[j].elapsed_time(ev[j + 1]) for j in range(3))
+    pos = torch.arange(tokens, device=device)
+    valid = (ids_sel >= 0) & (ids_sel * cfg.block_size <= pos[None, :, None, None])
+    keys = torch.clamp(pos[None, :, None, None] + 1 - ids_sel * cfg.block_size, 0, cfg.block_size)
+    fwd_flops = torch.where(valid, keys, 0).sum().item() * 4 * D * (Hq // cfg.num_key_value_heads)
+    bwd_flops = 2.5 * fwd_flops
+    return {"workload": "train_block16k", "value": world * batch * tokens / (ms / 1000.0), "unit": "tokens/s",
+            "ms_per_step": ms, "steps": steps, "batch_per_gpu": batch, "tokens": tokens, "loss": float(loss),
+            "parallelism": f"dp{world} (DDP, NCCL all-reduce of gradients)" if world > 1 else "dp1",
+            "scaling": "weak", "model": "1 LLaMA-style block: d 1024, Hq=Hkv=16, D 64, SwiGLU 2816, RMSNorm, "
+                                          "RoPE 1e4 (fraction 0.5), pisa2, block 64, branching 4, top-K 16",
+            "attention_layer": {"select_ms": sel_ms, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+                                "fwd_frac": fwd_flops / 1e12 / (fwd_ms / 1000.0) / tensor,
+                                "bwd_frac": bwd_flops / 1e12 / (bwd_ms / 1000.0) / tensor,
+                                "bwd_flops_rule": "2.5 x the forward's selected FLOPs"}}
+
+
 def compact_line(w, m, hbm, tensor):
     """A secondary workload's measurement: throughput, stages and kernels."""
     return {"workload": w.name, "tokens": w.tokens, "branching": w.branching, "topk": w.topk,
@@ -642,6 +731,8 @@ def main():
             extra[name] = compact_line(WORKLOADS[name], mx, hbm, tensor)
             torch.cuda.empty_cache()
     long_ctx = None if args.no_extra else long_context_bench(device, world, rank, hbm, tensor)
+    training = None if args.no_extra else training_bench(device, world, rank, tensor)
+    torch.cuda.empty_cache()
     decode = None if args.no_decode else decode_bench(args, device, world, hbm)
 
     if rank == 0:
@@ -680,6 +771,7 @@ def main():
             / 1e12 / (m["step_ms"] / 1000.0) / tensor,
             "workloads": extra,
             "long_context": long_ctx,
+            "training": training,
             "decode": decode,
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -202,7 +202,13 @@ PISA_API int64_t pisa_sparse_attn_fwd_workspace_bytes(int64_t B, int64_t Tq, int
  * Backward of pisa_sparse_attn_fwd: dq [B,Tq,Hq,D], dk/dv [B,N,H,D|Dv] in
  * dtype, contiguous.  Gradient of the reference's autograd through
  * sparse_attn_torch.py:6-35.  q/k/v/out/dout/dq/dk/dv contiguous.
- * workspace: pisa_sparse_attn_bwd_workspace_bytes(...) bytes.
+ * workspace: pisa_sparse_attn_bwd_tc_workspace_bytes(...) bytes (when that
+ *   is nonzero: fp16/bf16, block size 64, D = Dv = 64) run the
+ *   tensor-core backward over the forward's request buckets, with its status
+ *   word at workspace offset 0; otherwise (or with a smaller workspace of at
+ *   least pisa_sparse_attn_bwd_workspace_bytes(...) bytes) the per-query
+ *   gather kernels run.  The reference's GPU backward is fla-core's
+ *   ParallelNSAFunction (sparse_attn_fla.py:59-68).
  */
 PISA_API int pisa_sparse_attn_bwd(const void *q, const void *k, const void *v, const void *out,
                          const void *dout, const float *lse, const void *indices, int index_bytes,
@@ -214,6 +220,11 @@ PISA_API int pisa_sparse_attn_bwd(const void *q, const void *k, const void *v, c
 
 PISA_API int64_t pisa_sparse_attn_bwd_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H,
                                              int64_t D, int64_t Dv, int64_t N);
+
+/* Workspace bytes of the tensor-core backward for these shapes (0: not eligible). */
+PISA_API int64_t pisa_sparse_attn_bwd_tc_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D,
+                                                         int64_t Dv, int64_t N, int64_t S, int64_t block_size,
+                                                         int dtype);
 
 /*
  * pisa_sparse_attn_bwd without a caller workspace, for callers that cannot

@@ -44,6 +44,7 @@ SIGNATURES = {
     "pisa_sparse_attn_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _L, _I, _L, _L, _L, _L, _L,
                                   _L, _L, _L, _L, _F, _I, _P, _P, _P, _P, _L, _P]),
     "pisa_sparse_attn_bwd_workspace_bytes": (_L, [_L, _L, _L, _L, _L, _L, _L]),
+    "pisa_sparse_attn_bwd_tc_workspace_bytes": (_L, [_L, _L, _L, _L, _L, _L, _L, _L, _L, _I]),
     "pisa_sparse_attn_bwd_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _L, _I, _L, _L, _L, _L, _L,
                                           _L, _L, _L, _L, _F, _I, _P, _P, _P, _P]),
     "pisa_sparse_attn_bwd_noalloc_max_bytes": (_L, []),

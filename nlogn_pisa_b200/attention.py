@@ -55,7 +55,12 @@ def attention_backward(q, k, v, out, dout, lse, indices, block_size, scale, posi
     batch, tokens, q_heads, dim = q.shape
     heads, length, dim_v = k.shape[2], k.shape[1], v.shape[-1]
     library = _lib.lib()
-    ws = library.pisa_sparse_attn_bwd_workspace_bytes(batch, tokens, q_heads, heads, dim, dim_v, length)
+    # the tensor-core backward when the shapes allow it, else the gather kernels
+    ws = library.pisa_sparse_attn_bwd_tc_workspace_bytes(batch, tokens, q_heads, heads, dim, dim_v, length,
+                                                         indices.shape[-1], block_size, code)
+    tensor_core = ws > 0
+    if not tensor_core:
+        ws = library.pisa_sparse_attn_bwd_workspace_bytes(batch, tokens, q_heads, heads, dim, dim_v, length)
     workspace = torch.empty(ws, dtype=torch.uint8, device=q.device)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     with torch.cuda.device(q.device):
@@ -65,6 +70,8 @@ def attention_backward(q, k, v, out, dout, lse, indices, block_size, scale, posi
             tokens, q_heads, heads, dim, dim_v, length, indices.shape[-1], block_size, float(scale),
             int(bool(causal)), _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv), _lib.ptr(workspace), ws,
             _lib.stream_of(q.device)))
+    if tensor_core and _lib.status_checks():
+        _lib.check_workspace(workspace, q.device)
     return dq, dk, dv
 
 

@@ -657,25 +657,8 @@ int attn_tc_typed(AttnTcArgs a, cudaStream_t stream) {
   a.fTW = FastDiv::make(uint32_t(a.TW));
   a.fRT = FastDiv::make(uint32_t(a.RT));
   for (int t0 = 0; t0 < a.T; t0 += a.chunk) {
-    a.t0 = t0;
-    a.tlen = std::min(a.chunk, a.T - t0);
-    a.nwin = (a.tlen + a.TW - 1) / a.TW;
-    a.ftlen = FastDiv::make(uint32_t(a.tlen));
-    a.fnwin = FastDiv::make(uint32_t(a.nwin));
-    a.num_buckets = int64_t(a.B) * a.nwin * a.H * a.NB;
-    const int64_t reqs = int64_t(a.B) * a.tlen * a.H * a.S;
-    a.capacity = (reqs + a.RT - 1) / a.RT + a.num_buckets;
-    e = cudaMemsetAsync(a.counts, 0, sizeof(int32_t) * a.num_buckets, stream);
-    if (e == cudaSuccess) e = cudaMemsetAsync(a.cursors, 0, sizeof(int32_t) * a.num_buckets, stream);
-    if (e == cudaSuccess) e = cudaMemsetAsync(a.tile_req, 0xFF, sizeof(int32_t) * a.capacity * a.RT, stream);
-    if (e != cudaSuccess) return fail_cuda(e, "attention bucket clear");
-    const unsigned grid = unsigned((reqs + 255) / 256);
-    attn_count_kernel<<<grid, 256, 0, stream>>>(a);
-    PISA_CHECK_LAUNCH();
-    e = launch_tile_scan(a.counts, a.offsets, a.total_tiles, a.num_buckets, a.RT, stream);
-    if (e != cudaSuccess) return fail_cuda(e, "attention tile scan");
-    attn_scatter_kernel<<<grid, 256, 0, stream>>>(a);
-    PISA_CHECK_LAUNCH();
+    const int rc = attn_bucket_chunk(a, t0, stream);
+    if (rc != PISA_OK) return rc;
     {
       TimedLaunch timed(PISA_KERNEL_ATTN_TILES, stream);
       attn_tc_kernel<T><<<unsigned(a.num_sms), kPipeThreads, smem, stream>>>(a);
@@ -699,6 +682,29 @@ int attn_tc_typed(AttnTcArgs a, cudaStream_t stream) {
 }
 
 }  // namespace
+
+int attn_bucket_chunk(AttnTcArgs& a, int t0, cudaStream_t stream) {
+  a.t0 = t0;
+  a.tlen = std::min(a.chunk, a.T - t0);
+  a.nwin = (a.tlen + a.TW - 1) / a.TW;
+  a.ftlen = FastDiv::make(uint32_t(a.tlen));
+  a.fnwin = FastDiv::make(uint32_t(a.nwin));
+  a.num_buckets = int64_t(a.B) * a.nwin * a.H * a.NB;
+  const int64_t reqs = int64_t(a.B) * a.tlen * a.H * a.S;
+  a.capacity = (reqs + a.RT - 1) / a.RT + a.num_buckets;
+  cudaError_t e = cudaMemsetAsync(a.counts, 0, sizeof(int32_t) * a.num_buckets, stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(a.cursors, 0, sizeof(int32_t) * a.num_buckets, stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(a.tile_req, 0xFF, sizeof(int32_t) * a.capacity * a.RT, stream);
+  if (e != cudaSuccess) return fail_cuda(e, "attention bucket clear");
+  const unsigned grid = unsigned((reqs + 255) / 256);
+  attn_count_kernel<<<grid, 256, 0, stream>>>(a);
+  PISA_CHECK_LAUNCH();
+  e = launch_tile_scan(a.counts, a.offsets, a.total_tiles, a.num_buckets, a.RT, stream);
+  if (e != cudaSuccess) return fail_cuda(e, "attention tile scan");
+  attn_scatter_kernel<<<grid, 256, 0, stream>>>(a);
+  PISA_CHECK_LAUNCH();
+  return PISA_OK;
+}
 
 int attn_fwd_tc(const AttnTcArgs& a, int dtype, cudaStream_t stream) {
   if (dtype == PISA_BF16) return attn_tc_typed<__nv_bfloat16>(a, stream);

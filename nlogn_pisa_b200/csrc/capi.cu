@@ -777,6 +777,65 @@ int pisa_sparse_attn_fwd(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh
   return attn_fwd(a, dtype, static_cast<cudaStream_t>(stream));
 }
 
+}  // extern "C"
+
+namespace pisa {
+
+// Workspace of the tensor-core backward: status word, fp32 dK / dV / dQ
+// accumulators, the row dot products D = dO . O, then the request buckets of
+// one token chunk (chunks keep request indices below 2^31).
+struct BwdPlan {
+  bool tc = false;
+  int64_t TW = 4096, chunk = 0, NB = 0, RT = 0, num_buckets = 0, capacity = 0;
+  int64_t status_off = 0, dk_off = 0, dv_off = 0, dvec_off = 0, dq_off = 0, counts_off = 0, cursors_off = 0,
+          offsets_off = 0, misc_off = 0, owner_off = 0, req_off = 0, total = 0;
+};
+
+static BwdPlan plan_attn_bwd(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t Dv, int64_t N,
+                             int64_t S, int64_t C, int dtype) {
+  BwdPlan p;
+  const int64_t G = Hq / H;
+  // (head_dim 64: two 64 KB operand stages, two K/V buffers and the P / dS
+  // tiles fill 193 KB of shared memory; 128-wide heads would not fit)
+  p.tc = (dtype == PISA_BF16 || dtype == PISA_F16) && is_pow2(G) && G <= 32 && C == 64 && D == 64 && Dv == 64 &&
+         S > 0 && S <= 64 && B * Tq * Hq >= 128;
+  if (!p.tc) return p;
+  const int64_t per_token = B * H * S;
+  p.chunk = std::min<int64_t>(Tq, std::max<int64_t>(p.TW, ((int64_t(1) << 31) - 1) / per_token / p.TW * p.TW));
+  if (p.chunk * per_token >= (int64_t(1) << 31)) { p.tc = false; return p; }
+  p.NB = (N + C - 1) / C;
+  p.RT = 128 / G;
+  const int64_t nwin = (p.chunk + p.TW - 1) / p.TW;
+  p.num_buckets = B * nwin * H * p.NB;
+  p.capacity = (p.chunk * per_token + p.RT - 1) / p.RT + p.num_buckets;
+  if (p.capacity * p.RT >= (int64_t(1) << 31)) { p.tc = false; return p; }
+  int64_t off = 0;
+  p.status_off = off; off += 256;
+  p.dk_off = off; off += align_up(B * N * H * D * 4, 256);
+  p.dv_off = off; off += align_up(B * N * H * Dv * 4, 256);
+  p.dvec_off = off; off += align_up(B * Tq * Hq * 4, 256);
+  p.dq_off = off; off += align_up(B * Tq * Hq * D * 4, 256);
+  p.counts_off = off; off += align_up(p.num_buckets * 4, 256);
+  p.cursors_off = off; off += align_up(p.num_buckets * 4, 256);
+  p.offsets_off = off; off += align_up(p.num_buckets * 4, 256);
+  p.misc_off = off; off += 256;
+  p.owner_off = off; off += align_up(p.capacity * 4, 256);
+  p.req_off = off; off += align_up(p.capacity * p.RT * 4, 256);
+  p.total = off;
+  return p;
+}
+
+}  // namespace pisa
+
+extern "C" {
+
+int64_t pisa_sparse_attn_bwd_tc_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D,
+                                                int64_t Dv, int64_t N, int64_t S, int64_t block_size, int dtype) {
+  if (B <= 0 || Tq <= 0 || Hq <= 0 || H <= 0 || Hq % H || N <= 0 || block_size < 1) return 0;
+  const BwdPlan p = plan_attn_bwd(B, Tq, Hq, H, D, Dv, N, S, block_size, dtype);
+  return p.tc ? p.total : 0;
+}
+
 int64_t pisa_sparse_attn_bwd_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H,
                                              int64_t D, int64_t Dv, int64_t N) {
   (void)Tq; (void)Hq;
@@ -797,6 +856,42 @@ int pisa_sparse_attn_bwd(const void* q, const void* k, const void* v, const void
   if (index_bytes != 4 && index_bytes != 8) return fail(PISA_ERR_INVALID, "indices must be int32 or int64");
   if (D % 8 || Dv % 8 || D > 256 || Dv > 256) return fail(PISA_ERR_UNSUPPORTED, "head_dim must be a multiple of 8 and at most 256");
   if (!lse || !dq || !dk || !dv) return fail(PISA_ERR_INVALID, "lse, dq, dk and dv are required");
+  const BwdPlan bp = plan_attn_bwd(B, Tq, Hq, H, D, Dv, N, S, block_size, dtype);
+  if (bp.tc && workspace && workspace_bytes >= bp.total && out) {
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dout) || !aligned16(out))
+      return fail(PISA_ERR_UNSUPPORTED, "rows must be 16-byte aligned");
+    char* ws = static_cast<char*>(workspace);
+    cudaError_t e = cudaMemsetAsync(ws + bp.status_off, 0, 256, s);
+    if (e != cudaSuccess) return fail_cuda(e, "status clear");
+    AttnTcArgs a{};
+    a.q = q; a.q_st = Hq * D; a.q_sh = D; a.q_sb = Tq * Hq * D;
+    a.k = k; a.k_st = H * D; a.k_sh = D; a.k_sb = N * H * D;
+    a.v = v; a.v_st = H * Dv; a.v_sh = Dv; a.v_sb = N * H * Dv;
+    a.indices = indices; a.index_bytes = index_bytes;
+    a.positions = positions; a.pos_offset = position_offset;
+    a.B = int(B); a.T = int(Tq); a.Hq = int(Hq); a.H = int(H); a.G = int(Hq / H);
+    a.D = int(D); a.Dp = int(D); a.Dv = int(Dv); a.Dvp = int(Dv);
+    a.N = int(N); a.S = int(S); a.C = int(block_size); a.NB = int(bp.NB); a.TW = int(bp.TW);
+    a.RT = int(bp.RT); a.chunk = int(bp.chunk);
+    a.scale = scale; a.causal = causal ? 1 : 0; a.bf16 = dtype == PISA_BF16 ? 1 : 0;
+    a.counts = reinterpret_cast<int32_t*>(ws + bp.counts_off);
+    a.cursors = reinterpret_cast<int32_t*>(ws + bp.cursors_off);
+    a.offsets = reinterpret_cast<int32_t*>(ws + bp.offsets_off);
+    a.total_tiles = reinterpret_cast<int32_t*>(ws + bp.misc_off);
+    a.status = reinterpret_cast<int*>(ws + bp.status_off);
+    a.tile_owner = reinterpret_cast<int32_t*>(ws + bp.owner_off);
+    a.tile_req = reinterpret_cast<int32_t*>(ws + bp.req_off);
+    a.num_sms = num_sms();
+    a.out = const_cast<void*>(out); a.dout = dout; a.lse_in = lse;
+    a.dvec = reinterpret_cast<float*>(ws + bp.dvec_off);
+    a.dq_acc = reinterpret_cast<float*>(ws + bp.dq_off);
+    a.dk_acc = reinterpret_cast<float*>(ws + bp.dk_off);
+    a.dv_acc = reinterpret_cast<float*>(ws + bp.dv_off);
+    int rc = make_tensor_map(&a.tm_k, k, dtype, B, N, H, D, a.k_sb, a.k_st, a.k_sh, 1, uint32_t(block_size));
+    if (rc == PISA_OK) rc = make_tensor_map(&a.tm_v, v, dtype, B, N, H, Dv, a.v_sb, a.v_st, a.v_sh, 1, uint32_t(block_size));
+    if (rc) return rc;
+    return attn_bwd_tc(a, dtype, dq, dk, dv, s);
+  }
   const int64_t need = pisa_sparse_attn_bwd_workspace_bytes(B, Tq, Hq, H, D, Dv, N);
   if (!workspace || workspace_bytes < need) return fail(PISA_ERR_INVALID, "workspace too small");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dout)) return fail(PISA_ERR_UNSUPPORTED, "rows must be 16-byte aligned");

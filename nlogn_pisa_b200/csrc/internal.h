@@ -235,9 +235,24 @@ struct AttnTcArgs {
   void* out;
   float* lse;
   int* status;
+  // backward (attn_bwd_tc.cu): contiguous dout, the forward's lse, the row
+  // dot products D = dout . out, and fp32 gradient accumulators
+  const void* dout;
+  const float* lse_in;
+  float* dvec;        // [B, T, Hq]
+  float* dq_acc;      // [B, T, Hq, D]
+  float* dk_acc;      // [B, N, H, D]
+  float* dv_acc;      // [B, N, H, Dv]
 };
 
 int attn_fwd_tc(const AttnTcArgs& a, int dtype, cudaStream_t stream);
+
+// Buckets the requests of token chunk [t0, t0 + chunk) of `a` (count, scan,
+// scatter into tile_owner / tile_req); sets the chunk fields of `a`.
+int attn_bucket_chunk(AttnTcArgs& a, int t0, cudaStream_t stream);
+
+// Tensor-core backward over the same buckets (attn_bwd_tc.cu); writes dq, dk, dv.
+int attn_bwd_tc(const AttnTcArgs& a, int dtype, void* dq, void* dk, void* dv, cudaStream_t stream);
 int attn_bwd(const AttnArgs& a, int dtype, void* dk, void* dv, cudaStream_t stream);
 
 }  // namespace pisa

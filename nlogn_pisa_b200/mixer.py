@@ -89,6 +89,8 @@ class PyramidSparseAttention(nn.Module):
             raise ValueError(f"attention_method {config.attention_method!r} is not served by nlogn_pisa_b200")
         self.config = config
         self.layer_idx = layer_idx
+        # pyramid branching: the reference's is 2; a config may ask for 4 (this library's extension)
+        self.branching = getattr(config, "branching", 2)
         q_width = config.num_attention_heads * config.head_dim
         kv_width = config.num_key_value_heads * config.head_dim
         self.q_proj = nn.Linear(config.hidden_size, q_width, bias=config.bias)
@@ -117,8 +119,8 @@ class PyramidSparseAttention(nn.Module):
         next_cache = None
         if use_cache:
             next_cache = {} if cache is None else cache
-            pyramid = (PyramidCache.from_keys(k.detach(), block_size=cfg.block_size) if cache is None
-                       else cache["pyramid"].append(k.detach()))
+            pyramid = (PyramidCache.from_keys(k.detach(), block_size=cfg.block_size, branching=self.branching)
+                       if cache is None else cache["pyramid"].append(k.detach()))
             next_cache["pyramid"] = pyramid
             values = TensorCache.from_tensor(v.detach()) if cache is None else cache["value_storage"].append(v.detach())
             k, v = pyramid.keys, values.tensor
@@ -130,7 +132,7 @@ class PyramidSparseAttention(nn.Module):
         indices = select_blocks(q.detach(), k.detach(), method=cfg.attention_method, block_size=cfg.block_size,
                                 topk=cfg.topk, cu_seqlens=cu_seqlens, query_offset=offset,
                                 force_first=cfg.force_first, force_recent=cfg.force_recent, pyramid=pyramid,
-                                leaf_tile=cfg.leaf_tile, routing_schedule=schedule)
+                                leaf_tile=cfg.leaf_tile, routing_schedule=schedule, branching=self.branching)
         output = sparse_attention(q, k, v, indices, block_size=cfg.block_size, cu_seqlens=cu_seqlens,
                                   query_offset=offset)
         if past_key_values is not None and use_cache:

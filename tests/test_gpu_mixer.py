@@ -21,7 +21,7 @@ ROOT = Path(__file__).resolve().parents[1]
 
 def _config(**kw):
     base = dict(hidden_size=256, num_attention_heads=8, num_key_value_heads=2, head_dim=64, attention_method="pisa",
-                block_size=16, topk=8, prefill_routing=None, leaf_tile=4, force_first=True, force_recent=1,
+                block_size=16, topk=8, prefill_routing="auto", leaf_tile=4, force_first=True, force_recent=1,
                 rope_theta=10000.0, rope_fraction=0.5, rope_position_mode="document", bias=False, backend="auto")
     base.update(kw)
     return SimpleNamespace(**base)
