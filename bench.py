@@ -42,6 +42,9 @@ def parse_args():
     p.add_argument("--ref-rows", type=int, default=48, help="sampled rows per CPU worker (reference arm)")
     p.add_argument("--no-decode", action="store_true", help="skip the 128K-KV decode measurement")
     p.add_argument("--no-extra", action="store_true", help="skip the binary-pyramid and 256K lines")
+    p.add_argument("--triton-comparator", action="store_true",
+                   help="time the reference's own Triton selection (baseline/_ref) beside ours on this GPU "
+                        "and print that comparison as one JSON line instead of the benchmark")
     return p.parse_args()
 
 
@@ -362,7 +365,12 @@ def prefill_measure(w, device, rank, steps, warmup, world, kernel_timing=True, s
     invalid = (br - 1) - (leaf % br)        # siblings of the current leaf past the causal edge
     scored = torch.where(leaf + 1 > K, cand - forced - invalid, 0)
     es = q.element_size()
-    dense_nodes = sum(sizes[lv] for lv in range(1, top + 1) if sizes[lv] > K)   # scored coarse nodes per row
+    plan = lib.pisa_select_level_plan(B, N, Hq, H, D, N, code, method, C, br, K, top, first_width,
+                                      _lib.SCHEDULES["grouped"])
+    dense_lv = [lv for lv in range(1, top + 1) if (plan >> lv) & 1]           # levels scored densely
+    dense_nodes = sum(sizes[lv] for lv in dense_lv)                          # dense scores per row
+    # the descent's own coarse work per row: every scored level's candidates x their children
+    coarse_cols = sum((first_width if lv == top else br * K) * br for lv in range(1, top + 1) if sizes[lv] > K)
     work = {
         "attn_flops": attn_keys * G * 4 * D,
         "leaf_flops": scored.sum().item() * H * B * 2 * D * G * C,
@@ -371,8 +379,10 @@ def prefill_measure(w, device, rank, steps, warmup, world, kernel_timing=True, s
         "combine_bytes": valid_ids.sum().item() * G * (D * es + 8) + B * N * Hq * D * es,
         # router: read the dense coarse scores, write the leaf candidates (int32) and masks (u8)
         "router_bytes": B * N * H * (dense_nodes * 4 + br * K * 5),
-        # dense coarse levels: children of every scored coarse node, G query rows of D
-        "dense_flops": B * N * H * G * 2 * D * sum(sizes[lv - 1] for lv in range(1, top + 1) if sizes[lv] > K),
+        # dense coarse levels: children of every node of those levels, G query rows of D
+        "dense_flops": B * N * H * G * 2 * D * sum(sizes[lv - 1] for lv in dense_lv),
+        # the descent's algorithmic coarse work (candidate children per scored level)
+        "coarse_flops": B * N * H * G * 2 * D * coarse_cols,
         # final top-K: read candidates, masks and scores of the b*K leaf slots, write K int64 ids
         "final_bytes": B * N * H * (br * K * 9 + K * 8),
         "selected_flops": attn_keys * G * 4 * D,
@@ -448,7 +458,7 @@ def kernel_report(m, hbm, tensor):
 def stage_report(m, hbm, tensor):
     w = m["work"]
     work = {"pyramid": ("hbm", w["pyramid_bytes"] / 1e9, hbm, "GB/s"),
-            "select": ("tensor", (w["leaf_flops"] + w["dense_flops"]) / 1e12, tensor, "TFLOP/s"),
+            "select": ("tensor", (w["leaf_flops"] + w["coarse_flops"]) / 1e12, tensor, "TFLOP/s"),
             "attention": ("tensor", w["attn_flops"] / 1e12, tensor, "TFLOP/s")}
     out = {}
     for name, ms in m["stage_ms"].items():
@@ -680,10 +690,114 @@ def compact_line(w, m, hbm, tensor):
             "stages": stage_report(m, hbm, tensor), "kernels": kernel_report(m, hbm, tensor)}
 
 
+# ---------------------------------------------------------------------------
+# same-box GPU comparator: the reference's Triton selection
+# ---------------------------------------------------------------------------
+# (name, tokens, kv heads, head dim, topk, force_recent): the selection
+# benchmark geometry of the reference (pisa/benchmarks/flash_sparse_attn/
+# top_k_pyramid/benchmark.py:84-95: B=1, Hq=32, Hkv=2, D=64, block 64, K=8,
+# first + previous + current block forced, seed 2024) and the 32K prefill
+# configuration with the reference's binary pyramid.
+COMPARATOR_CASES = (
+    ("selection_bench", 65536, 2, 64, 8, 2),
+    ("selection_bench", 131072, 2, 64, 8, 2),
+    ("selection_bench", 262144, 2, 64, 8, 2),
+    ("prefill32k_b2", 32768, 8, 128, 32, 1),
+)
+
+
+def _device_ms(fn, steps, warmup, flush):
+    """Median CUDA-event milliseconds of fn() over `steps` calls, L2 flushed before each."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    times = []
+    for _ in range(steps):
+        flush.zero_()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        fn()
+        end.record()
+        end.synchronize()
+        times.append(start.elapsed_time(end))
+    return statistics.median(times)
+
+
+def triton_comparator(args):
+    """Selection time (fresh pyramid + prefill routing) of the reference's own
+    Triton path, select_blocks(..., backend="triton", routing_schedule=
+    "grouped", leaf_tile=4) from the offline install under baseline/_ref
+    (top_k_pyramid.py:11-122 -> top_k_pyramid_triton.py:311-447), beside this
+    library's select_blocks on the same inputs and GPU, and its BSA
+    selection (bsa_fn, backend="triton") at the selection-benchmark geometry.
+    The agreement is the fraction of (token, KV head) rows whose id sets are
+    equal; the Triton path and the torch path may differ in the last score
+    bits (top_k_pyramid.py:44-45)."""
+    import torch
+
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "pisa" / "ops").exists():
+        print(json.dumps({"comparator": "reference triton selection",
+                          "unavailable": "the reference package is not installed under baseline/_ref"}))
+        return 0
+    sys.path.insert(0, str(ref_root))
+    import nlogn_pisa_b200 as P
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    try:
+        from pisa.ops.flash_sparse_attn.bsa import bsa_fn
+        from pisa.ops.flash_sparse_attn.top_k_pyramid import top_k_pyramid_fn
+    except Exception as exc:
+        print(json.dumps({"comparator": "reference triton selection",
+                          "unavailable": f"reference import failed: {type(exc).__name__}: {exc}"}))
+        return 0
+    rows = []
+    for name, n, hkv, d, topk, recent in COMPARATOR_CASES:
+        torch.manual_seed(2024)
+        q = torch.randn(1, n, 32, d, device=device, dtype=torch.bfloat16)
+        k = torch.randn(1, n, hkv, d, device=device, dtype=torch.bfloat16)
+        opts = dict(method="pisa", block_size=64, topk=topk, force_first=True, force_recent=recent,
+                    routing_schedule="grouped", leaf_tile=4)
+        row = {"case": name, "tokens": n, "q_heads": 32, "kv_heads": hkv, "head_dim": d, "topk": topk,
+               "force_recent": recent, "branching": 2}
+        ours = lambda: P.select_blocks(q, k, backend="cuda", branching=2, **opts)  # noqa: E731
+        ref = lambda: top_k_pyramid_fn(q, k, backend="triton", **opts)  # noqa: E731
+        row["ours_ms"] = _device_ms(ours, args.steps, max(args.warmup, 3), flush)
+        try:
+            row["triton_ms"] = _device_ms(ref, args.steps, max(args.warmup, 3), flush)
+            a = ours().sort(-1).values
+            b = ref().to(torch.int64).sort(-1).values
+            row["rows_equal"] = float((a == b).all(-1).float().mean())
+            row["triton_over_ours"] = row["triton_ms"] / row["ours_ms"]
+        except Exception as exc:
+            row["triton_error"] = f"{type(exc).__name__}: {str(exc)[:200]}"
+        if name == "selection_bench":
+            try:
+                row["bsa_triton_ms"] = _device_ms(lambda: bsa_fn(q, k, block_size=64, topk=topk, backend="triton"),
+                                                  args.steps, max(args.warmup, 3), flush)
+            except Exception as exc:
+                row["bsa_error"] = f"{type(exc).__name__}: {str(exc)[:200]}"
+        rows.append(row)
+        del q, k
+        torch.cuda.empty_cache()
+    import triton
+
+    print(json.dumps({"comparator": "reference triton selection (same GPU, same inputs)",
+                      "gpu": torch.cuda.get_device_name(device), "triton": triton.__version__,
+                      "timing": f"median of {args.steps} CUDA-event samples, 256 MiB L2 flush before each",
+                      "cases": rows}), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     from nlogn_pisa_b200.workloads import WORKLOADS
 
+    if args.triton_comparator:
+        return triton_comparator(args)
     workload = WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference(args, workload)

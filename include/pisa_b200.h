@@ -140,6 +140,18 @@ PISA_API int64_t pisa_select_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, 
                                              int64_t first_width, int schedule, int build_summary);
 
 /*
+ * How pisa_select_blocks will score the coarse levels for these shapes
+ * (profiling aid; no counterpart in the reference): bit l of the low 32 bits
+ * is set when level l is scored densely (every node for every row, on the
+ * tensor cores), bit l of the high 32 bits when the router scores level l
+ * per row over the row's own candidates.  Other levels need no scores (the
+ * all-fit shortcut) or are scored by the per-item router.  -1 on bad shapes.
+ */
+PISA_API int64_t pisa_select_level_plan(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t N,
+                                        int dtype, int method, int64_t block_size, int64_t branching,
+                                        int64_t topk, int64_t top, int64_t first_width, int schedule);
+
+/*
  * Leaf scores of arbitrary candidate lists.  Replaces grouped_leaf_scores
  * (pisa/pisa/ops/flash_sparse_attn/top_k_pyramid/leaf_triton.py:144-232)
  * with its masks (leaf_scoreable_mask, leaf_triton.py:23-60).

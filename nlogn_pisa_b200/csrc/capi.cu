@@ -176,6 +176,7 @@ struct SelectPlan {
   Geometry geo{};
   // dense tensor-core scoring of whole coarse levels (dense.cu), by token chunk
   int dense_off[kMaxLevels];
+  uint32_t row_levels = 0;   // levels scored per row inside the warp router
   int64_t dense_row = 0, dense_chunk = 0, dense_off_ws = 0, status_off = 0;
   int64_t W0 = 0, NF = 0, NP = 0, nwin = 0, TW = 4096, RT = 0, rows = 0, num_buckets = 0, capacity = 0;
   int64_t pyramid_off = 0, cand_off = 0, flags_off = 0, scores_off = 0, counts_off = 0,
@@ -211,18 +212,31 @@ static SelectPlan plan_select(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int6
   const bool dense_ok = (dtype == PISA_BF16 || dtype == PISA_F16) && is_pow2(G) && G <= 32 &&
                         D % 8 == 0 && D <= 256 && Tq * G >= 1024 &&
                         (method == PISA_METHOD_PISA1 || br == 2 || br == 4);
+  // A level can instead be scored by the warp router per row, over the row's
+  // own candidates' children (at most 64 columns, G <= 16 heads, 16-bit
+  // inputs): that reads W*s child summaries per row where the dense kernel
+  // reads every child once per tile of 128/G tokens, so the row form wins
+  // once a level has more than W*s*128/G children -- the long-context levels
+  // whose dense scoring grows with the square of the sequence length.
+  const bool row_ok = (dtype == PISA_BF16 || dtype == PISA_F16) && G <= 16 && D % 8 == 0 && D <= 256 &&
+                      (method == PISA_METHOD_PISA1 || br == 2 || br == 4);
   for (int l = 0; l < kMaxLevels; ++l) p.dense_off[l] = -1;
-  if (dense_ok) {
-    for (int64_t l = top; l >= 0; --l) {
-      const int64_t n = p.geo.sizes[l];
-      int64_t children;
-      if (method == PISA_METHOD_PISA1) {
-        children = n;
-      } else {
-        if (l == 0 || n <= K) continue;
-        children = p.geo.sizes[l - 1];
-      }
-      if (children > 8192) continue;
+  p.row_levels = 0;
+  for (int64_t l = top; l >= 0; --l) {
+    const int64_t n = p.geo.sizes[l];
+    int64_t children;
+    if (method == PISA_METHOD_PISA1) {
+      children = n;
+    } else {
+      if (l == 0 || n <= K) continue;
+      children = p.geo.sizes[l - 1];
+    }
+    const int64_t cols = (l == top ? fw : K * br) * (method == PISA_METHOD_PISA1 ? 1 : br);
+    const bool dense_level = dense_ok && children <= 8192;
+    const bool row_level = row_ok && cols <= 64 && (!dense_level || cols * 128 < children * G);
+    if (row_level) {
+      p.row_levels |= 1u << l;
+    } else if (dense_level) {
       p.dense_off[l] = int(p.dense_row);
       p.dense_row += n;
     }
@@ -281,6 +295,20 @@ int64_t pisa_select_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H
     return 0;
   return plan_select(B, Tq, Hq, H, D, N, dtype, method, block_size, branching, topk, top,
                      first_width, schedule, build_summary).total;
+}
+
+int64_t pisa_select_level_plan(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t N, int dtype,
+                               int method, int64_t block_size, int64_t branching, int64_t topk, int64_t top,
+                               int64_t first_width, int schedule) {
+  if (B <= 0 || Tq <= 0 || Hq <= 0 || H <= 0 || D <= 0 || N <= 0 || block_size < 1 ||
+      branching < 2 || top < 0 || top >= kMaxLevels || Hq % H)
+    return -1;
+  const SelectPlan p = plan_select(B, Tq, Hq, H, D, N, dtype, method, block_size, branching, topk, top,
+                                   first_width, schedule, 0);
+  int64_t dense = 0;
+  for (int l = 0; l <= top; ++l)
+    if (p.dense_off[l] >= 0) dense |= int64_t(1) << l;
+  return dense | (int64_t(p.row_levels) << 32);
 }
 
 int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, const void* keys,
@@ -388,6 +416,7 @@ int pisa_select_blocks(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, 
   }
   bool counted = true;
   for (int l = 0; l < kMaxLevels; ++l) a.dense_off[l] = plan.dense_off[l];
+  a.row_levels = plan.row_levels;
   int rc = PISA_OK;
   if (plan.dense_row == 0) {
     a.t_begin = 0; a.t_count = int(Tq);

@@ -76,6 +76,9 @@ struct RouteArgs {
   const float* dense;   // precomputed level scores, rows local to the range
   int64_t dense_stride;
   int dense_off[kMaxLevels];  // per level offset in a dense row, -1 = compute here
+  // bit l: level l is scored by the warp router itself, one warp per row,
+  // with mma.sync over the row's own candidate children (router.cu)
+  uint32_t row_levels;
   FastDiv fbr, fH, ftc;       // branching, KV heads, t_count (set by the launcher)
   // grouped leaf buckets: when set, the warp router counts each active
   // (row, family) request into fam_counts (bucket = (b, window, head, family))

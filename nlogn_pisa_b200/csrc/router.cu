@@ -17,6 +17,8 @@
 // candidate block at the leaf level (lanes own keys; warp shuffles combine the
 // per-lane running max / sum of exponentials).  Warp 0 runs the network in
 // registers (element i in lane i%32, slot i/32).
+#include <type_traits>
+
 #include "internal.h"
 #include "score.cuh"
 
@@ -199,8 +201,188 @@ __device__ __forceinline__ void warp_sort(float (&s)[8], int (&id)[8], int lane)
   for (int e = 0; e < Network<WP>::E; ++e) { s[e] = ss[e]; id[e] = ii[e]; }
 }
 
+// ---------------------------------------------------------------------------
+// Per-row scoring of a coarse level inside the warp router.
+//
+// When a level holds many more nodes than a row can ever score (b*K
+// candidates, b children each), scoring every node for every token (the
+// dense kernel) does far more work than the descent needs: quadratic in the
+// sequence length.  A row-scored level instead takes the row's own
+// candidates: their children summaries (at most 64 columns) against the
+// row's G <= 16 query heads, S = Q X^T as a 16 x 8 x 16 warp MMA per column
+// tile (mma.sync; bf16/fp16 in, fp32 accumulate), then the score equations
+// of block_scores (top_k_pyramid_torch.py:48-80) per candidate, summed over
+// the heads.  tcgen05 needs M >= 64 rows per MMA; one row's G heads give 16.
+//   A fragment (row-major 16 x 16): a0 = Q[g][k0..k0+1], a1 = Q[g+8][k0..],
+//     a2 = Q[g][k0+8..], a3 = Q[g+8][k0+8..], g = lane/4, k0 = 2*(lane%4)
+//   B fragment (column n = lane/4): b0 = X[n][k0..k0+1], b1 = X[n][k0+8..]
+//   C fragment: c0, c1 = S[g][2*(lane%4) + {0,1}], c2, c3 = S[g+8][same]
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+__device__ __forceinline__ uint32_t ld_u32(const void* p) {
+  return __ldg(static_cast<const unsigned int*>(p));
+}
+
+// The row's query heads as A fragments, KS k-steps of 16 dims (zero past D and past G heads).
+template <typename T, int KS>
+__device__ __forceinline__ void load_q_frags(const RouteArgs& a, int b, int t, int h, int lane,
+                                             uint32_t (&qf)[KS][4]) {
+  const int g = lane >> 2, k0 = 2 * (lane & 3);
+  const T* q0 = static_cast<const T*>(a.q) + int64_t(b) * a.q_sb + int64_t(t) * a.q_st;
+  const T* r0 = g < a.G ? q0 + int64_t(h * a.G + g) * a.q_sh : nullptr;
+  const T* r1 = g + 8 < a.G ? q0 + int64_t(h * a.G + g + 8) * a.q_sh : nullptr;
+#pragma unroll
+  for (int ks = 0; ks < KS; ++ks) {
+    const int k = ks * 16 + k0;
+    const bool lo = k < a.D, hi = k + 8 < a.D;
+    qf[ks][0] = (r0 && lo) ? ld_u32(r0 + k) : 0u;
+    qf[ks][1] = (r1 && lo) ? ld_u32(r1 + k) : 0u;
+    qf[ks][2] = (r0 && hi) ? ld_u32(r0 + k + 8) : 0u;
+    qf[ks][3] = (r1 && hi) ? ld_u32(r1 + k + 8) : 0u;
+  }
+}
+
+// Scores of the scoreable candidates of one level (element i in lane i%32,
+// slot i/32; sid = the id when scoreable, else -1) into sc_out[i] (shared
+// memory of this warp, `width` entries; unscored entries are left alone).
+template <typename T, int KS>
+__device__ void row_level_scores(const RouteArgs& a, const uint32_t (&qf)[KS][4], const int (&sid)[8],
+                                 int width, int level, int b, int h, int lane, float* sc_out) {
+  const bool self = a.method == PISA_METHOD_PISA1;
+  const int sup = self ? 1 : a.br;                 // columns per candidate: 1, 2 or 4
+  const int lgs = sup == 1 ? 0 : (sup == 2 ? 1 : 2);
+  const int child_level = self ? level : level - 1;
+  const int child_len = a.levels.size[child_level];
+  const int64_t node_stride = int64_t(a.H) * a.D;
+  const T* base = static_cast<const T*>(a.summary) + int64_t(b) * a.s_sb +
+                  a.levels.offset[child_level] * node_stride + int64_t(h) * a.D;
+  const int ncols = width << lgs;
+  const int g = lane >> 2, k0 = 2 * (lane & 3);
+  const bool row0 = g < a.G, row1 = g + 8 < a.G;
+  for (int nt = 0; nt * 8 < ncols; ++nt) {
+    // B column of this lane: candidate cb, child jb
+    const int colb = nt * 8 + g;
+    const int cb = colb >> lgs, jb = colb & (sup - 1);
+    const int idb0 = __shfl_sync(kFull, sid[0], cb & 31), idb1 = __shfl_sync(kFull, sid[1], cb & 31);
+    const int idb = colb < ncols ? (cb < 32 ? idb0 : idb1) : -1;
+    const int node = idb < 0 ? -1 : (self ? idb : idb * a.br + jb);
+    const bool have = node >= 0 && node < child_len;
+    if (__ballot_sync(kFull, idb >= 0) == 0) continue;   // no scoreable candidate in this tile
+    const T* xr = base + int64_t(have ? node : 0) * node_stride;
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      const int k = ks * 16 + k0;
+      const uint32_t b0 = (have && k < a.D) ? ld_u32(xr + k) : 0u;
+      const uint32_t b1 = (have && k + 8 < a.D) ? ld_u32(xr + k + 8) : 0u;
+      mma16816<T>(c, qf[ks], b0, b1);
+    }
+    // this lane's C columns: 2*(lane%4) and +1 of the tile
+    const int col0 = nt * 8 + k0;
+    const int cand = col0 >> lgs;
+    float part = 0.f;   // this lane's heads' contribution to the candidate score
+    if (sup == 1) {
+      // pisa1: q . node mean (scale 1); columns col0 and col0 + 1 are two candidates
+      float p0 = (row0 ? c[0] : 0.f) + (row1 ? c[2] : 0.f);
+      float p1 = (row0 ? c[1] : 0.f) + (row1 ? c[3] : 0.f);
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        p0 += __shfl_xor_sync(kFull, p0, o);
+        p1 += __shfl_xor_sync(kFull, p1, o);
+      }
+      if (g == 0) {
+        if (col0 < ncols) sc_out[col0] = p0;
+        if (col0 + 1 < ncols) sc_out[col0 + 1] = p1;
+      }
+      continue;
+    }
+    // children of candidate `cand` that exist at the child level
+    const int cid0 = __shfl_sync(kFull, sid[0], cand & 31), cid1 = __shfl_sync(kFull, sid[1], cand & 31);
+    const int cid = col0 < ncols ? (cand < 32 ? cid0 : cid1) : -1;
+    const int nchild = cid < 0 ? 0 : max(0, min(sup, child_len - cid * a.br));
+    if (sup == 2) {
+      // both children in this lane: (c0, c1) for head g, (c2, c3) for head g+8
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        if (!(r == 0 ? row0 : row1)) continue;
+        const float z0 = c[2 * r] * a.scale, z1 = c[2 * r + 1] * a.scale;
+        float v;
+        if (a.method == PISA_METHOD_PISA) {
+          if (nchild >= 2) {
+            const float m = fmaxf(z0, z1);
+            v = m + logf(expf(z0 - m) + expf(z1 - m));
+          } else {
+            v = z0;
+          }
+        } else {
+          const float diff = z0 - z1;
+          v = nchild >= 2 ? 0.5f * (z0 + z1) + 0.125f * diff * diff : z0;
+        }
+        part += v;
+      }
+    } else {
+      // four children over a lane pair (lane%4 = 2m, 2m+1): exchange partners
+      float o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = __shfl_xor_sync(kFull, c[i], 1);
+      const bool low = (lane & 1) == 0;
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        if (!(r == 0 ? row0 : row1)) continue;
+        // children 0..3 of the candidate in column order
+        float x[4];
+        x[0] = low ? c[2 * r] : o[2 * r];
+        x[1] = low ? c[2 * r + 1] : o[2 * r + 1];
+        x[2] = low ? o[2 * r] : c[2 * r];
+        x[3] = low ? o[2 * r + 1] : c[2 * r + 1];
+        float v;
+        if (a.method == PISA_METHOD_PISA) {
+          float m = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) if (i < nchild) m = fmaxf(m, x[i] * a.scale);
+          float s = 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) if (i < nchild) s += expf(x[i] * a.scale - m);
+          v = nchild > 0 ? m + logf(s) : 0.f;
+        } else {
+          float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) if (i < nchild) { s1 += x[i]; s2 += x[i] * x[i]; }
+          const float cnt = float(nchild > 0 ? nchild : 1);
+          const float mean = s1 / cnt;
+          const float var = fmaxf(s2 / cnt - mean * mean, 0.f);
+          v = a.scale * mean + a.c2 * var;
+        }
+        part += v;
+      }
+    }
+    // sum over the heads: lanes with the same lane%4 hold the other head rows
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) part += __shfl_xor_sync(kFull, part, o);
+    if (g == 0 && cid >= 0 && (sup == 2 || (lane & 1) == 0)) sc_out[cand] = part;
+  }
+}
+
+template <typename T, int KS>
 __global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
   __shared__ int kept[4][64];
+  __shared__ float s_row[4][64];   // row-scored level: candidate scores of each warp
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t local = int64_t(blockIdx.x) * 4 + warp;
   if (local >= int64_t(a.B) * a.t_count * a.H) return;
@@ -212,8 +394,12 @@ __global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
   const int t = a.t_begin + tl;
   const int64_t item = (int64_t(b) * a.T + t) * a.H + h;
   const int64_t pos = a.positions ? a.positions[int64_t(b) * a.T + t] : a.pos_offset + t;
-  const float* dense_row = a.dense + local * a.dense_stride;
+  const float* dense_row = a.dense ? a.dense + local * a.dense_stride : nullptr;
   const int64_t leaf = pos / a.C;
+  uint32_t qf[KS > 0 ? KS : 1][4];
+  if constexpr (KS > 0) {
+    if (a.row_levels) load_q_frags<T, KS>(a, b, t, h, lane, qf);
+  }
   // forced-recent leaves leaf-r (r < force_recent, leaf-r >= 0) have, at any
   // level, ancestors forming the contiguous id range [lo_leaf / div, leaf / div]
   const int64_t lo_leaf = leaf - a.force_recent + 1 > 0 ? leaf - a.force_recent + 1 : 0;
@@ -270,13 +456,26 @@ __global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
       return;
     }
     const int off = a.dense_off[level];
+    bool row_scored = false;
+    if constexpr (KS > 0) {
+      if (((a.row_levels >> level) & 1u) && !identity) {
+        int sid[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sid[e] = (e * 32 + lane < width && valid[e] && !forced[e]) ? id[e] : -1;
+        row_level_scores<T, KS>(a, qf, sid, width, level, b, h, lane, s_row[warp]);
+        __syncwarp();
+        row_scored = true;
+      }
+    }
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const bool scoreable = valid[e] && !forced[e] && !identity;
-      float v = scoreable ? dense_row[off + id[e]] : 0.f;
+      float v = 0.f;
+      if (scoreable) v = row_scored ? s_row[warp][e * 32 + lane] : dense_row[off + id[e]];
       sc[e] = !valid[e] ? kNegFill : (forced[e] ? kPosFill : v);
       if (e * 32 + lane >= width) { sc[e] = kNegFill; id[e] = -1; }
     }
+    __syncwarp();
     switch (width) {
       case 16: warp_sort<16>(sc, id, lane); break;
       case 32: warp_sort<32>(sc, id, lane); break;
@@ -344,24 +543,44 @@ int route_t(const RouteArgs& a, cudaStream_t stream) {
 
 int route(const RouteArgs& a, int dtype, cudaStream_t stream, bool* counted) {
   if (counted) *counted = false;
-  // every scored level precomputed: the warp-per-item router
-  bool all_dense = a.dense != nullptr;
-  for (int l = a.top; l >= 0 && all_dense; --l) {
+  // every scored level precomputed or row-scored: the warp-per-item router
+  bool warp_ok = true;
+  for (int l = a.top; l >= 0 && warp_ok; --l) {
     if (l == 0 && a.coarse_only) break;
-    if (a.dense_off[l] < 0) {
+    const bool dense = a.dense != nullptr && a.dense_off[l] >= 0;
+    const bool rowl = (a.row_levels >> l) & 1u;
+    if (!dense && !rowl) {
       // unscored levels are fine only when every row takes the all-fit shortcut
-      if (a.method == PISA_METHOD_PISA1 || a.levels.size[l] > a.K) all_dense = false;
+      if (a.method == PISA_METHOD_PISA1 || a.levels.size[l] > a.K) warp_ok = false;
     }
   }
   const int64_t items = int64_t(a.B) * a.t_count * a.H;
-  if (all_dense && items < (int64_t(1) << 31)) {
+  if (warp_ok && items < (int64_t(1) << 31)) {
     if (items == 0) return PISA_OK;
     RouteArgs w = a;
     w.fbr = FastDiv::make(uint32_t(a.br));
     w.fH = FastDiv::make(uint32_t(a.H));
     w.ftc = FastDiv::make(uint32_t(a.t_count));
+    const unsigned grid = unsigned((items + 3) / 4);
     TimedLaunch timed(PISA_KERNEL_ROUTER, stream);
-    route_warp_kernel<<<unsigned((items + 3) / 4), 128, 0, stream>>>(w);
+    if (a.row_levels == 0) {
+      route_warp_kernel<float, 0><<<grid, 128, 0, stream>>>(w);
+    } else {
+      // row-scored levels: 16-bit inputs, head_dim a multiple of 16 up to 256
+      const int ks = (a.D + 15) / 16;
+      const bool bf = dtype == PISA_BF16;
+      if (dtype == PISA_F32) return fail(PISA_ERR_UNSUPPORTED, "row-scored levels need fp16 or bf16");
+      if (ks <= 4) {
+        if (bf) route_warp_kernel<__nv_bfloat16, 4><<<grid, 128, 0, stream>>>(w);
+        else route_warp_kernel<__half, 4><<<grid, 128, 0, stream>>>(w);
+      } else if (ks <= 8) {
+        if (bf) route_warp_kernel<__nv_bfloat16, 8><<<grid, 128, 0, stream>>>(w);
+        else route_warp_kernel<__half, 8><<<grid, 128, 0, stream>>>(w);
+      } else {
+        if (bf) route_warp_kernel<__nv_bfloat16, 16><<<grid, 128, 0, stream>>>(w);
+        else route_warp_kernel<__half, 16><<<grid, 128, 0, stream>>>(w);
+      }
+    }
     PISA_CHECK_LAUNCH();
     if (counted) *counted = a.fam_counts != nullptr;
     return PISA_OK;

@@ -126,3 +126,26 @@ def test_decode_step_128k_cache_64_sequences(cuda_device):
         _check_ids(got, want, trace, 1.0)
         ref, _ = O.sparse_attention(qn, kn, vn, got, C, positions=pos)
         np.testing.assert_allclose(out[b:b + 1].float().cpu().numpy(), ref, rtol=0, atol=2e-2)
+
+
+@pytest.mark.parametrize("method,branching", [("pisa", 2), ("pisa2", 2), ("pisa1", 2), ("pisa", 4), ("pisa2", 4)])
+def test_selection_benchmark_geometry_row_scored_levels(cuda_device, method, branching):
+    """The reference's selection-benchmark geometry (Hq=32, Hkv=2, D=64, C=64,
+    K=8, first + previous + current block forced; benchmark.py:84-95) at a
+    length where the warp router scores the long coarse levels per row
+    (mma.sync over each row's own candidate children) instead of densely."""
+    import nlogn_pisa_b200 as P
+
+    torch.manual_seed(2024)
+    B, N, Hq, H, D, C, K = 1, 65536, 32, 2, 64, 64, 8
+    q = torch.randn(B, N, Hq, D, device=cuda_device, dtype=torch.bfloat16)
+    k = torch.randn(B, N, H, D, device=cuda_device, dtype=torch.bfloat16)
+    ids = P.select_blocks(q, k, method=method, block_size=C, topk=K, force_recent=2, branching=branching)
+    rows = _rows(N, 6, 11)
+    qn = q[:, rows].float().cpu().numpy()
+    kn = k.float().cpu().numpy()
+    levels = O.build_pyramid(kn, C, "bf16", branching=branching)
+    pos = np.broadcast_to(rows[None], (1, len(rows)))
+    trace = {}
+    want = O.pyramid_select(qn, kn, method, C, K, pos, True, 2, levels, branching=branching, trace=trace)
+    _check_ids(ids[:, rows].cpu().numpy(), want, trace, 0.9)
