@@ -214,12 +214,11 @@ static SelectPlan plan_select(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int6
                         (method == PISA_METHOD_PISA1 || br == 2 || br == 4);
   // A level can instead be scored by the warp router per row, over the row's
   // own candidates' children (at most 64 columns, G <= 16 heads, 16-bit
-  // inputs): that reads W*s child summaries per row where the dense kernel
-  // reads every child once per tile of 128/G tokens, so the row form wins
-  // once a level has more than W*s*128/G children -- the long-context levels
-  // whose dense scoring grows with the square of the sequence length.
+  // inputs): W*s child summaries per row, the descent's own work, where the
+  // dense kernel scores every node of the level for every row -- work that
+  // grows with the square of the sequence length.
   const bool row_ok = (dtype == PISA_BF16 || dtype == PISA_F16) && G <= 16 && D % 8 == 0 && D <= 256 &&
-                      (method == PISA_METHOD_PISA1 || br == 2 || br == 4);
+                      (method == PISA_METHOD_PISA1 || br == 2 || br == 4) && std::max(fw, K * br) <= 64;
   for (int l = 0; l < kMaxLevels; ++l) p.dense_off[l] = -1;
   p.row_levels = 0;
   for (int64_t l = top; l >= 0; --l) {
@@ -233,7 +232,9 @@ static SelectPlan plan_select(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int6
     }
     const int64_t cols = (l == top ? fw : K * br) * (method == PISA_METHOD_PISA1 ? 1 : br);
     const bool dense_level = dense_ok && children <= 8192;
-    const bool row_level = row_ok && cols <= 64 && (!dense_level || cols * 128 < children * G);
+    // (a dense level also reloads every row's queries, so at these widths the
+    // row form is the cheaper one whatever the level's size)
+    const bool row_level = row_ok && cols <= 64;
     if (row_level) {
       p.row_levels |= 1u << l;
     } else if (dense_level) {

@@ -17,10 +17,12 @@
 // candidate block at the leaf level (lanes own keys; warp shuffles combine the
 // per-lane running max / sum of exponentials).  Warp 0 runs the network in
 // registers (element i in lane i%32, slot i/32).
+#include <algorithm>
 #include <type_traits>
 
 #include "internal.h"
 #include "score.cuh"
+#include "tc.cuh"
 
 namespace pisa {
 
@@ -184,14 +186,10 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const RouteArgs a) {
   }
 }
 
-// Warp-per-item router for descents whose every scored level has precomputed
-// scores (dense.cu): levels >= 1 for pisa/pisa2 when the leaf level is left to
-// the grouped tensor-core scorer (coarse_only), every level for pisa1.  The
-// candidates and scores live in registers (element i in lane i%32, slot
-// i/32), validity is counted with ballots, and the same comparison network
-// picks the K survivors; their children are expanded through shared memory.
-template <int WP>
-__device__ __forceinline__ void warp_sort(float (&s)[8], int (&id)[8], int lane) {
+// The comparison network over the first WP elements of E register slots
+// (element i in lane i%32, slot i/32).
+template <int WP, int E>
+__device__ __forceinline__ void warp_sort(float (&s)[E], int (&id)[E], int lane) {
   float ss[Network<WP>::E];
   int ii[Network<WP>::E];
 #pragma unroll
@@ -201,69 +199,101 @@ __device__ __forceinline__ void warp_sort(float (&s)[8], int (&id)[8], int lane)
   for (int e = 0; e < Network<WP>::E; ++e) { s[e] = ss[e]; id[e] = ii[e]; }
 }
 
+// The network of the level's width (a power of two from 16 to 32*E).
+template <int E>
+__device__ __forceinline__ void warp_sort_width(float (&s)[E], int (&id)[E], int lane, int width) {
+  if (width <= 16) warp_sort<16, E>(s, id, lane);
+  else if (width <= 32) warp_sort<32, E>(s, id, lane);
+  else if constexpr (E >= 2) {
+    if (width <= 64) warp_sort<64, E>(s, id, lane);
+    else if constexpr (E >= 4) {
+      if (width <= 128) warp_sort<128, E>(s, id, lane);
+      else if constexpr (E >= 8) warp_sort<256, E>(s, id, lane);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Per-row scoring of a coarse level inside the warp router.
 //
-// When a level holds many more nodes than a row can ever score (b*K
-// candidates, b children each), scoring every node for every token (the
-// dense kernel) does far more work than the descent needs: quadratic in the
-// sequence length.  A row-scored level instead takes the row's own
+// Dense scoring (dense.cu) scores every node of a level for every token:
+// its work grows with the square of the sequence length, and each level
+// reloads the rows' queries.  A row-scored level instead takes the row's own
 // candidates: their children summaries (at most 64 columns) against the
 // row's G <= 16 query heads, S = Q X^T as a 16 x 8 x 16 warp MMA per column
 // tile (mma.sync; bf16/fp16 in, fp32 accumulate), then the score equations
 // of block_scores (top_k_pyramid_torch.py:48-80) per candidate, summed over
-// the heads.  tcgen05 needs M >= 64 rows per MMA; one row's G heads give 16.
-//   A fragment (row-major 16 x 16): a0 = Q[g][k0..k0+1], a1 = Q[g+8][k0..],
-//     a2 = Q[g][k0+8..], a3 = Q[g+8][k0+8..], g = lane/4, k0 = 2*(lane%4)
-//   B fragment (column n = lane/4): b0 = X[n][k0..k0+1], b1 = X[n][k0+8..]
-//   C fragment: c0, c1 = S[g][2*(lane%4) + {0,1}], c2, c3 = S[g+8][same]
+// the heads -- the reference descent's own O(K) work per level.  (tcgen05
+// needs M >= 64 rows per MMA; one row's G heads give 16.)
+//
+// Fragment layout (m16n8k16, g = lane/4, c = lane%4).  The dot product sums
+// over all head dims, so any one-to-one map of the MMA's k index onto the
+// dims, shared by A and B, gives the same sums; the map used here lets each
+// lane fetch its part of a row with one 16-byte load per 32 dims: for the
+// dim pair-step p (dims 32p .. 32p+31) lane c holds dims 32p+8c .. 32p+8c+7,
+// whose words 0,1 are (k0..1, k8..9) of k-step 2p and words 2,3 those of
+// k-step 2p+1, with k0 = 2c.
+//   A (row-major 16 x 16): a0/a2 = Q[g] words, a1/a3 = Q[g+8] words
+//   B (column n = g of the tile): b0/b1 = X[n] words
+//   C: c0, c1 = S[g][2c + {0,1}], c2, c3 = S[g+8][same]
 // ---------------------------------------------------------------------------
+constexpr float kLog2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
+
+// log2 on the MUFU unit (lg2.approx: relative error about 2^-22)
+__device__ __forceinline__ float lg2f(float x) {
+  float r;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 template <typename T>
-__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   } else {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   }
 }
 
-__device__ __forceinline__ uint32_t ld_u32(const void* p) {
-  return __ldg(static_cast<const unsigned int*>(p));
+// 16 bytes of a query / summary row (read-only path), zero when absent.
+__device__ __forceinline__ uint4 ld_row16(const void* p, bool ok) {
+  return ok ? __ldg(static_cast<const uint4*>(p)) : make_uint4(0u, 0u, 0u, 0u);
 }
 
-// The row's query heads as A fragments, KS k-steps of 16 dims (zero past D and past G heads).
-template <typename T, int KS>
+// The row's query heads as A fragments: KP pair-steps of 32 dims, rows g and
+// g+8 (zero past D and past G heads).
+template <typename T, int KP>
 __device__ __forceinline__ void load_q_frags(const RouteArgs& a, int b, int t, int h, int lane,
-                                             uint32_t (&qf)[KS][4]) {
-  const int g = lane >> 2, k0 = 2 * (lane & 3);
-  const T* q0 = static_cast<const T*>(a.q) + int64_t(b) * a.q_sb + int64_t(t) * a.q_st;
-  const T* r0 = g < a.G ? q0 + int64_t(h * a.G + g) * a.q_sh : nullptr;
-  const T* r1 = g + 8 < a.G ? q0 + int64_t(h * a.G + g + 8) * a.q_sh : nullptr;
+                                             uint4 (&q0)[KP], uint4 (&q1)[KP]) {
+  const int g = lane >> 2, c = lane & 3;
+  const T* base = static_cast<const T*>(a.q) + int64_t(b) * a.q_sb + int64_t(t) * a.q_st;
+  const T* r0 = base + int64_t(h * a.G + g) * a.q_sh;
+  const T* r1 = base + int64_t(h * a.G + g + 8) * a.q_sh;
 #pragma unroll
-  for (int ks = 0; ks < KS; ++ks) {
-    const int k = ks * 16 + k0;
-    const bool lo = k < a.D, hi = k + 8 < a.D;
-    qf[ks][0] = (r0 && lo) ? ld_u32(r0 + k) : 0u;
-    qf[ks][1] = (r1 && lo) ? ld_u32(r1 + k) : 0u;
-    qf[ks][2] = (r0 && hi) ? ld_u32(r0 + k + 8) : 0u;
-    qf[ks][3] = (r1 && hi) ? ld_u32(r1 + k + 8) : 0u;
+  for (int p = 0; p < KP; ++p) {
+    const int d = 32 * p + 8 * c;
+    q0[p] = ld_row16(r0 + d, g < a.G && d < a.D);
+    q1[p] = ld_row16(r1 + d, g + 8 < a.G && d < a.D);
   }
 }
 
 // Scores of the scoreable candidates of one level (element i in lane i%32,
 // slot i/32; sid = the id when scoreable, else -1) into sc_out[i] (shared
-// memory of this warp, `width` entries; unscored entries are left alone).
-template <typename T, int KS>
-__device__ void row_level_scores(const RouteArgs& a, const uint32_t (&qf)[KS][4], const int (&sid)[8],
-                                 int width, int level, int b, int h, int lane, float* sc_out) {
+// memory of this warp, `width` <= 64 entries; unscored entries are left alone).
+template <typename T, int KP>
+__device__ void row_level_scores(const RouteArgs& a, const uint4 (&q0)[KP], const uint4 (&q1)[KP],
+                                 int sid0, int sid1, int width, int level, int b, int h, int lane,
+                                 float* sc_out) {
+  constexpr int NG = KP >= 4 ? 1 : 4 / KP;        // column tiles whose loads are in flight together
   const bool self = a.method == PISA_METHOD_PISA1;
   const int sup = self ? 1 : a.br;                 // columns per candidate: 1, 2 or 4
   const int lgs = sup == 1 ? 0 : (sup == 2 ? 1 : 2);
@@ -273,114 +303,132 @@ __device__ void row_level_scores(const RouteArgs& a, const uint32_t (&qf)[KS][4]
   const T* base = static_cast<const T*>(a.summary) + int64_t(b) * a.s_sb +
                   a.levels.offset[child_level] * node_stride + int64_t(h) * a.D;
   const int ncols = width << lgs;
-  const int g = lane >> 2, k0 = 2 * (lane & 3);
+  const int g = lane >> 2, c = lane & 3;
   const bool row0 = g < a.G, row1 = g + 8 < a.G;
-  for (int nt = 0; nt * 8 < ncols; ++nt) {
-    // B column of this lane: candidate cb, child jb
-    const int colb = nt * 8 + g;
-    const int cb = colb >> lgs, jb = colb & (sup - 1);
-    const int idb0 = __shfl_sync(kFull, sid[0], cb & 31), idb1 = __shfl_sync(kFull, sid[1], cb & 31);
-    const int idb = colb < ncols ? (cb < 32 ? idb0 : idb1) : -1;
-    const int node = idb < 0 ? -1 : (self ? idb : idb * a.br + jb);
-    const bool have = node >= 0 && node < child_len;
-    if (__ballot_sync(kFull, idb >= 0) == 0) continue;   // no scoreable candidate in this tile
-    const T* xr = base + int64_t(have ? node : 0) * node_stride;
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int nt0 = 0; nt0 * 8 < ncols; nt0 += NG) {
+    // this group's B rows: column nt*8 + g of each tile, one 16-byte load per pair-step
+    uint4 xv[NG][KP];
+    bool any[NG];
 #pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-      const int k = ks * 16 + k0;
-      const uint32_t b0 = (have && k < a.D) ? ld_u32(xr + k) : 0u;
-      const uint32_t b1 = (have && k + 8 < a.D) ? ld_u32(xr + k + 8) : 0u;
-      mma16816<T>(c, qf[ks], b0, b1);
-    }
-    // this lane's C columns: 2*(lane%4) and +1 of the tile
-    const int col0 = nt * 8 + k0;
-    const int cand = col0 >> lgs;
-    float part = 0.f;   // this lane's heads' contribution to the candidate score
-    if (sup == 1) {
-      // pisa1: q . node mean (scale 1); columns col0 and col0 + 1 are two candidates
-      float p0 = (row0 ? c[0] : 0.f) + (row1 ? c[2] : 0.f);
-      float p1 = (row0 ? c[1] : 0.f) + (row1 ? c[3] : 0.f);
+    for (int u = 0; u < NG; ++u) {
+      const int colb = (nt0 + u) * 8 + g;
+      const int cb = colb >> lgs, jb = colb & (sup - 1);
+      const int i0 = __shfl_sync(kFull, sid0, cb & 31), i1 = __shfl_sync(kFull, sid1, cb & 31);
+      const int idb = colb < ncols ? (cb < 32 ? i0 : i1) : -1;
+      const int node = idb < 0 ? -1 : (self ? idb : idb * a.br + jb);
+      const bool have = node >= 0 && node < child_len;
+      any[u] = __ballot_sync(kFull, idb >= 0) != 0;
+      const T* xr = base + int64_t(have ? node : 0) * node_stride;
 #pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        p0 += __shfl_xor_sync(kFull, p0, o);
-        p1 += __shfl_xor_sync(kFull, p1, o);
+      for (int p = 0; p < KP; ++p) {
+        const int d = 32 * p + 8 * c;
+        xv[u][p] = ld_row16(xr + d, have && d < a.D);
       }
-      if (g == 0) {
-        if (col0 < ncols) sc_out[col0] = p0;
-        if (col0 + 1 < ncols) sc_out[col0 + 1] = p1;
-      }
-      continue;
     }
-    // children of candidate `cand` that exist at the child level
-    const int cid0 = __shfl_sync(kFull, sid[0], cand & 31), cid1 = __shfl_sync(kFull, sid[1], cand & 31);
-    const int cid = col0 < ncols ? (cand < 32 ? cid0 : cid1) : -1;
-    const int nchild = cid < 0 ? 0 : max(0, min(sup, child_len - cid * a.br));
-    if (sup == 2) {
-      // both children in this lane: (c0, c1) for head g, (c2, c3) for head g+8
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        if (!(r == 0 ? row0 : row1)) continue;
-        const float z0 = c[2 * r] * a.scale, z1 = c[2 * r + 1] * a.scale;
-        float v;
-        if (a.method == PISA_METHOD_PISA) {
-          if (nchild >= 2) {
-            const float m = fmaxf(z0, z1);
-            v = m + logf(expf(z0 - m) + expf(z1 - m));
+    for (int u = 0; u < NG; ++u) {
+      const int nt = nt0 + u;
+      if (nt * 8 >= ncols || !any[u]) continue;    // warp-uniform
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int p = 0; p < KP; ++p) {
+        mma16816<T>(acc, q0[p].x, q1[p].x, q0[p].y, q1[p].y, xv[u][p].x, xv[u][p].y);
+        mma16816<T>(acc, q0[p].z, q1[p].z, q0[p].w, q1[p].w, xv[u][p].z, xv[u][p].w);
+      }
+      // this lane's C columns: 2c and 2c + 1 of the tile
+      const int col0 = nt * 8 + 2 * c;
+      if (sup == 1) {
+        // pisa1: q . node mean (scale 1); columns col0 and col0 + 1 are two candidates
+        float p0 = (row0 ? acc[0] : 0.f) + (row1 ? acc[2] : 0.f);
+        float p1 = (row0 ? acc[1] : 0.f) + (row1 ? acc[3] : 0.f);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          p0 += __shfl_xor_sync(kFull, p0, o);
+          p1 += __shfl_xor_sync(kFull, p1, o);
+        }
+        if (g == 0) {
+          if (col0 < ncols) sc_out[col0] = p0;
+          if (col0 + 1 < ncols) sc_out[col0 + 1] = p1;
+        }
+        continue;
+      }
+      // children of candidate `cand` that exist at the child level
+      const int cand = col0 >> lgs;
+      const int c0 = __shfl_sync(kFull, sid0, cand & 31), c1 = __shfl_sync(kFull, sid1, cand & 31);
+      const int cid = col0 < ncols ? (cand < 32 ? c0 : c1) : -1;
+      const int nchild = cid < 0 ? 0 : max(0, min(sup, child_len - cid * a.br));
+      float part = 0.f;   // this lane's heads' contribution to the candidate score
+      if (sup == 2) {
+        // both children in this lane: (c0, c1) for head g, (c2, c3) for head g+8
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          if (!(r == 0 ? row0 : row1)) continue;
+          const float z0 = acc[2 * r] * a.scale, z1 = acc[2 * r + 1] * a.scale;
+          float v;
+          if (a.method == PISA_METHOD_PISA) {
+            // log(e^z0 + e^z1) = m + ln2 * log2(1 + 2^(-|z0 - z1| * log2 e))
+            v = nchild >= 2 ? fmaxf(z0, z1) + kLn2 * lg2f(1.f + tc::ex2f(-fabsf(z0 - z1) * kLog2e)) : z0;
           } else {
-            v = z0;
+            const float diff = z0 - z1;
+            v = nchild >= 2 ? 0.5f * (z0 + z1) + 0.125f * diff * diff : z0;
           }
-        } else {
-          const float diff = z0 - z1;
-          v = nchild >= 2 ? 0.5f * (z0 + z1) + 0.125f * diff * diff : z0;
+          part += v;
         }
-        part += v;
-      }
-    } else {
-      // four children over a lane pair (lane%4 = 2m, 2m+1): exchange partners
-      float o[4];
+      } else {
+        // four children over a lane pair (c = 2m, 2m+1): exchange with the partner
+        float o[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] = __shfl_xor_sync(kFull, c[i], 1);
-      const bool low = (lane & 1) == 0;
+        for (int i = 0; i < 4; ++i) o[i] = __shfl_xor_sync(kFull, acc[i], 1);
+        const bool low = (lane & 1) == 0;
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        if (!(r == 0 ? row0 : row1)) continue;
-        // children 0..3 of the candidate in column order
-        float x[4];
-        x[0] = low ? c[2 * r] : o[2 * r];
-        x[1] = low ? c[2 * r + 1] : o[2 * r + 1];
-        x[2] = low ? o[2 * r] : c[2 * r];
-        x[3] = low ? o[2 * r + 1] : c[2 * r + 1];
-        float v;
-        if (a.method == PISA_METHOD_PISA) {
-          float m = -INFINITY;
+        for (int r = 0; r < 2; ++r) {
+          if (!(r == 0 ? row0 : row1)) continue;
+          float x[4];   // children 0..3 of the candidate, in column order
+          x[0] = low ? acc[2 * r] : o[2 * r];
+          x[1] = low ? acc[2 * r + 1] : o[2 * r + 1];
+          x[2] = low ? o[2 * r] : acc[2 * r];
+          x[3] = low ? o[2 * r + 1] : acc[2 * r + 1];
+          float v;
+          if (a.method == PISA_METHOD_PISA) {
+            // base 2: y = x * scale * log2 e; LSE = ln2 * (max y + log2 sum 2^(y - max y))
+            const float k2 = a.scale * kLog2e;
+            float m = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) if (i < nchild) m = fmaxf(m, x[i] * a.scale);
-          float s = 0.f;
+            for (int i = 0; i < 4; ++i) if (i < nchild) m = fmaxf(m, x[i] * k2);
+            float s = 0.f;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) if (i < nchild) s += expf(x[i] * a.scale - m);
-          v = nchild > 0 ? m + logf(s) : 0.f;
-        } else {
-          float s1 = 0.f, s2 = 0.f;
+            for (int i = 0; i < 4; ++i) if (i < nchild) s += tc::ex2f(fmaf(x[i], k2, -m));
+            v = nchild > 0 ? kLn2 * (m + lg2f(s)) : 0.f;
+          } else {
+            float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) if (i < nchild) { s1 += x[i]; s2 += x[i] * x[i]; }
-          const float cnt = float(nchild > 0 ? nchild : 1);
-          const float mean = s1 / cnt;
-          const float var = fmaxf(s2 / cnt - mean * mean, 0.f);
-          v = a.scale * mean + a.c2 * var;
+            for (int i = 0; i < 4; ++i) if (i < nchild) { s1 += x[i]; s2 += x[i] * x[i]; }
+            const float cnt = float(nchild > 0 ? nchild : 1);
+            const float mean = s1 / cnt;
+            const float var = fmaxf(s2 / cnt - mean * mean, 0.f);
+            v = a.scale * mean + a.c2 * var;
+          }
+          part += v;
         }
-        part += v;
       }
+      // sum over the heads: lanes with the same lane%4 hold the other head rows
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) part += __shfl_xor_sync(kFull, part, o);
+      if (g == 0 && cid >= 0 && (sup == 2 || (lane & 1) == 0)) sc_out[cand] = part;
     }
-    // sum over the heads: lanes with the same lane%4 hold the other head rows
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) part += __shfl_xor_sync(kFull, part, o);
-    if (g == 0 && cid >= 0 && (sup == 2 || (lane & 1) == 0)) sc_out[cand] = part;
   }
 }
 
-template <typename T, int KS>
-__global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
+// Warp-per-item router for descents whose every scored level has precomputed
+// scores (dense.cu) or is row-scored here (KP > 0 pair-steps of head dims):
+// levels >= 1 for pisa/pisa2 when the leaf level is left to the grouped
+// tensor-core scorer (coarse_only), every level for pisa1.  The candidates
+// and scores live in registers (element i in lane i%32, slot i/32; E slots,
+// widths up to 32*E), validity is counted with ballots, and the same
+// comparison network picks the K survivors; their children are expanded
+// through shared memory.
+template <typename T, int KP, int E>
+__global__ void __launch_bounds__(128, (KP > 0 && KP <= 4) ? 6 : 1) route_warp_kernel(const RouteArgs a) {
   __shared__ int kept[4][64];
   __shared__ float s_row[4][64];   // row-scored level: candidate scores of each warp
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -396,28 +444,28 @@ __global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
   const int64_t pos = a.positions ? a.positions[int64_t(b) * a.T + t] : a.pos_offset + t;
   const float* dense_row = a.dense ? a.dense + local * a.dense_stride : nullptr;
   const int64_t leaf = pos / a.C;
-  uint32_t qf[KS > 0 ? KS : 1][4];
-  if constexpr (KS > 0) {
-    if (a.row_levels) load_q_frags<T, KS>(a, b, t, h, lane, qf);
-  }
+  uint4 q0[KP > 0 ? KP : 1], q1[KP > 0 ? KP : 1];
+  if constexpr (KP > 0) load_q_frags<T, KP>(a, b, t, h, lane, q0, q1);
   // forced-recent leaves leaf-r (r < force_recent, leaf-r >= 0) have, at any
   // level, ancestors forming the contiguous id range [lo_leaf / div, leaf / div]
   const int64_t lo_leaf = leaf - a.force_recent + 1 > 0 ? leaf - a.force_recent + 1 : 0;
-  int64_t span = a.C, div = 1;
-  for (int l = 0; l < a.top; ++l) { span *= a.br; div *= a.br; }
+  // branching is a power of two (2 or 4): ancestors by shifts
+  const int lgb = 31 - __clz(a.br);
+  int64_t span = int64_t(a.C) << (lgb * a.top);
+  int sh = lgb * a.top;   // log2 of br^level
 
-  int id[8];
-  float sc[8];
+  int id[E];
+  float sc[E];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) id[e] = e * 32 + lane;   // top level: 0..first_width-1
+  for (int e = 0; e < E; ++e) id[e] = e * 32 + lane;   // top level: 0..first_width-1
   int width = a.first_width;
   for (int level = a.top; level >= 0; --level) {
     const int len = a.levels.size[level];
-    const int64_t f_hi = leaf >= 0 ? leaf / div : -1, f_lo = leaf >= 0 ? lo_leaf / div : 0;
-    bool valid[8], forced[8];
+    const int64_t f_hi = leaf >= 0 ? leaf >> sh : -1, f_lo = leaf >= 0 ? lo_leaf >> sh : 0;
+    bool valid[E], forced[E];
     int nvalid = 0;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
+    for (int e = 0; e < E; ++e) {
       const int i = e * 32 + lane;
       int v = i < width ? id[e] : -1;
       if (v >= len) v = -1;
@@ -439,7 +487,7 @@ __global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
       // lane counts the family's request when any child is scoreable
       const int bucket0 = a.fam_counts ? ((b * a.nwin + t / a.TW) * a.H + h) * a.NP : 0;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
+      for (int e = 0; e < E; ++e) {
         const int i = e * 32 + lane;
         const bool scoreable = i < width && valid[e] && !forced[e] && !identity;
         if (i < width) {
@@ -457,18 +505,19 @@ __global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
     }
     const int off = a.dense_off[level];
     bool row_scored = false;
-    if constexpr (KS > 0) {
+    if constexpr (KP > 0) {
       if (((a.row_levels >> level) & 1u) && !identity) {
-        int sid[8];
+        int sid[2];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) sid[e] = (e * 32 + lane < width && valid[e] && !forced[e]) ? id[e] : -1;
-        row_level_scores<T, KS>(a, qf, sid, width, level, b, h, lane, s_row[warp]);
+        for (int e = 0; e < 2; ++e)
+          sid[e] = (e < E && e * 32 + lane < width && valid[e] && !forced[e]) ? id[e < E ? e : 0] : -1;
+        row_level_scores<T, KP>(a, q0, q1, sid[0], sid[1], width, level, b, h, lane, s_row[warp]);
         __syncwarp();
         row_scored = true;
       }
     }
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
+    for (int e = 0; e < E; ++e) {
       const bool scoreable = valid[e] && !forced[e] && !identity;
       float v = 0.f;
       if (scoreable) v = row_scored ? s_row[warp][e * 32 + lane] : dense_row[off + id[e]];
@@ -476,17 +525,11 @@ __global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
       if (e * 32 + lane >= width) { sc[e] = kNegFill; id[e] = -1; }
     }
     __syncwarp();
-    switch (width) {
-      case 16: warp_sort<16>(sc, id, lane); break;
-      case 32: warp_sort<32>(sc, id, lane); break;
-      case 64: warp_sort<64>(sc, id, lane); break;
-      case 128: warp_sort<128>(sc, id, lane); break;
-      default: warp_sort<256>(sc, id, lane); break;
-    }
+    warp_sort_width<E>(sc, id, lane, width);
     if (level == 0) {
       int64_t* out = a.out_ids + item * a.K;
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
+      for (int e = 0; e < (E < 2 ? E : 2); ++e) {
         const int i = e * 32 + lane;
         if (i < a.K) out[i] = (id[e] < 0 || int64_t(id[e]) * a.C > pos) ? -1 : id[e];
       }
@@ -494,22 +537,22 @@ __global__ void __launch_bounds__(128) route_warp_kernel(const RouteArgs a) {
     }
     // survivors -> shared memory -> children in network order
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
+    for (int e = 0; e < (E < 2 ? E : 2); ++e) {
       const int i = e * 32 + lane;
       if (i < a.K) kept[warp][i] = id[e];
     }
     __syncwarp();
     width = a.K * a.br;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
+    for (int e = 0; e < E; ++e) {
       const int i = e * 32 + lane;
       const int q = int(a.fbr.div(uint32_t(i)));
       const int parent = i < width ? kept[warp][q] : -1;
       id[e] = parent < 0 ? -1 : parent * a.br + (i - q * a.br);
     }
     __syncwarp();
-    span /= a.br;
-    div /= a.br;
+    span >>= lgb;
+    sh -= lgb;
   }
 }
 
@@ -563,22 +606,29 @@ int route(const RouteArgs& a, int dtype, cudaStream_t stream, bool* counted) {
     w.ftc = FastDiv::make(uint32_t(a.t_count));
     const unsigned grid = unsigned((items + 3) / 4);
     TimedLaunch timed(PISA_KERNEL_ROUTER, stream);
+    const int max_width = std::max(a.first_width, a.K * a.br);
     if (a.row_levels == 0) {
-      route_warp_kernel<float, 0><<<grid, 128, 0, stream>>>(w);
+      // register slots per lane for the widest network of the descent
+      if (max_width <= 32) route_warp_kernel<float, 0, 1><<<grid, 128, 0, stream>>>(w);
+      else if (max_width <= 64) route_warp_kernel<float, 0, 2><<<grid, 128, 0, stream>>>(w);
+      else if (max_width <= 128) route_warp_kernel<float, 0, 4><<<grid, 128, 0, stream>>>(w);
+      else route_warp_kernel<float, 0, 8><<<grid, 128, 0, stream>>>(w);
     } else {
-      // row-scored levels: 16-bit inputs, head_dim a multiple of 16 up to 256
-      const int ks = (a.D + 15) / 16;
+      // row-scored levels (planned only for 16-bit inputs, G <= 16 and widths
+      // up to 64): pair-steps of 32 head dims
+      if (dtype == PISA_F32 || max_width > 64 || a.G > 16)
+        return fail(PISA_ERR_UNSUPPORTED, "row-scored levels need fp16/bf16, G <= 16 and widths up to 64");
+      const int kp = (a.D + 31) / 32;
       const bool bf = dtype == PISA_BF16;
-      if (dtype == PISA_F32) return fail(PISA_ERR_UNSUPPORTED, "row-scored levels need fp16 or bf16");
-      if (ks <= 4) {
-        if (bf) route_warp_kernel<__nv_bfloat16, 4><<<grid, 128, 0, stream>>>(w);
-        else route_warp_kernel<__half, 4><<<grid, 128, 0, stream>>>(w);
-      } else if (ks <= 8) {
-        if (bf) route_warp_kernel<__nv_bfloat16, 8><<<grid, 128, 0, stream>>>(w);
-        else route_warp_kernel<__half, 8><<<grid, 128, 0, stream>>>(w);
+      if (kp <= 2) {
+        if (bf) route_warp_kernel<__nv_bfloat16, 2, 2><<<grid, 128, 0, stream>>>(w);
+        else route_warp_kernel<__half, 2, 2><<<grid, 128, 0, stream>>>(w);
+      } else if (kp <= 4) {
+        if (bf) route_warp_kernel<__nv_bfloat16, 4, 2><<<grid, 128, 0, stream>>>(w);
+        else route_warp_kernel<__half, 4, 2><<<grid, 128, 0, stream>>>(w);
       } else {
-        if (bf) route_warp_kernel<__nv_bfloat16, 16><<<grid, 128, 0, stream>>>(w);
-        else route_warp_kernel<__half, 16><<<grid, 128, 0, stream>>>(w);
+        if (bf) route_warp_kernel<__nv_bfloat16, 8, 2><<<grid, 128, 0, stream>>>(w);
+        else route_warp_kernel<__half, 8, 2><<<grid, 128, 0, stream>>>(w);
       }
     }
     PISA_CHECK_LAUNCH();

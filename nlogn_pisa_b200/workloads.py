@@ -48,6 +48,10 @@ WORKLOADS = {
     # 16K is the smallest length at which the coarse level is scored densely and routed by warps
     "prefill8k": Workload("prefill8k", 1, 8192, 32, 8, 128, 64, 32, 4, True, 1, "pisa", "bf16"),
     "prefill16k": Workload("prefill16k", 1, 16384, 32, 8, 128, 64, 32, 4, True, 1, "pisa", "bf16"),
+    # a smaller case of the 256K configuration for profiler captures: three
+    # dense coarse levels as at 256K, 1024 leaves
+    "prefill64k": Workload("prefill64k", 1, 65536, 32, 8, 128, 64, 32, 4, True, 1, "pisa", "bf16",
+                           key_block_offset_std=0.5),
     # 256K causal prefill with informative block means
     "prefill256k": Workload("prefill256k", 1, 262144, 32, 8, 128, 64, 32, 4, True, 1, "pisa", "bf16",
                             key_block_offset_std=0.5),
