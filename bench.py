@@ -192,8 +192,39 @@ def decode_bench(args, device, world, peaks_hbm):
     per_head = summaries + br * K * C * D * 2 + 2 * K * C * D * 2
     step_bytes = Bd * H * per_head + 2 * Bd * Hq * D * 2
     achieved = step_bytes / (step_us * 1e-6) / 1e9
+
+    # the same step as one fused launch (pisa_decode_select_attend): selection
+    # and attention per (sequence, KV head) in one CTA
+    ids_f = torch.empty_like(ids)
+    out_f = torch.empty_like(out)
+
+    def fused_step():
+        _lib.check(lib.pisa_decode_select_attend(
+            _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3], _lib.ptr(v), *v.stride()[:3],
+            _lib.ptr(storage), storage.stride(0), _c_array(offsets), _c_array(sizes), len(sizes), None, N - 1,
+            code, Bd, 1, Hq, H, D, D, N, method, C, br, K, 1, 1, top, first_width, float(D ** -0.5),
+            _lib.ptr(ids_f), _lib.ptr(out_f), None, sptr))
+
+    for _ in range(max(args.warmup, 3)):
+        fused_step()
+    torch.cuda.synchronize()
+    launches0 = lib.pisa_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fused_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    fused_launches = (lib.pisa_launch_count() - launches0) / steps
+    fused_us = max_over_ranks([e0.elapsed_time(e1) / steps], device, world)[0] * 1000.0
+    same = (torch.sort(ids_f, -1).values == torch.sort(ids, -1).values).all(-1).float().mean().item()
+    fused_achieved = step_bytes / (fused_us * 1e-6) / 1e9
     del k, v, storage
     return {"workload": "decode128k", "batch": Bd, "kv_tokens": N, "q_heads": Hq, "kv_heads": H, "head_dim": D,
+            "fused_kernel": {"us_per_step": fused_us, "us_per_token": fused_us / Bd, "launches_per_step": fused_launches,
+                             "rows_with_same_ids_as_two_step_path": same,
+                             "roofline": {"bound": "hbm", "achieved": fused_achieved, "unit": "GB/s",
+                                          "peak": peaks_hbm, "frac": fused_achieved / peaks_hbm}},
             "block_size": C, "branching": br, "topk": K,
             "schedule": os.environ.get("PISA_BENCH_DECODE_SCHEDULE", "fused"),
             "us_per_step": step_us, "us_per_token": step_us / Bd, "steps": steps,

@@ -205,6 +205,31 @@ PISA_API int pisa_sparse_attn_fwd(const void *q, int64_t q_sb, int64_t q_st, int
                          float *lse, void *workspace, int64_t workspace_bytes,
                          pisa_stream_t stream);
 
+/*
+ * Fused single-token decode step: block selection and attention over the
+ * selected blocks in one launch (one CTA per (sequence, token, KV head)).
+ * Replaces the reference's decode pair select_blocks(routing_schedule=
+ * "fused") -> top_k_pyramid_triton.py:125-276 (leaf scoring fused into the
+ * router) followed by decode_attention (decode/decode_triton.py:8-115).
+ * Selection arguments as pisa_select_blocks (the pyramid `summary` with its
+ * level tables is required: the caller's PyramidCache); attention as
+ * pisa_sparse_attn_fwd with causal masking at each query's position.
+ * values: [B,N,H,Dv] (element strides); Dv in {64, 128, 256}; G <= 16 and
+ *   G*Dv <= 2048.
+ * out_ids [B,Tq,H,topk] int64 (network-rank order, -1 padded), out
+ * [B,Tq,Hq,Dv] in dtype, lse [B,Tq,Hq] fp32 or NULL.  No workspace.
+ */
+PISA_API int pisa_decode_select_attend(const void *q, int64_t q_sb, int64_t q_st, int64_t q_sh, const void *keys,
+                                       int64_t key_sb, int64_t key_st, int64_t key_sh, const void *values,
+                                       int64_t value_sb, int64_t value_st, int64_t value_sh, const void *summary,
+                                       int64_t summary_sb, const int64_t *level_offsets, const int64_t *level_sizes,
+                                       int64_t num_levels, const int64_t *positions, int64_t position_offset,
+                                       int dtype, int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D,
+                                       int64_t Dv, int64_t N, int method, int64_t block_size, int64_t branching,
+                                       int64_t topk, int force_first, int64_t force_recent, int64_t top,
+                                       int64_t first_width, float scale, int64_t *out_ids, void *out, float *lse,
+                                       pisa_stream_t stream);
+
 /* Workspace bytes of pisa_sparse_attn_fwd for these shapes (0: none needed). */
 PISA_API int64_t pisa_sparse_attn_fwd_workspace_bytes(int64_t B, int64_t Tq, int64_t Hq, int64_t H,
                                                       int64_t D, int64_t Dv, int64_t N, int64_t S,

@@ -38,6 +38,9 @@ SIGNATURES = {
                                 _P, _L, _P]),
     "pisa_select_workspace_bytes": (_L, [_L, _L, _L, _L, _L, _L, _I, _I, _L, _L, _L, _L, _L, _I, _I]),
     "pisa_select_level_plan": (_L, [_L, _L, _L, _L, _L, _L, _I, _I, _L, _L, _L, _L, _L, _I]),
+    "pisa_decode_select_attend": (_I, [_P, _L, _L, _L, _P, _L, _L, _L, _P, _L, _L, _L, _P, _L, _P, _P, _L, _P, _L,
+                                       _I, _L, _L, _L, _L, _L, _L, _L, _I, _L, _L, _L, _I, _L, _L, _L, _F,
+                                       _P, _P, _P, _P]),
     "pisa_sparse_attn_fwd": (_I, [_P, _L, _L, _L, _P, _L, _L, _L, _P, _L, _L, _L, _P, _I, _P, _L,
                                   _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _F, _I, _P, _P, _P, _L,
                                   _P]),

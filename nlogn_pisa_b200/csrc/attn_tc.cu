@@ -105,6 +105,15 @@ __device__ __forceinline__ void ld_shared16(uint32_t addr, uint32_t& x0, uint32_
   asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(x0), "=r"(x1), "=r"(x2), "=r"(x3) : "r"(addr)
                : "memory");
 }
+// CTA-scope release store / acquire load of a shared-memory counter
+__device__ __forceinline__ void st_release_cta(int* p, int v) {
+  asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" :: "r"(tc::smem_u32(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_cta(int* p) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(tc::smem_u32(p)) : "memory");
+  return v;
+}
 __device__ __forceinline__ void ld_cs32(const void* p, uint32_t (&w)[8]) {
   asm volatile("ld.global.cs.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]),
@@ -155,6 +164,11 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
   __shared__ uint64_t meta_full[kMeta];
   __shared__ int s_req[kMeta][128], s_nv[kMeta][128];
   __shared__ int s_fail;
+  // tiles whose P.V has completed, published by the readout (which waits for
+  // every one in order): the producer, which needs only some of them, reads
+  // this count instead of waiting on o_full, whose phase parity no longer
+  // names the phase it wants once the barrier is two phases behind
+  __shared__ int s_o_done;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int total = *a.total_tiles;
@@ -188,6 +202,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
     }
     for (int i = 0; i < kMeta; ++i) tc::mbar_init(&meta_full[i], kLoadWarps);
     s_fail = 0;
+    s_o_done = 0;
     tc::fence_barrier_init();
   }
   if (warp == 0) tc::tmem_alloc(&tmem_slot, a.tmem_cols);
@@ -284,7 +299,12 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
           // P.V of tile it-1 the one to wait for; it never needs tile it).
           if (kvb ? used1 : used0) {
             const int wt = nacc == 2 ? it - 2 : it - 1;
-            if (wt >= 0 && !tc::mbar_wait(&o_full[acc_of(wt)], round_of(wt) & 1)) { s_fail = 1; break; }
+            bool freed = wt < 0;
+            for (uint32_t i = 0; !freed && i < (1u << 24); ++i) {
+              freed = ld_acquire_cta(&s_o_done) > wt;
+              if (!freed && i >= 64) __nanosleep(32);
+            }
+            if (!freed) { s_fail = 1; break; }
           }
           if (kvb) used1 = 1; else used0 = 1;
           const uint32_t ks_addr = kv_addr + kvb * kv_bytes, vs_addr = ks_addr + qch * a.C * 128;
@@ -489,6 +509,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) attn_tc_kernel(const __grid_c
         const bool got = tc::mbar_wait(&o_full[ab], rnd & 1);
         if (!got) s_fail = 1;
         tc::fence_after_sync();
+        if (warp == 4 && lane == 0) st_release_cta(&s_o_done, it + 1);
         if (!tc::mbar_wait(&meta_full[it & (kMeta - 1)], (it >> 4) & 1)) s_fail = 1;
         const int req = r < a.RT ? s_req[it & (kMeta - 1)][r] : -1;
         const uint32_t obase = tmem + lane_base + nacc * a.sp_cols + ab * a.o_cols;

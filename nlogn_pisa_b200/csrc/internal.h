@@ -84,6 +84,15 @@ struct RouteArgs {
   // (row, family) request into fam_counts (bucket = (b, window, head, family))
   int32_t* fam_counts;
   int NP, nwin, TW;
+  // fused decode (per-item router only): after the leaf top-K the same CTA
+  // attends over the K selected blocks and writes out [B,T,Hq,Dv] and lse
+  int attend;
+  const void* values;
+  int64_t v_sb, v_st, v_sh;
+  int Dv;
+  float attn_scale;
+  void* out;
+  float* lse;
 };
 
 // Routes the rows of a.t_begin .. a.t_begin + a.t_count; `counted` (may be

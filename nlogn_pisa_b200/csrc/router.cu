@@ -54,15 +54,126 @@ __device__ __forceinline__ void network_step(float* sc, int* ids, int width, int
       const int v = id[e];
       if (level > 0) {
         for (int j = 0; j < br; ++j) next_ids[i * br + j] = v < 0 ? -1 : v * br + j;
-      } else if (out) {
-        out[i] = (v < 0 || int64_t(v) * C > pos) ? -1 : v;
+      } else {
+        // final ids (also kept in shared memory for a fused attention)
+        const int fin = (v < 0 || int64_t(v) * C > pos) ? -1 : v;
+        if (out) out[i] = fin;
+        next_ids[i] = fin;
       }
     }
   }
 }
 
-template <typename T, int GMAX>
-__global__ void __launch_bounds__(kThreads) route_kernel(const RouteArgs a) {
+// Fused decode: attention of the row's G query heads over its K selected
+// blocks (ids in shared memory, -1 = none) with the semantics of
+// sparse_attn_torch.py:6-35 (one softmax over the union of the blocks'
+// visible keys, causal at the row's position).  Warp w takes slots w, w+4,
+// ...; per chunk of 32 keys: logits with lane = key (q from shared memory),
+// online softmax per head, then P.V with lane = VPL value columns (the warp
+// reads each value row whole).  The four warps merge through shared memory.
+template <typename T, int GMAX, int VPL>
+__device__ void decode_attend(const RouteArgs& a, const int* sel, const float* qs, int b, int t, int h,
+                              int64_t pos, float* scratch) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int W = kThreads / 32;
+  const int G = a.G, Dv = a.Dv;
+  float* pw = scratch;                     // [W][G][32] probabilities of the current chunk
+  float* mw = pw + W * G * 32;             // [W][G]
+  float* lw = mw + W * G;                  // [W][G]
+  float* ow = lw + W * G;                  // [W][G][Dv]
+  const T* kbase = static_cast<const T*>(a.keys) + int64_t(b) * a.k_sb + int64_t(h) * a.k_sh;
+  const T* vbase = static_cast<const T*>(a.values) + int64_t(b) * a.v_sb + int64_t(h) * a.v_sh + lane * VPL;
+  float m[GMAX], l[GMAX], o[GMAX][VPL];
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+    m[g] = -INFINITY; l[g] = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) o[g][j] = 0.f;
+  }
+  for (int s = warp; s < a.K; s += W) {
+    const int id = sel[s];
+    if (id < 0) continue;
+    const int64_t k0 = int64_t(id) * a.C;
+    const int64_t k1 = min64(min64(k0 + a.C, int64_t(a.N)), pos + 1);
+    for (int64_t base = k0; base < k1; base += 32) {
+      const int nk = int(min64(32, k1 - base));
+      float z[GMAX];
+      if (lane < nk) {
+        row_dots<T, GMAX>(kbase + (base + lane) * a.k_st, qs, G, a.D, z);
+      }
+#pragma unroll
+      for (int g = 0; g < GMAX; ++g) {
+        if (g >= G) continue;
+        const float zv = lane < nk ? z[g] * a.attn_scale : -INFINITY;
+        const float mnew = fmaxf(m[g], warp_max(zv));
+        const float alpha = m[g] == -INFINITY ? 0.f : expf(m[g] - mnew);
+        const float pv = zv == -INFINITY ? 0.f : expf(zv - mnew);
+        l[g] = l[g] * alpha + warp_sum(pv);
+        m[g] = mnew;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) o[g][j] *= alpha;
+        pw[(warp * G + g) * 32 + lane] = pv;
+      }
+      __syncwarp();
+      // P.V: four value rows in flight, each read whole by the warp
+      for (int k0 = 0; k0 < nk; k0 += 4) {
+        float x[4][VPL];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (k0 + u < nk) {
+            const T* vr = vbase + (base + k0 + u) * a.v_st;
+#pragma unroll
+            for (int j = 0; j < VPL; ++j) x[u][j] = to_f32<T>(vr[j]);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (k0 + u >= nk) break;
+#pragma unroll
+          for (int g = 0; g < GMAX; ++g) {
+            if (g >= G) continue;
+            const float pv = pw[(warp * G + g) * 32 + k0 + u];
+#pragma unroll
+            for (int j = 0; j < VPL; ++j) o[g][j] = fmaf(pv, x[u][j], o[g][j]);
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+    if (g >= G) continue;
+    if (lane == 0) { mw[warp * G + g] = m[g]; lw[warp * G + g] = l[g]; }
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) ow[(warp * G + g) * Dv + lane * VPL + j] = o[g][j];
+  }
+  __syncthreads();
+  T* op = static_cast<T*>(a.out) + ((int64_t(b) * a.T + t) * (int64_t(a.H) * G) + int64_t(h) * G) * Dv;
+  for (int i = tid; i < G * Dv; i += kThreads) {
+    const int g = i / Dv, d = i - g * Dv;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < W; ++w) M = fmaxf(M, mw[w * G + g]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        const float mm = mw[w * G + g];
+        if (mm == -INFINITY) continue;
+        const float f = expf(mm - M);
+        L += lw[w * G + g] * f;
+        O += ow[(w * G + g) * Dv + d] * f;
+      }
+    }
+    op[i] = from_f32<T>(L > 0.f ? O / L : 0.f);
+    if (d == 0 && a.lse)
+      a.lse[(int64_t(b) * a.T + t) * (int64_t(a.H) * G) + int64_t(h) * G + g] = L > 0.f ? M + logf(L) : -INFINITY;
+  }
+}
+
+template <typename T, int GMAX, bool ATTEND>
+__global__ void __launch_bounds__(kThreads, ATTEND ? 4 : 1) route_kernel(const RouteArgs a) {
   extern __shared__ __align__(16) float smem[];
   float* qs = smem;                                    // [G][D]
   int* ids = reinterpret_cast<int*>(qs + a.G * a.D);   // [kMaxWidth]
@@ -183,6 +294,20 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const RouteArgs a) {
     width = a.K * a.br;
     span /= a.br;
     div /= a.br;
+  }
+  if constexpr (ATTEND) {
+    // the final ids are in ids[0 .. K); attention scratch after the router's
+    // arrays (the launcher admits G * Dv / 32 <= 64 accumulators per lane)
+    float* scratch = reinterpret_cast<float*>(fl + ((kMaxWidth + 15) / 16) * 16);
+    switch (a.Dv / 32) {
+      case 2: decode_attend<T, GMAX, 2>(a, ids, qs, b, t, h, pos, scratch); break;
+      case 4:
+        if constexpr (GMAX <= 16) decode_attend<T, GMAX, 4>(a, ids, qs, b, t, h, pos, scratch);
+        break;
+      default:
+        if constexpr (GMAX <= 8) decode_attend<T, GMAX, 8>(a, ids, qs, b, t, h, pos, scratch);
+        break;
+    }
   }
 }
 
@@ -558,8 +683,14 @@ __global__ void __launch_bounds__(128, (KP > 0 && KP <= 4) ? 6 : 1) route_warp_k
 
 template <typename T, int GMAX>
 int launch_route(const RouteArgs& a, cudaStream_t stream) {
-  const size_t smem = size_t(a.G) * a.D * sizeof(float) + kMaxWidth * (2 * sizeof(int) + 1);
-  auto kernel = route_kernel<T, GMAX>;
+  size_t smem = size_t(a.G) * a.D * sizeof(float) + kMaxWidth * (2 * sizeof(int) + 1);
+  if (a.attend) {
+    // fused decode attention: probabilities, per-warp (m, l) and partial outputs
+    const int W = kThreads / 32;
+    smem = size_t(a.G) * a.D * sizeof(float) + kMaxWidth * 2 * sizeof(int) + (kMaxWidth + 15) / 16 * 16 +
+           sizeof(float) * (size_t(W) * a.G * 32 + 2 * W * a.G + size_t(W) * a.G * a.Dv);
+  }
+  auto kernel = a.attend ? route_kernel<T, GMAX, true> : route_kernel<T, GMAX, false>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return fail_cuda(e, "route smem attribute");
@@ -574,6 +705,8 @@ int launch_route(const RouteArgs& a, cudaStream_t stream) {
 
 template <typename T>
 int route_t(const RouteArgs& a, cudaStream_t stream) {
+  if (a.attend && (a.G > 16 || a.G * (a.Dv / 32) > 64))
+    return fail(PISA_ERR_UNSUPPORTED, "fused decode needs G <= 16 and G * value head_dim <= 2048");
   if (a.G <= 1) return launch_route<T, 1>(a, stream);
   if (a.G <= 2) return launch_route<T, 2>(a, stream);
   if (a.G <= 4) return launch_route<T, 4>(a, stream);
@@ -597,6 +730,7 @@ int route(const RouteArgs& a, int dtype, cudaStream_t stream, bool* counted) {
       if (a.method == PISA_METHOD_PISA1 || a.levels.size[l] > a.K) warp_ok = false;
     }
   }
+  if (a.attend) warp_ok = false;   // the fused decode attention lives in the per-item router
   const int64_t items = int64_t(a.B) * a.t_count * a.H;
   if (warp_ok && items < (int64_t(1) << 31)) {
     if (items == 0) return PISA_OK;

@@ -8,26 +8,47 @@
 
 namespace pisa {
 
+// acc[g] = row . q_g for the G query rows of `qs` ([G][D] fp32 in shared
+// memory, read as broadcasts).  The row's 16-byte vectors are fetched eight
+// at a time before any arithmetic, so a row costs one or two memory round
+// trips instead of one per vector.
 template <typename T, int GMAX>
 __device__ __forceinline__ void row_dots(const T* __restrict__ row, const float* __restrict__ qs,
                                          int G, int D, float (&acc)[GMAX]) {
   constexpr int V = Vec<T>::N;
+  constexpr int NB = 8;                      // vectors in flight
 #pragma unroll
   for (int g = 0; g < GMAX; ++g) acc[g] = 0.f;
-  for (int d = 0; d < D; d += V) {
-    float x[V];
-    load_vec<T>(row + d, x);
+  for (int d0 = 0; d0 < D; d0 += NB * V) {
+    uint4 raw[NB];
 #pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-      if (g < G) {
-        const float* qg = qs + g * D + d;
+    for (int u = 0; u < NB; ++u)
+      raw[u] = d0 + u * V < D ? __ldg(reinterpret_cast<const uint4*>(row + d0 + u * V)) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-        for (int i = 0; i < V; i += 4) {
-          const float4 qv = *reinterpret_cast<const float4*>(qg + i);
-          acc[g] = fmaf(qv.x, x[i + 0], acc[g]);
-          acc[g] = fmaf(qv.y, x[i + 1], acc[g]);
-          acc[g] = fmaf(qv.z, x[i + 2], acc[g]);
-          acc[g] = fmaf(qv.w, x[i + 3], acc[g]);
+    for (int u = 0; u < NB; ++u) {
+      if (d0 + u * V >= D) break;
+      float x[V];
+      if constexpr (sizeof(T) == 4) {
+        x[0] = __uint_as_float(raw[u].x); x[1] = __uint_as_float(raw[u].y);
+        x[2] = __uint_as_float(raw[u].z); x[3] = __uint_as_float(raw[u].w);
+      } else {
+        const T* e = reinterpret_cast<const T*>(&raw[u]);
+#pragma unroll
+        for (int i = 0; i < V; ++i) x[i] = to_f32<T>(e[i]);
+      }
+      const int d = d0 + u * V;
+#pragma unroll
+      for (int g = 0; g < GMAX; ++g) {
+        if (g < G) {
+          const float* qg = qs + g * D + d;
+#pragma unroll
+          for (int i = 0; i < V; i += 4) {
+            const float4 qv = *reinterpret_cast<const float4*>(qg + i);
+            acc[g] = fmaf(qv.x, x[i + 0], acc[g]);
+            acc[g] = fmaf(qv.y, x[i + 1], acc[g]);
+            acc[g] = fmaf(qv.z, x[i + 2], acc[g]);
+            acc[g] = fmaf(qv.w, x[i + 3], acc[g]);
+          }
         }
       }
     }

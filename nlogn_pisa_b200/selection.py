@@ -299,3 +299,54 @@ def grouped_leaf_scores(q, k, candidates, block_size, method, tile_size=4, *, po
 
 
 top_k_pyramid_fn = select_blocks
+
+
+@torch.no_grad()
+def decode_select_attend(q, k, v, pyramid, method="pisa", block_size=64, topk=8, query_offset=None,
+                         force_first=True, force_recent=2, scale=None, branching=2, return_lse=False):
+    """One decode step in one launch: the block selection of
+    ``select_blocks(..., routing_schedule="fused", pyramid=pyramid)`` and the
+    attention of ``sparse_attention`` over those blocks (causal at each
+    query's position), fused per (token, KV head).
+
+    Returns ``(out [B,Tq,Hq,Dv], ids [B,Tq,Hkv,K])`` (and the fp32 lse when
+    ``return_lse``).  ``pyramid`` is the cache's pyramid (a PyramidCache-like
+    object or a list of levels) of ``k``.  Inference only, like the
+    reference's decode attention (sparse_attn_fla.py:34-37).
+    """
+    validate_qkv(q, k)
+    require_cuda(q, k, v)
+    if method not in ("pisa1", "pisa2", "pisa"):
+        raise ValueError("method must be pisa1, pisa2 or pisa")
+    if block_size < 1 or topk < 1 or force_recent < 1:
+        raise ValueError("positive block_size/topk and force_recent >= 1 required")
+    if branching not in (2, 4):
+        raise ValueError("branching must be 2 or 4")
+    if topk & (topk - 1) or block_size & (block_size - 1) or not 8 <= topk <= 64 or block_size < 16:
+        raise ValueError("GPU routing requires power-of-two block_size >= 16 and topk in {8,16,32,64}")
+    if v.shape[:3] != k.shape[:3] or v.dtype != k.dtype or v.device != k.device:
+        raise ValueError("values must be [B, N, Hkv, Dv] like the keys")
+    if pyramid is None:
+        raise ValueError("the fused decode step needs the key pyramid (a PyramidCache)")
+    code = _lib.dtype_code(q)
+    blocks = -(-k.shape[1] // block_size)
+    if topk < min(blocks, force_recent + int(force_first)):
+        raise ValueError("topk cannot hold all required blocks")
+    positions, offset = query_positions(q, k, query_offset)
+    top, first_width = routing_geometry(blocks, topk, branching)
+    q, k, v = _rows16(q), _rows16(k), _rows16(v)
+    batch, tokens, q_heads, dim = q.shape
+    heads, length, dim_v = k.shape[2], k.shape[1], v.shape[-1]
+    summary, summary_sb, offsets, sizes = _pyramid_tables(pyramid, k, block_size, top, branching)
+    scale = dim ** -0.5 if scale is None else float(scale)
+    ids = torch.empty((batch, tokens, heads, topk), dtype=torch.int64, device=q.device)
+    out = torch.empty((batch, tokens, q_heads, dim_v), dtype=q.dtype, device=q.device)
+    lse = torch.empty((batch, tokens, q_heads), dtype=torch.float32, device=q.device)
+    with torch.cuda.device(q.device):
+        _lib.check(_lib.lib().pisa_decode_select_attend(
+            _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3], _lib.ptr(v), *v.stride()[:3],
+            _lib.ptr(summary), summary_sb, _c_array(offsets), _c_array(sizes), len(sizes),
+            _lib.ptr(positions), offset, code, batch, tokens, q_heads, heads, dim, dim_v, length,
+            _lib.METHODS[method], block_size, branching, topk, int(bool(force_first)), force_recent, top,
+            first_width, scale, _lib.ptr(ids), _lib.ptr(out), _lib.ptr(lse), _lib.stream_of(q.device)))
+    return (out, ids, lse) if return_lse else (out, ids)

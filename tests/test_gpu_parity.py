@@ -308,3 +308,38 @@ def test_batched_decode_step_matches_oracle(cuda_device):
     _check_ids(ids, want, trace)
     ref, _ = O.sparse_attention(qn, kn, vn, ids, C, positions=pos)
     np.testing.assert_allclose(out, ref, atol=2e-2, rtol=0)
+
+
+def test_tensor_core_attention_many_tiles_per_cta_poisoned_workspace(cuda_device):
+    """Enough tiles that every CTA of the persistent tile kernel runs two tile
+    groups (K/V buffers replaced mid-pipeline), on a workspace filled with NaN
+    bytes so that a partial read before it is written cannot go unnoticed."""
+    from nlogn_pisa_b200 import _lib
+
+    B, T, N, Hq, H, D, C, S = 1, 2000, 2000, 16, 16, 64, 64, 16
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn(B, T, Hq, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, N, H, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, N, H, D, generator=g).to(torch.bfloat16)
+    blocks = -(-N // C)
+    ids = torch.randint(-1, blocks + 1, (B, T, H, S), generator=g)
+    ids[..., 1] = ids[..., 0]
+    lib = _lib.lib()
+    code = _lib.BF16
+    wsb = lib.pisa_sparse_attn_fwd_workspace_bytes(B, T, Hq, H, D, D, N, S, C, code)
+    assert wsb > 0
+    qc, kc, vc, ic = (x.to(cuda_device) for x in (q, k, v, ids))
+    for _ in range(2):
+        ws = torch.full((wsb,), 0xFF, dtype=torch.uint8, device=cuda_device)
+        out = torch.empty((B, T, Hq, D), dtype=torch.bfloat16, device=cuda_device)
+        lse = torch.empty((B, T, Hq), dtype=torch.float32, device=cuda_device)
+        _lib.check(lib.pisa_sparse_attn_fwd(
+            _lib.ptr(qc), *qc.stride()[:3], _lib.ptr(kc), *kc.stride()[:3], _lib.ptr(vc), *vc.stride()[:3],
+            _lib.ptr(ic), 8, None, 0, code, B, T, Hq, H, D, D, N, S, C, float(D ** -0.5), 0, _lib.ptr(out),
+            _lib.ptr(lse), _lib.ptr(ws), wsb, _lib.stream_of(cuda_device)))
+        _lib.check_workspace(ws, cuda_device)
+        pos = O.query_positions(B, T, N, None)
+        want, want_lse = O.sparse_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), ids.numpy(), C,
+                                            positions=pos, causal=False)
+        np.testing.assert_allclose(out.float().cpu().numpy(), want, rtol=0, atol=2e-2)
+        np.testing.assert_allclose(lse.cpu().numpy(), want_lse, rtol=0, atol=1e-3)
