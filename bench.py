@@ -755,6 +755,38 @@ def _device_ms(fn, steps, warmup, flush):
     return statistics.median(times)
 
 
+def bsa_bench(device, steps=5):
+    """Selection time of the flat BSA comparator (bsa_fn, the reference's
+    baseline routing, bsa_torch.py:63-106) beside PISA routing on the same
+    32K prefill inputs and GPU: the reference README's PISA-over-BSA ratio,
+    measured on this library's own kernels."""
+    import torch
+
+    import nlogn_pisa_b200 as P
+    from nlogn_pisa_b200.workloads import WORKLOADS, make_inputs
+
+    w = WORKLOADS["prefill32k"]
+    q, k, _ = make_inputs(w, device, seed=w.seed)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    opts = dict(block_size=w.block_size, topk=w.topk, force_first=True, force_recent=1)
+    bsa_ms = _device_ms(lambda: P.bsa_fn(q, k, **opts), steps, 3, flush)
+    pisa_ms = {f"b{br}": _device_ms(lambda: P.select_blocks(q, k, method="pisa", branching=br, **opts),
+                                    steps, 3, flush) for br in (2, 4)}
+    blocks = -(-w.tokens // w.block_size)
+    # two passes of q . mean over the visible blocks of every (token, query head)
+    flops = 2 * 2 * w.head_dim * w.q_heads * w.batch * sum(min(blocks, (t // w.block_size) + 1)
+                                                            for t in range(w.tokens))
+    out = {"workload": w.name, "tokens": w.tokens, "topk": w.topk, "block_size": w.block_size,
+           "bsa_select_ms": bsa_ms, "pisa_select_ms": pisa_ms,
+           "bsa_over_pisa_b2": bsa_ms / pisa_ms["b2"], "bsa_over_pisa_b4": bsa_ms / pisa_ms["b4"],
+           "bsa_score_tflops": flops / 1e12 / (bsa_ms / 1000.0),
+           "timing": f"median of {steps} CUDA-event samples, 256 MiB L2 flush before each; each call "
+                     "includes its own leaf-mean or pyramid build"}
+    del q, k, flush
+    torch.cuda.empty_cache()
+    return out
+
+
 def triton_comparator(args):
     """Selection time (fresh pyramid + prefill routing) of the reference's own
     Triton path, select_blocks(..., backend="triton", routing_schedule=
@@ -806,11 +838,28 @@ def triton_comparator(args):
         except Exception as exc:
             row["triton_error"] = f"{type(exc).__name__}: {str(exc)[:200]}"
         if name == "selection_bench":
+            row["bsa_ours_ms"] = _device_ms(lambda: P.bsa_fn(q, k, block_size=64, topk=topk, force_recent=recent),
+                                            args.steps, max(args.warmup, 3), flush)
             try:
                 row["bsa_triton_ms"] = _device_ms(lambda: bsa_fn(q, k, block_size=64, topk=topk, backend="triton"),
                                                   args.steps, max(args.warmup, 3), flush)
             except Exception as exc:
                 row["bsa_error"] = f"{type(exc).__name__}: {str(exc)[:200]}"
+                # the FLA prefill route of bsa_fn needs another fla-core release than the
+                # box's; the reference's own Triton BSA kernel (bsa_triton.py:86-114) is
+                # its general GPU path
+                try:
+                    from pisa.ops.flash_sparse_attn.bsa.bsa_triton import select_bsa
+
+                    pos = torch.arange(n, device=device).expand(1, n).contiguous()
+                    row["bsa_triton_ms"] = _device_ms(lambda: select_bsa(q, k, 64, topk, pos, True, recent),
+                                                      args.steps, max(args.warmup, 3), flush)
+                    row["bsa_triton_path"] = "bsa_triton.select_bsa"
+                    got = P.bsa_fn(q, k, block_size=64, topk=topk, force_recent=recent).sort(-1).values
+                    want = select_bsa(q, k, 64, topk, pos, True, recent).sort(-1).values
+                    row["bsa_rows_equal"] = float((got == want).all(-1).float().mean())
+                except Exception as exc2:
+                    row["bsa_error2"] = f"{type(exc2).__name__}: {str(exc2)[:200]}"
         rows.append(row)
         del q, k
         torch.cuda.empty_cache()
@@ -875,6 +924,7 @@ def main():
             mx["tensors"] = None
             extra[name] = compact_line(WORKLOADS[name], mx, hbm, tensor)
             torch.cuda.empty_cache()
+    bsa = None if (args.no_extra or world > 1) else bsa_bench(device)
     long_ctx = None if args.no_extra else long_context_bench(device, world, rank, hbm, tensor)
     training = None if args.no_extra else training_bench(device, world, rank, tensor)
     torch.cuda.empty_cache()
@@ -915,6 +965,7 @@ def main():
             "select_attend_tensor_frac": (m["work"]["leaf_flops"] + m["work"]["attn_flops"])
             / 1e12 / (m["step_ms"] / 1000.0) / tensor,
             "workloads": extra,
+            "bsa": bsa,
             "long_context": long_ctx,
             "training": training,
             "decode": decode,

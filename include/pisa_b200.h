@@ -181,6 +181,39 @@ PISA_API int64_t pisa_leaf_scores_workspace_bytes(int64_t B, int64_t Tq, int64_t
                                                   int64_t block_size, int have_means);
 
 /*
+ * Flat BSA block selection, the reference's comparator for PISA routing.
+ * Replaces bsa_fn / bsa_select (pisa/pisa/ops/flash_sparse_attn/bsa/bsa.py:9-52,
+ * bsa_torch.py:63-106; GPU form bsa_triton.py:12-114), which select_blocks
+ * reaches with method="bsa" (top_k_pyramid.py:60-63).  Per (query token, KV
+ * head): each query head, scaled by D^-0.5 and rounded to `dtype`, scores
+ * the leaf means of the complete blocks; blocks before the current one get
+ * exp(logit - LSE of the complete blocks' logits), required blocks (block 0
+ * with force_first, the force_recent most recent) get 1; the values are
+ * summed over the G query heads and the best `topk` are kept by the
+ * reference's streaming comparison network (tiles of pow2(max(block_size,
+ * 2*topk)) blocks, bsa_torch.py:9-60), ids past the current block being -1.
+ * out_ids: [B,Tq,H,topk] int64 in network-rank order.
+ * leaf_means: [B, ceil(N/block_size), H, D] (node stride H*D, batch stride
+ *   means_sb), or NULL to pool them from `keys` inside `workspace`
+ *   (pisa_bsa_workspace_bytes(..., have_means=0) bytes).
+ * positions: device int64 [B,Tq], or NULL for position_offset + token.  With
+ *   `positions` the caller checks that topk holds every row's required blocks
+ *   (the Python mirror does); without, the entry point checks it.
+ * Constraints: G <= 16, D % 8 == 0 (fp32: D % 4) and D <= 256,
+ *   max(block_size, 2*topk) <= 256.
+ */
+PISA_API int pisa_bsa_select(const void *q, int64_t q_sb, int64_t q_st, int64_t q_sh, const void *keys,
+                             int64_t key_sb, int64_t key_st, int64_t key_sh, const void *leaf_means,
+                             int64_t means_sb, const int64_t *positions, int64_t position_offset, int dtype,
+                             int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t D, int64_t N,
+                             int64_t block_size, int64_t topk, int force_first, int64_t force_recent,
+                             int64_t *out_ids, void *workspace, int64_t workspace_bytes, pisa_stream_t stream);
+
+/* Workspace bytes of pisa_bsa_select (0 when leaf means are passed; -1 on bad shapes). */
+PISA_API int64_t pisa_bsa_workspace_bytes(int64_t B, int64_t N, int64_t H, int64_t D, int dtype,
+                                          int64_t block_size, int have_means);
+
+/*
  * Attention over selected key blocks with one softmax over their union
  * (causal inside blocks), forward.  Replaces sparse_attention's CUDA branch
  * (pisa/pisa/ops/flash_sparse_attn/sparse_attn/sparse_attn.py:10-61 ->
@@ -341,7 +374,8 @@ PISA_API int pisa_ex2_selftest(const float *x, float *poly, float *mufu, int64_t
 #define PISA_KERNEL_DENSE_LEVEL 4   /* tensor-core scoring of whole coarse levels */
 #define PISA_KERNEL_ROUTER 5        /* coarse-to-fine router (warp-per-row or per-item form) */
 #define PISA_KERNEL_LEAF_FINAL 6    /* final top-K over the leaf candidates */
-#define PISA_KERNEL_COUNT 7
+#define PISA_KERNEL_BSA 7           /* flat BSA selection (pisa_bsa_select) */
+#define PISA_KERNEL_COUNT 8
 
 /* Kernels this library has launched in this process so far. */
 PISA_API int64_t pisa_launch_count(void);

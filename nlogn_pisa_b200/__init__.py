@@ -12,13 +12,13 @@ TensorCache).  All computation runs in the hand-written CUDA library
 from .attention import sparse_attention, sparse_attn_fn
 from .cache import PyramidCache, TensorCache
 from ._lib import set_status_checks
-from .selection import (build_pyramid, decode_select_attend, grouped_leaf_scores, mean_pool, routing_geometry,
-                        select_blocks, top_k_pyramid_fn)
+from .selection import (bsa_fn, build_pyramid, decode_select_attend, grouped_leaf_scores, mean_pool,
+                        routing_geometry, select_blocks, top_k_pyramid_fn)
 
 mean_pooling_fn = mean_pool
 
 __all__ = [
     "select_blocks", "top_k_pyramid_fn", "sparse_attention", "sparse_attn_fn", "mean_pool",
     "mean_pooling_fn", "build_pyramid", "routing_geometry", "PyramidCache", "TensorCache",
-    "grouped_leaf_scores", "set_status_checks", "decode_select_attend",
+    "grouped_leaf_scores", "set_status_checks", "decode_select_attend", "bsa_fn",
 ]

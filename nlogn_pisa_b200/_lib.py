@@ -55,6 +55,9 @@ SIGNATURES = {
     "pisa_leaf_scores": (_I, [_P, _L, _L, _L, _P, _L, _L, _L, _P, _L, _P, _I, _P, _I, _L, _L, _L, _L,
                               _L, _L, _L, _I, _L, _L, _I, _L, _P, _P, _L, _P]),
     "pisa_leaf_scores_workspace_bytes": (_L, [_L, _L, _L, _L, _L, _L, _L, _I, _I, _L, _I]),
+    "pisa_bsa_select": (_I, [_P, _L, _L, _L, _P, _L, _L, _L, _P, _L, _P, _L, _I, _L, _L, _L, _L, _L, _L, _L,
+                             _L, _I, _L, _P, _P, _L, _P]),
+    "pisa_bsa_workspace_bytes": (_L, [_L, _L, _L, _L, _I, _L, _I]),
     "pisa_rotary": (_I, [_P, _L, _L, _L, _P, _L, _L, _L, _P, _L, _L, _P, _I, _L, _L, _L, _L, _P]),
     "pisa_workspace_status": (_I, [_P, _P]),
     "pisa_wait_selftest": (_I, [_I, _L, _P, _L, _P]),
@@ -140,7 +143,7 @@ def dtype_code(t):
 
 
 KERNELS = {"leaf_tiles": 0, "attn_tiles": 1, "attn_combine": 2, "pyramid": 3, "dense_level": 4, "router": 5,
-           "leaf_final": 6}
+           "leaf_final": 6, "bsa": 7}
 
 
 def kernel_timing(enable):

@@ -43,9 +43,15 @@ def build(force=False, verbose=False, jobs=None, out=None, defines=()):
     objdir.mkdir(parents=True, exist_ok=True)
     procs = []
     objs = []
+    headers = list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
+    newest_header = max((p.stat().st_mtime for p in headers), default=0.0)
     for src in sources():
         obj = objdir / (src.stem + ".o")
         objs.append(obj)
+        # an object is reused when it is newer than its source and every header
+        if (not force and out is None and obj.exists()
+                and obj.stat().st_mtime > max(src.stat().st_mtime, newest_header)):
+            continue
         cmd = [nvcc, *ARCH, *FLAGS, *(f"-D{d}" for d in defines), "-I", str(INCLUDE), "-I", str(CSRC), "-c",
                str(src), "-o", str(obj)]
         if verbose:

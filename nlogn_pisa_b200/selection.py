@@ -5,6 +5,7 @@ Aphelios-Tang/NlogN_PISA project):
   select_blocks / top_k_pyramid_fn -> pisa/pisa/ops/flash_sparse_attn/top_k_pyramid/top_k_pyramid.py:11-122
   routing_geometry                 -> top_k_pyramid_torch.py:124-133
   mean_pool / build_pyramid        -> pisa/pisa/ops/compress/mean_pooling/mean_pooling.py:8-52
+  bsa_fn (select_blocks "bsa")     -> pisa/pisa/ops/flash_sparse_attn/bsa/bsa.py:9-52, bsa_torch.py:63-106
 Same argument names, defaults and ValueError contract; every computation runs
 in libpisa_b200 (no Triton, no CPU fallback).  ``branching`` (default 2, the
 reference's only value) additionally allows a 4-ary pyramid.
@@ -128,7 +129,8 @@ def select_blocks(q, k, method="pisa", block_size=64, topk=8, cu_seqlens=None, q
     if method != "bsa" and force_recent == 0:
         raise ValueError("causal pyramid routing requires force_recent >= 1")
     if method == "bsa":
-        raise ValueError("the flat BSA baseline selection is not part of nlogn_pisa_b200")
+        return bsa_fn(q, k, block_size, topk, cu_seqlens=cu_seqlens, query_offset=query_offset,
+                      force_first=force_first, force_recent=force_recent, backend=backend)
     if branching not in (2, 4):
         raise ValueError("branching must be 2 or 4")
     if routing_schedule == "auto":
@@ -299,6 +301,59 @@ def grouped_leaf_scores(q, k, candidates, block_size, method, tile_size=4, *, po
 
 
 top_k_pyramid_fn = select_blocks
+
+
+@torch.no_grad()
+def bsa_fn(q, k, block_size=64, topk=8, *, cu_seqlens=None, query_offset=None, force_first=True,
+           force_recent=2, backend="auto"):
+    """Flat BSA block ids [B,Tq,Hkv,K] int64 in network-rank order, -1 padded.
+
+    Arguments as the reference's bsa_fn.  Every complete block is scored by
+    the softmax probability of its leaf mean under each query head, summed
+    over the KV head's query heads; required blocks (first, and the
+    ``force_recent`` most recent) score 1 per head.  Results follow the
+    reference's torch semantics (bsa_torch.py:63-106) on the CUDA library for
+    every backend name; packed documents are selected one by one with
+    document-relative ids.
+    """
+    validate_qkv(q, k)
+    if backend not in ("torch", "triton", "auto", "cuda"):
+        raise ValueError("backend must be torch, triton or auto")
+    if block_size < 1 or topk < 1 or force_recent < 0:
+        raise ValueError("positive block_size/topk and nonnegative force_recent required")
+    if cu_seqlens is not None:
+        segments = list(packed_queries(q, k, cu_seqlens, query_offset))
+        return torch.cat([_bsa_unpacked(q[:, qs:qe], k[:, ks:ke], block_size, topk, offset, force_first,
+                                        force_recent) for qs, qe, ks, ke, offset in segments], dim=1)
+    return _bsa_unpacked(q, k, block_size, topk, query_offset, force_first, force_recent)
+
+
+def bsa_required_blocks(last_position, block_size, force_first, force_recent):
+    """Distinct required blocks of the row at ``last_position`` (the most of any row)."""
+    current = last_position // block_size
+    return min(force_recent, current + 1) + int(bool(force_first) and current >= force_recent)
+
+
+def _bsa_unpacked(q, k, block_size, topk, query_offset, force_first, force_recent):
+    require_cuda(q, k)
+    code = _lib.dtype_code(q)
+    positions, offset = query_positions(q, k, query_offset)
+    last = offset + q.shape[1] - 1 if positions is None else int(positions.max())
+    if bsa_required_blocks(last, block_size, force_first, force_recent) > topk:
+        raise ValueError("topk is smaller than the number of required distinct blocks")
+    q, k = _rows16(q), _rows16(k)
+    batch, tokens, q_heads, dim = q.shape
+    heads, length = k.shape[2], k.shape[1]
+    library = _lib.lib()
+    ws_bytes = library.pisa_bsa_workspace_bytes(batch, length, heads, dim, code, block_size, 0)
+    workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+    out = torch.empty((batch, tokens, heads, topk), dtype=torch.int64, device=q.device)
+    with torch.cuda.device(q.device):
+        _lib.check(library.pisa_bsa_select(
+            _lib.ptr(q), *q.stride()[:3], _lib.ptr(k), *k.stride()[:3], None, 0, _lib.ptr(positions), offset,
+            code, batch, tokens, q_heads, heads, dim, length, block_size, topk, int(bool(force_first)),
+            int(force_recent), _lib.ptr(out), _lib.ptr(workspace), ws_bytes, _lib.stream_of(q.device)))
+    return out
 
 
 @torch.no_grad()

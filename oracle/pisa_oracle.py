@@ -16,6 +16,7 @@ Every function restates the reference algorithm of Aphelios-Tang/NlogN_PISA
 * bitonic top-K network   -> top_k_pyramid_torch.py:84-110
 * coarse-to-fine descent  -> top_k_pyramid_torch.py:137-177
 * query positions         -> pisa/pisa/utils/validation.py:38-56
+* flat BSA routing        -> pisa/pisa/ops/flash_sparse_attn/bsa/bsa_torch.py:9-106
 * selected attention      -> pisa/pisa/ops/flash_sparse_attn/sparse_attn/sparse_attn_torch.py:6-35
   (the log-sum-exp output and the analytic gradient are restated from the
   same masked softmax; the reference obtains gradients through autograd)
@@ -381,6 +382,135 @@ def select_blocks(q, k, method="pisa", block_size=64, topk=8, query_offset=None,
     levels = build_pyramid(k, block_size, dtype, branching=branching)
     return pyramid_select(q, k, method, block_size, topk, positions, force_first,
                           force_recent, levels, branching=branching, trace=trace)
+
+
+# ----------------------------------------------------------------------------
+# flat BSA routing (pisa/pisa/ops/flash_sparse_attn/bsa/bsa_torch.py)
+# ----------------------------------------------------------------------------
+
+def _merge(scores, ids, stage, descending):
+    """One bitonic merge of runs of 2**stage through XOR partners (bsa_torch.py:9-27).
+
+    ``descending=None`` makes run r descend when bit ``stage`` of its lanes is
+    set; otherwise every run goes the given way.  A pair exchanges when
+    (lower score > upper score) differs from the run's direction, so equal
+    scores exchange in descending runs and stay in ascending ones.
+    """
+    lane = np.arange(scores.shape[-1])
+    direction = (lane & (1 << stage)) != 0 if descending is None else np.full(lane.shape, descending)
+    for exponent in range(stage - 1, -1, -1):
+        distance = 1 << exponent
+        partner = lane ^ distance
+        lower = lane & ~distance
+        upper = lower | distance
+        exchange = (scores[..., lower] > scores[..., upper]) != direction
+        scores = np.where(exchange, scores[..., partner], scores)
+        ids = np.where(exchange, ids[..., partner], ids)
+    return scores, ids
+
+
+def streaming_topk(scores, ids, topk, tile_size):
+    """Best ``topk`` ids by tiles of ``tile_size`` (bsa_torch.py:30-60).
+
+    Each tile is sorted into alternating runs, merged ascending against the
+    retained best half of the earlier tiles, then merged descending; tiles
+    without a valid id leave the retained list alone.  Ids come out in
+    network-rank order.
+    """
+    if topk < 1 or tile_size < 2 * topk or tile_size & (tile_size - 1):
+        raise ValueError("tile_size must be a power of two and at least 2 * topk")
+    stages = tile_size.bit_length() - 1
+    half = tile_size // 2
+    retained_scores = np.full(scores.shape[:-1] + (tile_size,), -1, scores.dtype)
+    retained_ids = np.zeros(ids.shape[:-1] + (tile_size,), ids.dtype)
+    for start in range(0, scores.shape[-1], tile_size):
+        values = scores[..., start:start + tile_size]
+        indices = ids[..., start:start + tile_size]
+        active = (indices >= 0).any(-1, keepdims=True)
+        pad = tile_size - values.shape[-1]
+        if pad:
+            values = np.concatenate([values, np.zeros(values.shape[:-1] + (pad,), values.dtype)], -1)
+            indices = np.concatenate([indices, np.full(indices.shape[:-1] + (pad,), -1, indices.dtype)], -1)
+        for stage in range(1, stages):
+            values, indices = _merge(values, indices, stage, None)
+        if start:
+            values, indices = _merge(values, indices, stages, False)
+            values = np.concatenate([retained_scores[..., :half], values[..., half:]], -1)
+            indices = np.concatenate([retained_ids[..., :half], indices[..., half:]], -1)
+        values, indices = _merge(values, indices, stages, True)
+        retained_scores = np.where(active, values, retained_scores)
+        retained_ids = np.where(active, indices, retained_ids)
+    return retained_ids[..., :topk]
+
+
+def bsa_required(positions, block_size, force_first, force_recent):
+    """Largest number of distinct required blocks over the rows (bsa_torch.py:88-95)."""
+    current = np.asarray(positions) // block_size
+    recent = np.minimum(force_recent, current + 1)
+    return int((recent + ((current >= force_recent) & bool(force_first))).max())
+
+
+def bsa_select(q, k, block_size, topk, positions, force_first=True, force_recent=2, dtype="f32",
+               chunk=128, trace=None):
+    """Flat block routing by summed per-head probabilities (bsa_torch.py:63-106).
+
+    Summaries are the leaf means.  Each query head's logits against the
+    complete blocks (``(pos + 1) // C`` of them) give a log-sum-exp
+    normaliser; blocks strictly before the current one score
+    exp(logit - normaliser), required blocks (first, and the ``force_recent``
+    most recent) score 1, and the per-head values are summed over the G heads
+    of the KV head.  Ids past the current block are -1.  The query is scaled
+    by D**-0.5 in the accumulation type and rounded to its own dtype first.
+    Returns int64 ids [B, T, H, topk] in network-rank order.  ``trace`` gets
+    ``min_gap``: the relative gap between the K-th and (K+1)-th score per row.
+    """
+    if bsa_required(positions, block_size, force_first, force_recent) > topk:
+        raise ValueError("topk is smaller than the number of required distinct blocks")
+    summaries = mean_pool(k, block_size, dtype)
+    acc = acc_type(dtype)
+    batch, length, q_heads, dim = q.shape
+    heads = k.shape[2]
+    groups = q_heads // heads
+    width = 1 << (max(block_size, 2 * topk) - 1).bit_length()
+    count = summaries.shape[1]
+    blocks = np.arange(count)
+    scale = acc(dim ** -0.5)
+    out = np.empty((batch, length, heads, topk), np.int64)
+    gaps = np.empty((batch, length, heads))
+    for start in range(0, length, chunk):
+        stop = min(start + chunk, length)
+        query = cast(q[:, start:stop].astype(acc) * scale, dtype).astype(acc)
+        query = query.reshape(batch, stop - start, heads, groups, dim)
+        logits = np.einsum("bthgd,bmhd->bthgm", query, summaries.astype(acc)).astype(acc)
+        position = np.asarray(positions)[:, start:stop, None, None]
+        current = position // block_size
+        complete = (position + 1) // block_size
+        visible = (blocks < complete[..., None])
+        masked = np.where(visible, logits, -np.inf)
+        peak = masked.max(-1, keepdims=True)
+        safe = np.where(np.isfinite(peak), peak, 0)
+        with np.errstate(divide="ignore"):
+            normalizer = (safe + np.log(np.exp(masked - safe).sum(-1, keepdims=True, dtype=acc))).astype(acc)
+        normalizer = np.where(complete[..., None] > 0, normalizer, acc(0))
+        forced = np.zeros(current.shape + (count,), bool)
+        if force_first:
+            forced |= blocks == 0
+        for recent in range(force_recent):
+            forced |= (current[..., None] >= recent) & (blocks == current[..., None] - recent)
+        valid = blocks <= current[..., None]
+        candidate = np.where(blocks < current[..., None], logits, -np.inf)
+        with np.errstate(over="ignore"):
+            probabilities = np.exp(candidate - normalizer).astype(acc)
+        probabilities = np.where(forced, acc(1), probabilities)
+        scores = probabilities.sum(-2, dtype=acc)
+        ids = np.where(valid[..., 0, :], blocks, -1)
+        ids = np.broadcast_to(ids, scores.shape).astype(np.int64)
+        out[:, start:stop] = streaming_topk(scores, ids, topk, width)
+        if trace is not None:
+            gaps[:, start:stop] = _boundary_gap(scores, topk)
+    if trace is not None:
+        trace["min_gap"] = gaps
+    return out
 
 
 # ----------------------------------------------------------------------------

@@ -11,7 +11,8 @@ It imports the reference package ``pisa`` from ``<root>/pisa`` and calls
 (mean_pooling.py:45-52), and the leaf scores of random candidate lists with
 the reference's ``block_scores`` / ``routing_masks``
 (top_k_pyramid_torch.py:48-80,114-120; the grouped_leaf_scores semantics of
-leaf_triton.py:144-232).  Inputs are regenerated from their seed by
+leaf_triton.py:144-232), and the flat BSA selection ``bsa_fn(...,
+backend="torch")`` (bsa.py:9-52, bsa_torch.py:63-106).  Inputs are regenerated from their seed by
 :func:`inputs` (torch's CPU generator, fp32 normal draws in q, k, v, dout
 order, then a cast), so the fixtures hold only outputs plus input checksums.
 The reference is not needed to *read* the fixtures.
@@ -92,6 +93,26 @@ LEAF_CASES = {
 }
 
 
+# Flat BSA selection (bsa_fn(..., backend="torch"), bsa.py:9-52 -> bsa_torch.py:63-106)
+# on the inputs of :func:`inputs`; ``C < 2K`` cases widen the comparison tile.
+BSA_CASES = {
+    "bsa_tail_f32": dict(B=2, N=200, T=200, Hq=4, Hkv=2, D=16, C=16, K=4, ff=True, fr=1,
+                         dtype="f32", seed=21),
+    "bsa_bf16_g4": dict(B=1, N=257, T=257, Hq=8, Hkv=2, D=64, C=16, K=8, ff=True, fr=2,
+                        dtype="bf16", seed=22),
+    "bsa_wide_tile": dict(B=1, N=700, T=700, Hq=2, Hkv=2, D=32, C=16, K=16, ff=False, fr=3,
+                          dtype="f32", seed=23),
+    "bsa_bench_g4": dict(B=1, N=2048, T=2048, Hq=16, Hkv=4, D=128, C=64, K=32, ff=True, fr=1,
+                         dtype="bf16", seed=24),
+    "bsa_decode_bf16": dict(B=3, N=1500, T=1, Hq=8, Hkv=2, D=64, C=32, K=8, ff=True, fr=1,
+                            dtype="bf16", seed=25),
+    "bsa_offsets": dict(B=2, N=1000, T=3, offset=[500, 997], Hq=4, Hkv=1, D=32, C=32, K=8, ff=True,
+                        fr=2, dtype="f32", seed=26),
+    "bsa_no_recent": dict(B=1, N=300, T=300, Hq=16, Hkv=1, D=32, C=32, K=8, ff=True, fr=0,
+                          dtype="bf16", seed=27),
+}
+
+
 def leaf_inputs(case):
     """Seeded q, k, candidates (distinct ids per row in [-2, blocks + 2)) and positions."""
     g = torch.Generator().manual_seed(case["seed"])
@@ -142,7 +163,18 @@ def main(root, which=None):
     from pisa.ops.flash_sparse_attn.top_k_pyramid import select_blocks
     from pisa.ops.flash_sparse_attn.top_k_pyramid.top_k_pyramid_torch import block_scores, routing_masks
 
+    from pisa.ops.flash_sparse_attn.bsa import bsa_fn
+
     torch.set_num_threads(max(1, torch.get_num_threads()))
+    for name, case in BSA_CASES.items():
+        if which and name not in which:
+            continue
+        q, k, _, _ = inputs(case)
+        ids = bsa_fn(q, k, case["C"], case["K"], query_offset=offset_arg(case), force_first=case["ff"],
+                     force_recent=case["fr"], backend="torch")
+        rec = {"q_sum": checksum(q), "k_sum": checksum(k), "ids": ids.numpy().astype(np.int16)}
+        np.savez_compressed(HERE / f"{name}.npz", **rec)
+        print(name, {k: v.shape for k, v in rec.items()})
     for name, case in LEAF_CASES.items():
         if which and name not in which:
             continue

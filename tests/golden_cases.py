@@ -5,7 +5,7 @@ from pathlib import Path
 import numpy as np
 import torch
 
-from make_golden import CASES, LEAF_CASES, inputs, leaf_inputs, offset_arg  # noqa: F401  (tests/golden on sys.path)
+from make_golden import BSA_CASES, CASES, LEAF_CASES, inputs, leaf_inputs, offset_arg  # noqa: F401  (tests/golden on sys.path)
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 
@@ -39,3 +39,16 @@ def leaf_case(name):
         np.testing.assert_allclose(got, rec[f"{key}_sum"], rtol=1e-12, atol=1e-9,
                                    err_msg=f"seeded {key} for {name} drifted from the fixture")
     return case, rec, (q, k, cand, positions)
+
+
+def bsa_case(name):
+    """(case, rec, (q, k) torch tensors) for a flat BSA selection fixture."""
+    case = BSA_CASES[name]
+    q, k, _, _ = inputs(case)
+    rec = load(name)
+    for key, t in (("q", q), ("k", k)):
+        x = t.to(torch.float64)
+        got = np.array([x.sum().item(), x.square().sum().item(), x.abs().max().item()])
+        np.testing.assert_allclose(got, rec[f"{key}_sum"], rtol=1e-12, atol=1e-9,
+                                   err_msg=f"seeded {key} for {name} drifted from the fixture")
+    return case, rec, (q, k)

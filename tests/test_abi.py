@@ -141,3 +141,32 @@ def test_caller_pyramid_tables_are_validated_without_gpu():
     # shallower than the routing depth without reaching a single node
     rc, msg = call([64, 32], 2, 2, 16)
     assert rc == _lib.ERR_INVALID and "fewer levels" in msg
+
+
+def test_bsa_entry_checks_run_on_the_host():
+    """pisa_bsa_select rejects bad arguments before any device work; workspace is the leaf means."""
+    from nlogn_pisa_b200 import _lib
+
+    lib = _lib.lib()
+    assert lib.pisa_bsa_workspace_bytes(1, 4096, 4, 64, _lib.BF16, 64, 0) == 64 * 4 * 64 * 2
+    assert lib.pisa_bsa_workspace_bytes(1, 4096, 4, 64, _lib.BF16, 64, 1) == 0
+    assert lib.pisa_bsa_workspace_bytes(0, 4096, 4, 64, _lib.BF16, 64, 0) == -1
+    # 32 query heads per KV head exceed the 16-row warp tile
+    rc = lib.pisa_bsa_select(None, 0, 0, 0, None, 0, 0, 0, None, 0, None, 0, _lib.BF16, 1, 64, 32, 1, 64, 64,
+                             16, 8, 1, 2, None, None, 0, None)
+    assert rc == _lib.ERR_UNSUPPORTED and "16 query heads" in lib.pisa_last_error().decode()
+    # last row (position 4095, block 255) needs block 0 plus 9 recent blocks: more than topk 8
+    rc = lib.pisa_bsa_select(None, 0, 0, 0, None, 0, 0, 0, None, 0, None, 0, _lib.BF16, 1, 4096, 4, 4, 64,
+                             4096, 16, 8, 1, 9, None, None, 0, None)
+    assert rc == _lib.ERR_INVALID and "required" in lib.pisa_last_error().decode()
+
+
+def test_bsa_required_block_count_matches_oracle():
+    import numpy as np
+
+    from nlogn_pisa_b200.selection import bsa_required_blocks
+
+    for pos in (0, 15, 16, 47, 48, 1000):
+        for ff in (True, False):
+            for fr in (0, 1, 2, 3, 5):
+                assert bsa_required_blocks(pos, 16, ff, fr) == O.bsa_required(np.array([[pos]]), 16, ff, fr)

@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 
 import pisa_oracle as O
-from golden_cases import CASES, LEAF_CASES, leaf_case, load, np_inputs, offset_arg
+from golden_cases import BSA_CASES, CASES, LEAF_CASES, bsa_case, leaf_case, load, np_inputs, offset_arg
 
 SELECT_CASES = [n for n in CASES if n != "config1"]
 
@@ -140,3 +140,40 @@ def test_leaf_scores_match_reference(name, method):
         fin = np.isfinite(want)
         assert fin.any() and (~fin).any()
         np.testing.assert_allclose(got[fin], want[fin], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", sorted(BSA_CASES))
+def test_bsa_selection_matches_reference(name):
+    """Flat BSA ids equal the reference's bsa_fn(backend="torch") in network order."""
+    case, rec, (q, k) = bsa_case(name)
+    dt = case["dtype"]
+    as_np = (lambda t: t.double().numpy()) if dt == "f64" else (lambda t: t.float().numpy())
+    positions = O.query_positions(case["B"], case["T"], case["N"], offset_arg(case))
+    trace = {}
+    got = O.bsa_select(as_np(q), as_np(k), case["C"], case["K"], positions, case["ff"], case["fr"], dt,
+                       trace=trace)
+    want = rec["ids"].astype(np.int64)
+    rows, exact, tie, bad = O.compare_selection(got, want, trace["min_gap"])
+    assert len(bad) == 0 and exact == rows
+    np.testing.assert_array_equal(got, want)
+
+
+def test_bsa_streaming_network_ties():
+    """Streaming top-K keeps the network's tie order on equal scores and -1 padding.
+
+    Known answer from the reference's streaming_topk (bsa_torch.py:30-60) on
+    these inputs: [[10, 7, 6, 9], [4, -1, -1, -1]].
+    """
+    scores = np.array([[1, 1, 1, 1, 0, 0, 2, 2, 1, 1, 3, 0], [0] * 12], np.float32)
+    ids = np.broadcast_to(np.arange(12), (2, 12)).copy()
+    ids[:, 11] = -1
+    ids[1, 5:] = -1
+    assert O.streaming_topk(scores, ids, 4, 8).tolist() == [[10, 7, 6, 9], [4, -1, -1, -1]]
+
+
+def test_bsa_required_blocks_raise():
+    q = np.zeros((1, 4, 1, 8), np.float32)
+    k = np.zeros((1, 64, 1, 8), np.float32)
+    positions = np.array([[60, 61, 62, 63]])
+    with pytest.raises(ValueError):
+        O.bsa_select(q, k, 8, 2, positions, True, 3)
