@@ -45,6 +45,29 @@ __device__ __forceinline__ float lg2_approx(float x) {
   return r;
 }
 
+// LSE of a node whose SUP (2 or 4) children all exist, base 2 as in the
+// general path (y = v * scale * log2 e): the largest child contributes
+// 2^0 = 1 exactly, so only the others take an exponential; a min/max network
+// splits the values into the maximum and the rest.
+template <int SUP>
+__device__ __forceinline__ float lse_full_node(const float (&v)[32], int j, float k2) {
+  const float ln2 = 0.6931471805599453f;
+  if constexpr (SUP == 4) {
+    const float h0 = fmaxf(v[j], v[j + 1]), l0 = fminf(v[j], v[j + 1]);
+    const float h1 = fmaxf(v[j + 2], v[j + 3]), l1 = fminf(v[j + 2], v[j + 3]);
+    const float m = fmaxf(h0, h1), o = fminf(h0, h1);
+    const float my = m * k2;
+    const float sum = 1.f + tc::ex2f(fmaf(l0, k2, -my)) + tc::ex2f(fmaf(l1, k2, -my)) + tc::ex2f(fmaf(o, k2, -my));
+    return ln2 * (my + lg2_approx(sum));
+  } else if constexpr (SUP == 2) {
+    const float m = fmaxf(v[j], v[j + 1]), o = fminf(v[j], v[j + 1]);
+    const float my = m * k2;
+    return ln2 * (my + lg2_approx(1.f + tc::ex2f(fmaf(o, k2, -my))));
+  } else {
+    return v[j] * k2 * ln2;
+  }
+}
+
 // Per CTA: the tile's query rows stay in shared memory while the level's
 // child chunks stream through a ring of kStages buffers: the TMA runs
 // kStages - 1 chunks ahead and the MMA of chunk c+1 (into the other of two
@@ -168,6 +191,8 @@ __global__ void __launch_bounds__(kThreads) dense_level_kernel(const __grid_cons
         float score;
         if (a.method == PISA_METHOD_PISA1) {
           score = v[j];
+        } else if (a.method == PISA_METHOD_PISA && cnt == SUP && SUP >= 2) {
+          score = lse_full_node<SUP>(v, j, k2);
         } else if (a.method == PISA_METHOD_PISA) {
           // base 2: LSE = ln2 * (max y + log2 sum 2^(y - max y)), y = v * scale * log2 e
           float m = v[j];

@@ -9,10 +9,18 @@
 // Layout: all levels live in one storage [B, total, H, D] (node stride H*D),
 // level l starting at node offset level_offsets[l].
 //
-// The leaf pass is HBM-bound: every key byte is read once with 16-byte
-// vector loads, one CTA per (leaf block, batch), each thread owning 16-byte
-// columns of the [H*D] row and walking the block's tokens with eight loads in
-// flight.  Upper levels are <1% of the traffic (a few MB at 256K tokens).
+// A full build is two launches.  pyramid_group_kernel reads every key byte
+// once (16-byte vector loads) and writes the leaves and the lowest k levels:
+// one CTA per (group of L = br^k <= 16 leaves, batch, KV head), one thread
+// per (leaf, 16-byte column of the head row) walking the leaf's tokens with
+// eight loads in flight, so no cross-thread reduction is needed; the group's
+// upper nodes are pooled from the rounded leaf means held in shared memory.
+// pyramid_top_kernel then pools the remaining levels per (batch, KV head),
+// launched with programmatic dependent launch so that its launch overlaps the
+// group pass (it waits on griddepcontrol.wait for the group grid to finish).
+// Incremental updates (first_token > 0) recompute only the touched leaves and
+// their ancestors with one launch per level (leaf_mean_kernel,
+// parent_mean_kernel).
 #include "internal.h"
 
 namespace pisa {
@@ -87,11 +95,195 @@ parent_mean_kernel(T* storage, int64_t sb, int64_t child_off, int child_len, int
   }
 }
 
+constexpr int kGroupThreads = 256;
+constexpr int kMaxGroupLeaves = 16;
+
+template <typename T>
+__global__ void __launch_bounds__(kGroupThreads)
+pyramid_group_kernel(const T* __restrict__ keys, int64_t sb, int64_t st, int64_t sh, int N, int H, int D, int C,
+                     int br, int L, int k_local, T* __restrict__ out, int64_t out_sb, const LevelTable lv) {
+  constexpr int V = Vec<T>::N;
+  // let the dependent top-level launch start; it waits for this grid to finish
+  asm volatile("griddepcontrol.launch_dependents;");
+  extern __shared__ float pool[];   // rounded node values of the group: levels 0..k_local, [node][D]
+  const int CH = D / V;             // 16-byte columns of one head row
+  const int TL = kGroupThreads / CH;
+  const int col = threadIdx.x % CH, lane_leaf = threadIdx.x / CH;
+  const int group = blockIdx.x;
+  const int b = blockIdx.y / H, h = blockIdx.y % H;
+  const int n_leaves = lv.size[0];
+  T* dst_base = out + b * out_sb + int64_t(h) * D + col * V;
+  const T* src_base = keys + b * sb + h * sh + col * V;
+  if (threadIdx.x < TL * CH) {
+    for (int li = lane_leaf; li < L; li += TL) {
+      const int leaf = group * L + li;
+      if (leaf >= n_leaves) break;
+      const int64_t t0 = int64_t(leaf) * C;
+      const int64_t t1 = min64(t0 + C, N);
+      float acc[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] = 0.f;
+      int64_t t = t0;
+      for (; t + 8 <= t1; t += 8) {
+        float x[8][V];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) load_vec<T>(src_base + (t + u) * st, x[u]);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+          for (int i = 0; i < V; ++i) acc[i] += x[u][i];
+      }
+      for (; t < t1; ++t) {
+        float x[V];
+        load_vec<T>(src_base + t * st, x);
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] += x[i];
+      }
+      const float count = float(t1 - t0);
+      float* keep = pool + li * D + col * V;
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        acc[i] = to_f32<T>(from_f32<T>(acc[i] / count));   // rounded as the stored level
+        keep[i] = acc[i];
+      }
+      store_vec<T>(dst_base + (lv.offset[0] + leaf) * int64_t(H) * D, acc);
+    }
+  }
+  // levels 1 .. k_local of this group from the rounded values below them
+  int child_base = 0, width = L;
+  for (int l = 1; l <= k_local; ++l) {
+    __syncthreads();
+    const int nodes = width / br;
+    const int parent_base = child_base + width;
+    const int first = group * nodes;               // global index of the group's first node at level l
+    for (int item = threadIdx.x; item < nodes * CH; item += kGroupThreads) {
+      const int j = item / CH, c = item % CH;
+      const int node = first + j;
+      if (node >= lv.size[l]) continue;
+      const int c0 = node * br, c1 = min(c0 + br, lv.size[l - 1]);
+      float acc[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] = 0.f;
+      for (int ch = c0; ch < c1; ++ch) {
+        const float* x = pool + (child_base + (ch - group * width)) * D + c * V;
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] += x[i];
+      }
+      const float count = float(c1 - c0);
+      float* keep = pool + (parent_base + j) * D + c * V;
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        acc[i] = to_f32<T>(from_f32<T>(acc[i] / count));
+        keep[i] = acc[i];
+      }
+      store_vec<T>(out + b * out_sb + (lv.offset[l] + node) * int64_t(H) * D + int64_t(h) * D + c * V, acc);
+    }
+    child_base = parent_base;
+    width = nodes;
+  }
+}
+
+// Levels first_level .. levels-1 of one (batch, KV head), level by level from
+// the stored level below (read through L2: written by the group grid or by
+// this CTA's previous level).
+template <typename T>
+__global__ void __launch_bounds__(kGroupThreads)
+pyramid_top_kernel(T* storage, int64_t sb, int H, int D, int br, int first_level, int levels, const LevelTable lv) {
+  constexpr int V = Vec<T>::N;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int CH = D / V;
+  const int b = blockIdx.x / H, h = blockIdx.x % H;
+  T* base = storage + b * sb + int64_t(h) * D;
+  const int64_t node_stride = int64_t(H) * D;
+  for (int l = first_level; l < levels; ++l) {
+    if (l > first_level) __syncthreads();
+    for (int item = threadIdx.x; item < lv.size[l] * CH; item += kGroupThreads) {
+      const int node = item / CH, c = item % CH;
+      const int c0 = node * br, c1 = min(c0 + br, lv.size[l - 1]);
+      float acc[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] = 0.f;
+      for (int ch = c0; ch < c1; ++ch) {
+        float x[V];
+        load_vec_cg<T>(base + (lv.offset[l - 1] + ch) * node_stride + c * V, x);
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] += x[i];
+      }
+      const float count = float(c1 - c0);
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] = acc[i] / count;
+      store_vec<T>(base + (lv.offset[l] + node) * node_stride + c * V, acc);
+    }
+  }
+}
+
+// Full build (first_token == 0) in two launches; *done stays false when the
+// shape is outside the group kernel (the per-level launches then run).
+template <typename T>
+static int pyramid_full(const void* keys, int64_t B, int64_t N, int64_t H, int64_t D, int64_t sb, int64_t st,
+                        int64_t sh, int64_t C, int64_t br, int64_t levels, void* storage, int64_t ssb,
+                        const int64_t* offs, cudaStream_t stream, bool* done) {
+  *done = false;
+  constexpr int V = Vec<T>::N;
+  const int64_t CH = D / V;
+  if (CH < 1 || CH > kGroupThreads || B * H > 65535) return PISA_OK;
+  int k = 0, L = 1;
+  while (L * br <= kMaxGroupLeaves && k + 1 < levels) { L *= int(br); ++k; }
+  if (k == 0) L = kMaxGroupLeaves;   // leaves only in this pass: any group size
+  LevelTable lv{};
+  int64_t n = (N + C - 1) / C;
+  for (int64_t l = 0; l < levels; ++l) {
+    lv.offset[l] = offs[l];
+    lv.size[l] = int32_t(n);
+    n = (n + br - 1) / br;
+  }
+  const int64_t groups = (int64_t(lv.size[0]) + L - 1) / L;
+  if (groups > INT32_MAX) return PISA_OK;
+  int pool_nodes = 0;
+  for (int l = 0, w = L; l <= k; ++l, w /= int(br)) pool_nodes += w;
+  const size_t smem = size_t(pool_nodes) * D * sizeof(float);
+  if (smem > 96 * 1024) return PISA_OK;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(pyramid_group_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(smem));
+    if (e != cudaSuccess) return fail_cuda(e, "pyramid smem attribute");
+  }
+  *done = true;
+  TimedLaunch timed(PISA_KERNEL_PYRAMID, stream);
+  dim3 grid(unsigned(groups), unsigned(B * H));
+  pyramid_group_kernel<T><<<grid, kGroupThreads, smem, stream>>>(
+      static_cast<const T*>(keys), sb, st, sh, int(N), int(H), int(D), int(C), int(br), L, k,
+      static_cast<T*>(storage), ssb, lv);
+  PISA_CHECK_LAUNCH();
+  if (k + 1 < levels) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned(B * H));
+    cfg.blockDim = dim3(kGroupThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, pyramid_top_kernel<T>, static_cast<T*>(storage), ssb, int(H),
+                                       int(D), int(br), k + 1, int(levels), lv);
+    if (e != cudaSuccess) return fail_cuda(e, "pyramid top levels");
+    PISA_CHECK_LAUNCH();
+  }
+  return PISA_OK;
+}
+
 template <typename T>
 static int pyramid_impl(const void* keys, int64_t B, int64_t N, int64_t H, int64_t D, int64_t sb,
                         int64_t st, int64_t sh, int64_t C, int64_t br, int64_t levels,
                         void* storage, int64_t ssb, const int64_t* offs, int64_t first_token,
                         cudaStream_t stream) {
+  if (first_token == 0 && levels <= kMaxLevels) {
+    bool done = false;
+    int rc = pyramid_full<T>(keys, B, N, H, D, sb, st, sh, C, br, levels, storage, ssb, offs, stream, &done);
+    if (rc || done) return rc;
+  }
   const int threads = 128;
   TimedLaunch timed(PISA_KERNEL_PYRAMID, stream);
   int64_t n = (N + C - 1) / C;

@@ -148,6 +148,31 @@ def test_pyramid_matches_reference(cuda_device):
                                    O.mean_pool(O.cast(keys.numpy(), tag), 7, tag), rtol=1e-6, atol=1e-6)
 
 
+@pytest.mark.parametrize("dtype,branching,n,heads,dim,block", [
+    (torch.bfloat16, 4, 32768, 8, 128, 64),   # the 32K benchmark keys (16-leaf groups, two local levels)
+    (torch.bfloat16, 2, 5000, 3, 64, 32),     # binary, ragged tail at every level
+    (torch.float16, 4, 3333, 2, 256, 16),     # wide rows
+    (torch.float32, 4, 2100, 4, 128, 64),     # fp32 rows (32 columns of 16 bytes)
+    (torch.bfloat16, 4, 700, 5, 40, 64),      # 5 columns per row: a partial lane of leaves
+])
+def test_pyramid_two_pass_build_matches_oracle(cuda_device, dtype, branching, n, heads, dim, block):
+    """Every level bit-exact against the oracle's rounding chain, keys strided in batch and tokens."""
+    import nlogn_pisa_b200 as P
+
+    g = torch.Generator().manual_seed(n + dim)
+    big = torch.randn(2, n + 5, heads + 1, dim, generator=g).to(dtype).cuda()
+    keys = big[:, 3:3 + n, 1:]                 # a view: batch, token and head strides of the parent
+    assert not keys.is_contiguous()
+    tag = {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}[dtype]
+    want = O.build_pyramid(keys.cpu().float().numpy(), block, tag, branching=branching)
+    got = P.build_pyramid(keys, block, branching=branching)
+    assert len(got) == len(want)
+    for level, (a, b) in enumerate(zip(got, want)):
+        np.testing.assert_array_equal(a.float().cpu().numpy(), b, err_msg=f"level {level}")
+    pooled = P.mean_pool(keys, block)
+    np.testing.assert_array_equal(pooled.float().cpu().numpy(), want[0])
+
+
 def test_strided_keys_and_pyramid_cache(cuda_device):
     """Decode through a PyramidCache (strided key views, incremental pyramid)."""
     import nlogn_pisa_b200 as P
