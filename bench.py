@@ -42,6 +42,11 @@ def parse_args():
     p.add_argument("--ref-rows", type=int, default=48, help="sampled rows per CPU worker (reference arm)")
     p.add_argument("--no-decode", action="store_true", help="skip the 128K-KV decode measurement")
     p.add_argument("--no-extra", action="store_true", help="skip the binary-pyramid and 256K lines")
+    p.add_argument("--only", choices=("decode", "training"),
+                   help="run one configuration alone and print its JSON object (profiling runs)")
+    p.add_argument("--decode-batch", type=int, default=64, help="sequences of the decode configuration")
+    p.add_argument("--decode-kv", type=int, default=131072, help="KV-cache tokens of the decode configuration")
+    p.add_argument("--train-tokens", type=int, default=16384, help="tokens per sequence of the training configuration")
     p.add_argument("--triton-comparator", action="store_true",
                    help="time the reference's own Triton selection (baseline/_ref) beside ours on this GPU "
                         "and print that comparison as one JSON line instead of the benchmark")
@@ -124,7 +129,7 @@ def decode_bench(args, device, world, peaks_hbm):
     from nlogn_pisa_b200 import _lib
     from nlogn_pisa_b200.selection import _c_array, level_sizes, routing_geometry  # noqa: F401
 
-    Bd, N, Hq, H, D, C, K, br = 64, 131072, 32, 8, 128, 64, 32, 4
+    Bd, N, Hq, H, D, C, K, br = args.decode_batch, args.decode_kv, 32, 8, 128, 64, 32, 4
     lib = _lib.lib()
     gen = torch.Generator(device=device).manual_seed(3)
     dt = torch.bfloat16
@@ -181,6 +186,7 @@ def decode_bench(args, device, world, peaks_hbm):
     _lib.kernel_timing(False)
     launches = (lib.pisa_launch_count() - launches0) / steps
     leaf_ms, _ = _lib.kernel_time("leaf_tiles")
+    other_us = {name: 1000.0 * _lib.kernel_time(name)[0] / steps for name in ("router", "leaf_final", "dense_level")}
     ms = max_over_ranks([sum(e[0].elapsed_time(e[2]) for e in ev) / steps,
                          sum(e[0].elapsed_time(e[1]) for e in ev) / steps,
                          sum(e[1].elapsed_time(e[2]) for e in ev) / steps], device, world)
@@ -220,7 +226,7 @@ def decode_bench(args, device, world, peaks_hbm):
     same = (torch.sort(ids_f, -1).values == torch.sort(ids, -1).values).all(-1).float().mean().item()
     fused_achieved = step_bytes / (fused_us * 1e-6) / 1e9
     del k, v, storage
-    return {"workload": "decode128k", "batch": Bd, "kv_tokens": N, "q_heads": Hq, "kv_heads": H, "head_dim": D,
+    return {"workload": f"decode{N // 1024}k", "batch": Bd, "kv_tokens": N, "q_heads": Hq, "kv_heads": H, "head_dim": D,
             "fused_kernel": {"us_per_step": fused_us, "us_per_token": fused_us / Bd, "launches_per_step": fused_launches,
                              "rows_with_same_ids_as_two_step_path": same,
                              "roofline": {"bound": "hbm", "achieved": fused_achieved, "unit": "GB/s",
@@ -229,6 +235,7 @@ def decode_bench(args, device, world, peaks_hbm):
             "schedule": os.environ.get("PISA_BENCH_DECODE_SCHEDULE", "fused"),
             "us_per_step": step_us, "us_per_token": step_us / Bd, "steps": steps,
             "select_us": select_us, "attention_us": attend_us, "leaf_tiles_us": 1000.0 * leaf_ms / steps,
+            "router_us": other_us["router"], "leaf_final_us": other_us["leaf_final"],
             "launches_per_step": launches,
             "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": step_bytes, "achieved": achieved,
                          "unit": "GB/s", "peak": peaks_hbm, "frac": achieved / peaks_hbm},
@@ -904,6 +911,13 @@ def main():
     tensor = peaks.get("bf16_tflops", 1590.0)
     src = "measured" if peaks else "fallback"
 
+    if args.only == "decode":
+        print(json.dumps(decode_bench(args, device, world, hbm)), flush=True)
+        return 0
+    if args.only == "training":
+        print(json.dumps(training_bench(device, world, rank, tensor, steps=args.steps, tokens=args.train_tokens)),
+              flush=True)
+        return 0
     w = workload
     clocks = ClockSampler(local)
     m = prefill_measure(w, device, rank, args.steps, args.warmup, world, sample_clocks=clocks)

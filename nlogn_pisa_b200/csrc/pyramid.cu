@@ -11,16 +11,19 @@
 //
 // A full build is two launches.  pyramid_group_kernel reads every key byte
 // once (16-byte vector loads) and writes the leaves and the lowest k levels:
-// one CTA per (group of L = br^k <= 16 leaves, batch, KV head), one thread
-// per (leaf, 16-byte column of the head row) walking the leaf's tokens with
-// eight loads in flight, so no cross-thread reduction is needed; the group's
-// upper nodes are pooled from the rounded leaf means held in shared memory.
+// one CTA per (group of L = br^k leaves, batch), one thread per (leaf,
+// 16-byte column of the whole node row, all KV heads) walking the leaf's
+// tokens with eight loads in flight, so warps read whole contiguous key rows
+// and no cross-thread reduction is needed; the group's upper nodes are pooled
+// from the rounded leaf means held in shared memory.
 // pyramid_top_kernel then pools the remaining levels per (batch, KV head),
 // launched with programmatic dependent launch so that its launch overlaps the
 // group pass (it waits on griddepcontrol.wait for the group grid to finish).
 // Incremental updates (first_token > 0) recompute only the touched leaves and
 // their ancestors with one launch per level (leaf_mean_kernel,
 // parent_mean_kernel).
+#include <algorithm>
+
 #include "internal.h"
 
 namespace pisa {
@@ -95,26 +98,32 @@ parent_mean_kernel(T* storage, int64_t sb, int64_t child_off, int child_len, int
   }
 }
 
-constexpr int kGroupThreads = 256;
-constexpr int kMaxGroupLeaves = 16;
+constexpr int kTopThreads = 1024;
+constexpr int kLeafThreads = 512;   // target threads of a group CTA (more when one row needs it)
 
+// Leaves and the lowest k_local levels of one group of L leaves of one batch
+// row: thread (leaf lane, 16-byte column of the whole [H*D] node row) sums a
+// leaf's tokens for its column, so every warp reads whole contiguous key rows
+// (all heads of a token are adjacent) and no cross-thread reduction is needed.
 template <typename T>
-__global__ void __launch_bounds__(kGroupThreads)
+__global__ void __launch_bounds__(1024)
 pyramid_group_kernel(const T* __restrict__ keys, int64_t sb, int64_t st, int64_t sh, int N, int H, int D, int C,
                      int br, int L, int k_local, T* __restrict__ out, int64_t out_sb, const LevelTable lv) {
   constexpr int V = Vec<T>::N;
   // let the dependent top-level launch start; it waits for this grid to finish
   asm volatile("griddepcontrol.launch_dependents;");
-  extern __shared__ float pool[];   // rounded node values of the group: levels 0..k_local, [node][D]
-  const int CH = D / V;             // 16-byte columns of one head row
-  const int TL = kGroupThreads / CH;
+  extern __shared__ float pool[];   // rounded node values of the group: levels 0..k_local, [node][H*D]
+  const int HD = H * D;
+  const int CH = HD / V;            // 16-byte columns of one node row
+  const int TL = blockDim.x / CH;   // leaf lanes
   const int col = threadIdx.x % CH, lane_leaf = threadIdx.x / CH;
   const int group = blockIdx.x;
-  const int b = blockIdx.y / H, h = blockIdx.y % H;
+  const int b = blockIdx.y;
   const int n_leaves = lv.size[0];
-  T* dst_base = out + b * out_sb + int64_t(h) * D + col * V;
-  const T* src_base = keys + b * sb + h * sh + col * V;
-  if (threadIdx.x < TL * CH) {
+  const int e = col * V, h = e / D, d = e - h * D;
+  const T* src_base = keys + b * sb + h * sh + d;
+  T* out_b = out + b * out_sb;
+  if (lane_leaf < TL) {
     for (int li = lane_leaf; li < L; li += TL) {
       const int leaf = group * L + li;
       if (leaf >= n_leaves) break;
@@ -140,13 +149,13 @@ pyramid_group_kernel(const T* __restrict__ keys, int64_t sb, int64_t st, int64_t
         for (int i = 0; i < V; ++i) acc[i] += x[i];
       }
       const float count = float(t1 - t0);
-      float* keep = pool + li * D + col * V;
+      float* keep = pool + li * HD + e;
 #pragma unroll
       for (int i = 0; i < V; ++i) {
         acc[i] = to_f32<T>(from_f32<T>(acc[i] / count));   // rounded as the stored level
         keep[i] = acc[i];
       }
-      store_vec<T>(dst_base + (lv.offset[0] + leaf) * int64_t(H) * D, acc);
+      store_vec<T>(out_b + (lv.offset[0] + leaf) * int64_t(HD) + e, acc);
     }
   }
   // levels 1 .. k_local of this group from the rounded values below them
@@ -156,8 +165,8 @@ pyramid_group_kernel(const T* __restrict__ keys, int64_t sb, int64_t st, int64_t
     const int nodes = width / br;
     const int parent_base = child_base + width;
     const int first = group * nodes;               // global index of the group's first node at level l
-    for (int item = threadIdx.x; item < nodes * CH; item += kGroupThreads) {
-      const int j = item / CH, c = item % CH;
+    for (int item = threadIdx.x; item < nodes * CH; item += blockDim.x) {
+      const int j = item / CH, c = item - j * CH;
       const int node = first + j;
       if (node >= lv.size[l]) continue;
       const int c0 = node * br, c1 = min(c0 + br, lv.size[l - 1]);
@@ -165,18 +174,18 @@ pyramid_group_kernel(const T* __restrict__ keys, int64_t sb, int64_t st, int64_t
 #pragma unroll
       for (int i = 0; i < V; ++i) acc[i] = 0.f;
       for (int ch = c0; ch < c1; ++ch) {
-        const float* x = pool + (child_base + (ch - group * width)) * D + c * V;
+        const float* x = pool + (child_base + (ch - group * width)) * HD + c * V;
 #pragma unroll
         for (int i = 0; i < V; ++i) acc[i] += x[i];
       }
       const float count = float(c1 - c0);
-      float* keep = pool + (parent_base + j) * D + c * V;
+      float* keep = pool + (parent_base + j) * HD + c * V;
 #pragma unroll
       for (int i = 0; i < V; ++i) {
         acc[i] = to_f32<T>(from_f32<T>(acc[i] / count));
         keep[i] = acc[i];
       }
-      store_vec<T>(out + b * out_sb + (lv.offset[l] + node) * int64_t(H) * D + int64_t(h) * D + c * V, acc);
+      store_vec<T>(out_b + (lv.offset[l] + node) * int64_t(HD) + c * V, acc);
     }
     child_base = parent_base;
     width = nodes;
@@ -187,7 +196,7 @@ pyramid_group_kernel(const T* __restrict__ keys, int64_t sb, int64_t st, int64_t
 // the stored level below (read through L2: written by the group grid or by
 // this CTA's previous level).
 template <typename T>
-__global__ void __launch_bounds__(kGroupThreads)
+__global__ void __launch_bounds__(kTopThreads)
 pyramid_top_kernel(T* storage, int64_t sb, int H, int D, int br, int first_level, int levels, const LevelTable lv) {
   constexpr int V = Vec<T>::N;
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -197,7 +206,7 @@ pyramid_top_kernel(T* storage, int64_t sb, int H, int D, int br, int first_level
   const int64_t node_stride = int64_t(H) * D;
   for (int l = first_level; l < levels; ++l) {
     if (l > first_level) __syncthreads();
-    for (int item = threadIdx.x; item < lv.size[l] * CH; item += kGroupThreads) {
+    for (int item = threadIdx.x; item < lv.size[l] * CH; item += blockDim.x) {
       const int node = item / CH, c = item % CH;
       const int c0 = node * br, c1 = min(c0 + br, lv.size[l - 1]);
       float acc[V];
@@ -225,11 +234,21 @@ static int pyramid_full(const void* keys, int64_t B, int64_t N, int64_t H, int64
                         const int64_t* offs, cudaStream_t stream, bool* done) {
   *done = false;
   constexpr int V = Vec<T>::N;
-  const int64_t CH = D / V;
-  if (CH < 1 || CH > kGroupThreads || B * H > 65535) return PISA_OK;
-  int k = 0, L = 1;
-  while (L * br <= kMaxGroupLeaves && k + 1 < levels) { L *= int(br); ++k; }
-  if (k == 0) L = kMaxGroupLeaves;   // leaves only in this pass: any group size
+  const int64_t CH = H * D / V;     // 16-byte columns of a node row
+  if (D % V || CH < 1 || CH > 1024 || B > 65535) return PISA_OK;
+  const int TL = int(std::max<int64_t>(1, kLeafThreads / CH));
+  // local levels: groups of L = br^k leaves with L <= TL (one leaf per lane)
+  // and the group's nodes within 64 KB of shared memory
+  int k = 0, L = 1, pool_nodes = 1;
+  while (k + 1 < levels && L * br <= TL && size_t(pool_nodes + L * br) * H * D * sizeof(float) <= 64 * 1024) {
+    L *= int(br);
+    pool_nodes = 0;
+    for (int w = L; w >= 1; w /= int(br)) pool_nodes += w;
+    ++k;
+  }
+  if (k == 0) { L = TL; pool_nodes = TL; }   // leaves only in this pass: one per lane
+  const size_t smem = size_t(pool_nodes) * H * D * sizeof(float);
+  if (smem > 96 * 1024) return PISA_OK;
   LevelTable lv{};
   int64_t n = (N + C - 1) / C;
   for (int64_t l = 0; l < levels; ++l) {
@@ -239,10 +258,6 @@ static int pyramid_full(const void* keys, int64_t B, int64_t N, int64_t H, int64
   }
   const int64_t groups = (int64_t(lv.size[0]) + L - 1) / L;
   if (groups > INT32_MAX) return PISA_OK;
-  int pool_nodes = 0;
-  for (int l = 0, w = L; l <= k; ++l, w /= int(br)) pool_nodes += w;
-  const size_t smem = size_t(pool_nodes) * D * sizeof(float);
-  if (smem > 96 * 1024) return PISA_OK;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(pyramid_group_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          int(smem));
@@ -250,15 +265,17 @@ static int pyramid_full(const void* keys, int64_t B, int64_t N, int64_t H, int64
   }
   *done = true;
   TimedLaunch timed(PISA_KERNEL_PYRAMID, stream);
-  dim3 grid(unsigned(groups), unsigned(B * H));
-  pyramid_group_kernel<T><<<grid, kGroupThreads, smem, stream>>>(
+  const dim3 grid(static_cast<unsigned>(groups), static_cast<unsigned>(B), 1u);
+  const int threads = int(std::min<int64_t>(1024, int64_t(TL) * CH));
+  pyramid_group_kernel<T><<<grid, threads, smem, stream>>>(
       static_cast<const T*>(keys), sb, st, sh, int(N), int(H), int(D), int(C), int(br), L, k,
       static_cast<T*>(storage), ssb, lv);
   PISA_CHECK_LAUNCH();
   if (k + 1 < levels) {
+    if (B * H > 65535) return fail(PISA_ERR_UNSUPPORTED, "batch x heads too large for the pyramid's top levels");
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(unsigned(B * H));
-    cfg.blockDim = dim3(kGroupThreads);
+    cfg.blockDim = dim3(kTopThreads);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
