@@ -13,7 +13,7 @@
 // once (16-byte vector loads) and writes the leaves and the lowest k levels:
 // one CTA per (group of L = br^k leaves, batch), one thread per (leaf,
 // 16-byte column of the whole node row, all KV heads) walking the leaf's
-// tokens with eight loads in flight, so warps read whole contiguous key rows
+// tokens with sixteen loads in flight, so warps read whole contiguous key rows
 // and no cross-thread reduction is needed; the group's upper nodes are pooled
 // from the rounded leaf means held in shared memory.
 // pyramid_top_kernel then pools the remaining levels per (batch, KV head),
@@ -99,14 +99,27 @@ parent_mean_kernel(T* storage, int64_t sb, int64_t child_off, int child_len, int
 }
 
 constexpr int kTopThreads = 1024;
-constexpr int kLeafThreads = 512;   // target threads of a group CTA (more when one row needs it)
+constexpr int kLeafThreads = 512;   // threads of a group CTA (wider node rows take the per-level launches)
+
+// acc[i] += element i of a raw 16-byte vector of T.
+template <typename T>
+__device__ __forceinline__ void add_raw(uint4 raw, float (&acc)[Vec<T>::N]) {
+  if constexpr (sizeof(T) == 4) {
+    acc[0] += __uint_as_float(raw.x); acc[1] += __uint_as_float(raw.y);
+    acc[2] += __uint_as_float(raw.z); acc[3] += __uint_as_float(raw.w);
+  } else {
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < Vec<T>::N; ++i) acc[i] += to_f32<T>(e[i]);
+  }
+}
 
 // Leaves and the lowest k_local levels of one group of L leaves of one batch
 // row: thread (leaf lane, 16-byte column of the whole [H*D] node row) sums a
 // leaf's tokens for its column, so every warp reads whole contiguous key rows
 // (all heads of a token are adjacent) and no cross-thread reduction is needed.
 template <typename T>
-__global__ void __launch_bounds__(1024)
+__global__ void __launch_bounds__(kLeafThreads)
 pyramid_group_kernel(const T* __restrict__ keys, int64_t sb, int64_t st, int64_t sh, int N, int H, int D, int C,
                      int br, int L, int k_local, T* __restrict__ out, int64_t out_sb, const LevelTable lv) {
   constexpr int V = Vec<T>::N;
@@ -133,21 +146,15 @@ pyramid_group_kernel(const T* __restrict__ keys, int64_t sb, int64_t st, int64_t
 #pragma unroll
       for (int i = 0; i < V; ++i) acc[i] = 0.f;
       int64_t t = t0;
-      for (; t + 8 <= t1; t += 8) {
-        float x[8][V];
+      // sixteen raw 16-byte loads in flight, summed in token order
+      for (; t + 16 <= t1; t += 16) {
+        uint4 raw[16];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) load_vec<T>(src_base + (t + u) * st, x[u]);
+        for (int u = 0; u < 16; ++u) raw[u] = __ldg(reinterpret_cast<const uint4*>(src_base + (t + u) * st));
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-#pragma unroll
-          for (int i = 0; i < V; ++i) acc[i] += x[u][i];
+        for (int u = 0; u < 16; ++u) add_raw<T>(raw[u], acc);
       }
-      for (; t < t1; ++t) {
-        float x[V];
-        load_vec<T>(src_base + t * st, x);
-#pragma unroll
-        for (int i = 0; i < V; ++i) acc[i] += x[i];
-      }
+      for (; t < t1; ++t) add_raw<T>(__ldg(reinterpret_cast<const uint4*>(src_base + t * st)), acc);
       const float count = float(t1 - t0);
       float* keep = pool + li * HD + e;
 #pragma unroll
@@ -235,7 +242,7 @@ static int pyramid_full(const void* keys, int64_t B, int64_t N, int64_t H, int64
   *done = false;
   constexpr int V = Vec<T>::N;
   const int64_t CH = H * D / V;     // 16-byte columns of a node row
-  if (D % V || CH < 1 || CH > 1024 || B > 65535) return PISA_OK;
+  if (D % V || CH < 1 || CH > kLeafThreads || B > 65535) return PISA_OK;
   const int TL = int(std::max<int64_t>(1, kLeafThreads / CH));
   // local levels: groups of L = br^k leaves with L <= TL (one leaf per lane)
   // and the group's nodes within 64 KB of shared memory
@@ -266,7 +273,7 @@ static int pyramid_full(const void* keys, int64_t B, int64_t N, int64_t H, int64
   *done = true;
   TimedLaunch timed(PISA_KERNEL_PYRAMID, stream);
   const dim3 grid(static_cast<unsigned>(groups), static_cast<unsigned>(B), 1u);
-  const int threads = int(std::min<int64_t>(1024, int64_t(TL) * CH));
+  const int threads = int(std::min<int64_t>(kLeafThreads, int64_t(TL) * CH));
   pyramid_group_kernel<T><<<grid, threads, smem, stream>>>(
       static_cast<const T*>(keys), sb, st, sh, int(N), int(H), int(D), int(C), int(br), L, k,
       static_cast<T*>(storage), ssb, lv);

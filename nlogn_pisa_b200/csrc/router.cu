@@ -31,6 +31,10 @@ namespace {
 constexpr int kThreads = 128;
 constexpr int kMaxWidth = 256;
 
+// 16-bit inputs score coarse levels with mma.sync (bf16 / fp16 operands)
+template <typename T>
+constexpr bool kMmaCoarse = std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value;
+
 template <int WP>
 __device__ __forceinline__ void network_step(float* sc, int* ids, int width, int K, int br,
                                              int level, int64_t pos, int C, int lane,
@@ -172,6 +176,34 @@ __device__ void decode_attend(const RouteArgs& a, const int* sel, const float* q
   }
 }
 
+// Per-row mma.sync scoring of a coarse level (defined with the warp router below).
+template <typename T, int KP>
+__device__ void row_level_scores(const RouteArgs& a, const uint4 (&q0)[KP], const uint4 (&q1)[KP],
+                                 int sid0, int sid1, int width, int level, int b, int h, int lane,
+                                 float* sc_out);
+template <typename T, int KP>
+__device__ __forceinline__ void load_q_frags(const RouteArgs& a, int b, int t, int h, int lane,
+                                             uint4 (&q0)[KP], uint4 (&q1)[KP]);
+
+// Coarse-level scores of the per-item router on the tensor cores: warp w
+// scores candidates 32w .. 32w+31 of the level (then 128 more per round)
+// with the row scorer's m16n8k16 MMAs over their child summaries; entries of
+// unscoreable candidates are left alone.
+template <typename T, int KP>
+__device__ void item_coarse_mma(const RouteArgs& a, const int* ids, const unsigned char* fl, bool identity,
+                                int width, int level, int b, int t, int h, int warp, int lane, float* sc) {
+  uint4 q0[KP], q1[KP];
+  load_q_frags<T, KP>(a, b, t, h, lane, q0, q1);
+  for (int base = warp * 32; base < width; base += kThreads) {
+    const int i = base + lane;
+    const int f = i < width ? fl[i] : 0;
+    const bool scoreable = (f & 1) && !(f & 2) && !identity;
+    const int sid = scoreable ? ids[i] : -1;
+    if (__ballot_sync(kFull, sid >= 0) == 0) continue;   // warp-uniform
+    row_level_scores<T, KP>(a, q0, q1, sid, -1, min(32, width - base), level, b, h, lane, sc + base);
+  }
+}
+
 template <typename T, int GMAX, bool ATTEND>
 __global__ void __launch_bounds__(kThreads, ATTEND ? 4 : 1) route_kernel(const RouteArgs a) {
   extern __shared__ __align__(16) float smem[];
@@ -249,8 +281,12 @@ __global__ void __launch_bounds__(kThreads, ATTEND ? 4 : 1) route_kernel(const R
       return;
     }
 
-    // fill values and thread-per-candidate scoring
+    // fill values and thread-per-candidate scoring (coarse levels of 16-bit
+    // inputs go to the tensor cores below instead)
     const bool warp_leaf = level == 0 && a.method != PISA_METHOD_PISA1 && a.dense_off[0] < 0;
+    const bool coarse_level = level > 0 || a.method == PISA_METHOD_PISA1;
+    const bool mma_level = kMmaCoarse<T> && coarse_level && !(dense_row && a.dense_off[level] >= 0) &&
+                           a.G <= 16 && (a.method == PISA_METHOD_PISA1 || a.br == 2 || a.br == 4) && !identity;
     for (int w = tid; w < width; w += kThreads) {
       const int f = fl[w];
       const bool valid = f & 1, forced = f & 2;
@@ -258,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, ATTEND ? 4 : 1) route_kernel(const R
       float v = 0.f;
       if (scoreable && !warp_leaf && dense_row && a.dense_off[level] >= 0) {
         v = dense_row[a.dense_off[level] + ids[w]];
-      } else if (scoreable && !warp_leaf) {
+      } else if (scoreable && !warp_leaf && !mma_level) {
         if (a.method == PISA_METHOD_PISA1) {
           v = coarse_score<T, GMAX>(a, summary + a.levels.offset[level] * node_stride, len, ids[w], qs);
         } else {
@@ -267,6 +303,14 @@ __global__ void __launch_bounds__(kThreads, ATTEND ? 4 : 1) route_kernel(const R
         }
       }
       sc[w] = !valid ? kNegFill : (forced ? kPosFill : v);
+    }
+    if constexpr (kMmaCoarse<T>) {
+      if (mma_level) {
+        __syncthreads();
+        if (a.D <= 64) item_coarse_mma<T, 2>(a, ids, fl, identity, width, level, b, t, h, warp, lane, sc);
+        else if (a.D <= 128) item_coarse_mma<T, 4>(a, ids, fl, identity, width, level, b, t, h, warp, lane, sc);
+        else item_coarse_mma<T, 8>(a, ids, fl, identity, width, level, b, t, h, warp, lane, sc);
+      }
     }
     if (warp_leaf) {
       __syncthreads();
