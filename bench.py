@@ -710,8 +710,8 @@ def training_bench(device, world, rank, tensor, steps=5, warmup=3, batch=4, toke
     keys = torch.clamp(pos[None, :, None, None] + 1 - ids_sel * cfg.block_size, 0, cfg.block_size)
     fwd_flops = torch.where(valid, keys, 0).sum().item() * 4 * D * (Hq // cfg.num_key_value_heads)
     bwd_flops = 2.5 * fwd_flops
-    return {"workload": "train_block16k", "value": world * batch * tokens / (ms / 1000.0), "unit": "tokens/s",
-            "ms_per_step": ms, "steps": steps, "batch_per_gpu": batch, "tokens": tokens, "loss": float(loss),
+    return {"workload": f"train_block{tokens // 1024}k", "value": world * batch * tokens / (ms / 1000.0), "unit": "tokens/s",
+            "ms_per_step": ms, "steps": steps, "batch_per_gpu": batch, "tokens": tokens, "loss": float(loss.detach()),
             "parallelism": f"dp{world} (DDP, NCCL all-reduce of gradients)" if world > 1 else "dp1",
             "scaling": "weak", "model": "1 LLaMA-style block: d 1024, Hq=Hkv=16, D 64, SwiGLU 2816, RMSNorm, "
                                           "RoPE 1e4 (fraction 0.5), pisa2, block 64, branching 4, top-K 16",
