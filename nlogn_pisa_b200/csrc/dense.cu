@@ -68,6 +68,32 @@ __device__ __forceinline__ float lse_full_node(const float (&v)[32], int j, floa
   }
 }
 
+// Sums each node score of one 32-column half over the G = 2^LG query-head
+// lanes of its token and stores it from one lane: a reduce-scatter by
+// shuffles (lane bit k keeps the upper or lower half of the remaining nodes
+// at stage k), so every head lane ends with NPT / G finished scores.  The
+// additions associate as the shuffle butterfly ((h0+h1)+(h2+h3))+... .
+template <int NPT, int LG>
+__device__ __forceinline__ void head_sum_store(float (&s)[NPT], int g, float* dst, bool live) {
+  int base = 0;
+#pragma unroll
+  for (int k = 0; k < LG; ++k) {
+    const int half = NPT >> (k + 1);
+    const bool hi = (g >> k) & 1;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float mine = hi ? s[half + i] : s[i];
+      const float other = hi ? s[i] : s[half + i];
+      s[i] = mine + __shfl_xor_sync(kFull, other, 1 << k);
+    }
+    base += hi ? half : 0;
+  }
+  if (live) {
+#pragma unroll
+    for (int i = 0; i < (NPT >> LG); ++i) dst[base + i] = s[i];
+  }
+}
+
 // Per CTA: the tile's query rows stay in shared memory while the level's
 // child chunks stream through a ring of kStages buffers: the TMA runs
 // kStages - 1 chunks ahead and the MMA of chunk c+1 (into the other of two
@@ -183,6 +209,21 @@ __global__ void __launch_bounds__(kThreads) dense_level_kernel(const __grid_cons
     for (int cc = 32 * half; cc < nc; cc += 64) {
       float v[32];
       tc::tmem_ld32(tmem + lane_base + bi * kChunk + cc, v);
+      if constexpr (SUP >= 2) {
+        // a complete half of LSE nodes with G in {2, 4, 8}: scores of every
+        // node, then one reduce-scatter over the head lanes
+        if (a.method == PISA_METHOD_PISA && cc + 32 <= nc && a.G >= 2 && a.G <= 8) {
+          constexpr int NPT = 32 / SUP;
+          float sc[NPT];
+#pragma unroll
+          for (int n = 0; n < NPT; ++n) sc[n] = lse_full_node<SUP>(v, n * SUP, k2);
+          float* dst = out + (c0 + cc) / SUP;
+          if (a.G == 2) head_sum_store<NPT, 1>(sc, g, dst, live);
+          else if (a.G == 4) head_sum_store<NPT, 2>(sc, g, dst, live);
+          else head_sum_store<NPT, 3>(sc, g, dst, live);
+          continue;
+        }
+      }
 #pragma unroll
       for (int j = 0; j < 32; j += SUP) {
         if (cc + j >= nc) break;                       // uniform across the warp
