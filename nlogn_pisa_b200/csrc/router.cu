@@ -1,6 +1,7 @@
 // K2: coarse-to-fine router (and, in the fused schedule, leaf scoring + top-K).
 //
-// One CTA of four warps routes one (batch, query token, KV head) item through
+// One CTA of four warps (up to sixteen in the fused decode kernel) routes one
+// (batch, query token, KV head) item through
 // levels top..0, as pyramid_select (pisa/pisa/ops/flash_sparse_attn/
 // top_k_pyramid/top_k_pyramid_torch.py:137-177):
 //   masks      valid = id>=0 & id*(C*b^l) <= pos; forced = first block or an
@@ -29,6 +30,10 @@ namespace pisa {
 namespace {
 
 constexpr int kThreads = 128;
+// the fused decode kernel with few items: sixteen warps per (sequence,
+// token, KV head), so that more candidate and selected key blocks are read
+// at once
+constexpr int kAttendThreads = 512;
 constexpr int kMaxWidth = 256;
 
 // 16-bit inputs score coarse levels with mma.sync (bf16 / fp16 operands)
@@ -74,12 +79,12 @@ __device__ __forceinline__ void network_step(float* sc, int* ids, int width, int
 // visible keys, causal at the row's position).  Warp w takes slots w, w+4,
 // ...; per chunk of 32 keys: logits with lane = key (q from shared memory),
 // online softmax per head, then P.V with lane = VPL value columns (the warp
-// reads each value row whole).  The four warps merge through shared memory.
-template <typename T, int GMAX, int VPL>
+// reads each value row whole).  The warps merge through shared memory.
+template <typename T, int GMAX, int VPL, int NT>
 __device__ void decode_attend(const RouteArgs& a, const int* sel, const float* qs, int b, int t, int h,
                               int64_t pos, float* scratch) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  constexpr int W = kThreads / 32;
+  constexpr int W = NT / 32;
   const int G = a.G, Dv = a.Dv;
   float* pw = scratch;                     // [W][G][32] probabilities of the current chunk
   float* mw = pw + W * G * 32;             // [W][G]
@@ -154,7 +159,7 @@ __device__ void decode_attend(const RouteArgs& a, const int* sel, const float* q
   }
   __syncthreads();
   T* op = static_cast<T*>(a.out) + ((int64_t(b) * a.T + t) * (int64_t(a.H) * G) + int64_t(h) * G) * Dv;
-  for (int i = tid; i < G * Dv; i += kThreads) {
+  for (int i = tid; i < G * Dv; i += NT) {
     const int g = i / Dv, d = i - g * Dv;
     float M = -INFINITY;
 #pragma unroll
@@ -189,12 +194,12 @@ __device__ __forceinline__ void load_q_frags(const RouteArgs& a, int b, int t, i
 // scores candidates 32w .. 32w+31 of the level (then 128 more per round)
 // with the row scorer's m16n8k16 MMAs over their child summaries; entries of
 // unscoreable candidates are left alone.
-template <typename T, int KP>
+template <typename T, int KP, int NT>
 __device__ void item_coarse_mma(const RouteArgs& a, const int* ids, const unsigned char* fl, bool identity,
                                 int width, int level, int b, int t, int h, int warp, int lane, float* sc) {
   uint4 q0[KP], q1[KP];
   load_q_frags<T, KP>(a, b, t, h, lane, q0, q1);
-  for (int base = warp * 32; base < width; base += kThreads) {
+  for (int base = warp * 32; base < width; base += NT) {
     const int i = base + lane;
     const int f = i < width ? fl[i] : 0;
     const bool scoreable = (f & 1) && !(f & 2) && !identity;
@@ -204,8 +209,8 @@ __device__ void item_coarse_mma(const RouteArgs& a, const int* ids, const unsign
   }
 }
 
-template <typename T, int GMAX, bool ATTEND>
-__global__ void __launch_bounds__(kThreads, ATTEND ? 4 : 1) route_kernel(const RouteArgs a) {
+template <typename T, int GMAX, bool ATTEND, int NT>
+__global__ void __launch_bounds__(NT, ATTEND ? kAttendThreads / NT : 1) route_kernel(const RouteArgs a) {
   extern __shared__ __align__(16) float smem[];
   float* qs = smem;                                    // [G][D]
   int* ids = reinterpret_cast<int*>(qs + a.G * a.D);   // [kMaxWidth]
@@ -224,12 +229,12 @@ __global__ void __launch_bounds__(kThreads, ATTEND ? 4 : 1) route_kernel(const R
   const int64_t pos = a.positions ? a.positions[int64_t(b) * a.T + t] : a.pos_offset + t;
 
   const T* qp = static_cast<const T*>(a.q) + b * a.q_sb + t * a.q_st + int64_t(h) * a.G * a.q_sh;
-  for (int e = tid; e < a.G * a.D; e += kThreads) {
+  for (int e = tid; e < a.G * a.D; e += NT) {
     const int g = e / a.D, d = e % a.D;
     qs[e] = to_f32<T>(qp[g * a.q_sh + d]);
   }
   int width = a.first_width;
-  for (int w = tid; w < width; w += kThreads) ids[w] = w;
+  for (int w = tid; w < width; w += NT) ids[w] = w;
   const T* summary = static_cast<const T*>(a.summary) + b * a.s_sb + int64_t(h) * a.D;
   const T* key_base = static_cast<const T*>(a.keys) + b * a.k_sb + int64_t(h) * a.k_sh;
   const int64_t node_stride = int64_t(a.H) * a.D;
@@ -242,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, ATTEND ? 4 : 1) route_kernel(const R
 
   for (int level = a.top; level >= 0; --level) {
     const int len = a.levels.size[level];
-    for (int w = tid; w < width; w += kThreads) {
+    for (int w = tid; w < width; w += NT) {
       int id = ids[w];
       if (id >= len) id = -1;
       ids[w] = id;
@@ -272,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, ATTEND ? 4 : 1) route_kernel(const R
       // Leaf candidates with their masks: bit0 valid, bit1 forced, bit2 scoreable.
       int32_t* dst = a.candidates + int64_t(item) * a.W0;
       uint8_t* fdst = a.flags + int64_t(item) * a.W0;
-      for (int w = tid; w < width; w += kThreads) {
+      for (int w = tid; w < width; w += NT) {
         const int f = fl[w];
         const bool scoreable = (f & 1) && !(f & 2) && !identity;
         dst[w] = ids[w];
@@ -287,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, ATTEND ? 4 : 1) route_kernel(const R
     const bool coarse_level = level > 0 || a.method == PISA_METHOD_PISA1;
     const bool mma_level = kMmaCoarse<T> && coarse_level && !(dense_row && a.dense_off[level] >= 0) &&
                            a.G <= 16 && (a.method == PISA_METHOD_PISA1 || a.br == 2 || a.br == 4) && !identity;
-    for (int w = tid; w < width; w += kThreads) {
+    for (int w = tid; w < width; w += NT) {
       const int f = fl[w];
       const bool valid = f & 1, forced = f & 2;
       const bool scoreable = valid && !forced && !identity;
@@ -307,14 +312,14 @@ __global__ void __launch_bounds__(kThreads, ATTEND ? 4 : 1) route_kernel(const R
     if constexpr (kMmaCoarse<T>) {
       if (mma_level) {
         __syncthreads();
-        if (a.D <= 64) item_coarse_mma<T, 2>(a, ids, fl, identity, width, level, b, t, h, warp, lane, sc);
-        else if (a.D <= 128) item_coarse_mma<T, 4>(a, ids, fl, identity, width, level, b, t, h, warp, lane, sc);
-        else item_coarse_mma<T, 8>(a, ids, fl, identity, width, level, b, t, h, warp, lane, sc);
+        if (a.D <= 64) item_coarse_mma<T, 2, NT>(a, ids, fl, identity, width, level, b, t, h, warp, lane, sc);
+        else if (a.D <= 128) item_coarse_mma<T, 4, NT>(a, ids, fl, identity, width, level, b, t, h, warp, lane, sc);
+        else item_coarse_mma<T, 8, NT>(a, ids, fl, identity, width, level, b, t, h, warp, lane, sc);
       }
     }
     if (warp_leaf) {
       __syncthreads();
-      for (int w = warp; w < width; w += kThreads / 32) {
+      for (int w = warp; w < width; w += NT / 32) {
         const int f = fl[w];
         const bool scoreable = (f & 1) && !(f & 2) && !identity;
         if (scoreable) {
@@ -344,12 +349,12 @@ __global__ void __launch_bounds__(kThreads, ATTEND ? 4 : 1) route_kernel(const R
     // arrays (the launcher admits G * Dv / 32 <= 64 accumulators per lane)
     float* scratch = reinterpret_cast<float*>(fl + ((kMaxWidth + 15) / 16) * 16);
     switch (a.Dv / 32) {
-      case 2: decode_attend<T, GMAX, 2>(a, ids, qs, b, t, h, pos, scratch); break;
+      case 2: decode_attend<T, GMAX, 2, NT>(a, ids, qs, b, t, h, pos, scratch); break;
       case 4:
-        if constexpr (GMAX <= 16) decode_attend<T, GMAX, 4>(a, ids, qs, b, t, h, pos, scratch);
+        if constexpr (GMAX <= 16) decode_attend<T, GMAX, 4, NT>(a, ids, qs, b, t, h, pos, scratch);
         break;
       default:
-        if constexpr (GMAX <= 8) decode_attend<T, GMAX, 8>(a, ids, qs, b, t, h, pos, scratch);
+        if constexpr (GMAX <= 8) decode_attend<T, GMAX, 8, NT>(a, ids, qs, b, t, h, pos, scratch);
         break;
     }
   }
@@ -725,16 +730,16 @@ __global__ void __launch_bounds__(128, (KP > 0 && KP <= 4) ? 6 : 1) route_warp_k
   }
 }
 
-template <typename T, int GMAX>
-int launch_route(const RouteArgs& a, cudaStream_t stream) {
+template <typename T, int GMAX, bool ATTEND, int NT>
+int launch_route_nt(const RouteArgs& a, cudaStream_t stream) {
   size_t smem = size_t(a.G) * a.D * sizeof(float) + kMaxWidth * (2 * sizeof(int) + 1);
-  if (a.attend) {
+  if (ATTEND) {
     // fused decode attention: probabilities, per-warp (m, l) and partial outputs
-    const int W = kThreads / 32;
+    const int W = NT / 32;
     smem = size_t(a.G) * a.D * sizeof(float) + kMaxWidth * 2 * sizeof(int) + (kMaxWidth + 15) / 16 * 16 +
            sizeof(float) * (size_t(W) * a.G * 32 + 2 * W * a.G + size_t(W) * a.G * a.Dv);
   }
-  auto kernel = a.attend ? route_kernel<T, GMAX, true> : route_kernel<T, GMAX, false>;
+  auto kernel = route_kernel<T, GMAX, ATTEND, NT>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return fail_cuda(e, "route smem attribute");
@@ -742,9 +747,26 @@ int launch_route(const RouteArgs& a, cudaStream_t stream) {
   const int64_t items = int64_t(a.B) * a.t_count * a.H;
   if (items == 0) return PISA_OK;
   TimedLaunch timed(PISA_KERNEL_ROUTER, stream);
-  kernel<<<unsigned(items), kThreads, smem, stream>>>(a);
+  kernel<<<unsigned(items), NT, smem, stream>>>(a);
   PISA_CHECK_LAUNCH();
   return PISA_OK;
+}
+
+// The router keeps four warps per item; the fused decode kernel takes more
+// warps per item when there are few items (a CTA's leaf scoring and attention
+// are latency bound, so more warps read more key blocks at once), four when
+// the items fill the GPU (fewer, wider CTAs would leave items waiting for a
+// second wave: at 512 items sixteen warps measured 911 us against 742 us,
+// at 128 items 219 us against 548 us).
+template <typename T, int GMAX>
+int launch_route(const RouteArgs& a, cudaStream_t stream) {
+  if (!a.attend) return launch_route_nt<T, GMAX, false, kThreads>(a, stream);
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t items = int64_t(a.B) * a.t_count * a.H;
+  if (items <= sms) return launch_route_nt<T, GMAX, true, kAttendThreads>(a, stream);
+  if (items <= 2 * int64_t(sms)) return launch_route_nt<T, GMAX, true, kAttendThreads / 2>(a, stream);
+  return launch_route_nt<T, GMAX, true, kThreads>(a, stream);
 }
 
 template <typename T>
