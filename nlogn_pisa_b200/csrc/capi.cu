@@ -667,7 +667,11 @@ int pisa_leaf_scores(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, co
 namespace pisa {
 
 // Workspace layout of the bucketed tensor-core attention forward (one token
-// chunk at a time; the partials of a chunk are bounded to about 4 GiB: 12288-token chunks at the benchmark shape).
+// chunk at a time; the partials of a chunk are bounded to kAttnPartialBudget).
+// 16 GiB takes the 32K benchmark sequence in one chunk (about 10 GB of
+// partials) and the 256K one in six: fewer bucketing passes and tile-kernel
+// tails than 4 GiB chunks, on a GPU with 180 GB of HBM.
+constexpr int64_t kAttnPartialBudget = int64_t(16) << 30;
 struct AttnPlan {
   bool tc = false;
   int64_t TW = 4096, chunk = 0, NB = 0, RT = 0, num_buckets = 0, capacity = 0;
@@ -702,7 +706,7 @@ static AttnPlan plan_attn(int64_t B, int64_t Tq, int64_t Hq, int64_t H, int64_t 
   // 202 us against 319 us per 64-sequence decode step at 128K)
   if (!p.tc) return p;
   const int64_t per_token = H * S * G * (Dv * elem_size(dtype) + 8) * 9 / 8;
-  const int64_t fit = ((int64_t(1) << 32) / per_token) / p.TW * p.TW;
+  const int64_t fit = (kAttnPartialBudget / per_token) / p.TW * p.TW;
   p.chunk = std::min<int64_t>(Tq, std::max<int64_t>(p.TW, fit));
   p.NB = (N + C - 1) / C;
   p.RT = 128 / G;
