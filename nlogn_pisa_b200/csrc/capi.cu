@@ -669,7 +669,7 @@ namespace pisa {
 // Workspace layout of the bucketed tensor-core attention forward (one token
 // chunk at a time; the partials of a chunk are bounded to kAttnPartialBudget).
 // 16 GiB takes the 32K benchmark sequence in one chunk (about 10 GB of
-// partials) and the 256K one in six: fewer bucketing passes and tile-kernel
+// partials) and the 256K one in five: fewer bucketing passes and tile-kernel
 // tails than 4 GiB chunks, on a GPU with 180 GB of HBM.
 constexpr int64_t kAttnPartialBudget = int64_t(16) << 30;
 struct AttnPlan {

@@ -368,3 +368,42 @@ def test_tensor_core_attention_many_tiles_per_cta_poisoned_workspace(cuda_device
                                             positions=pos, causal=False)
         np.testing.assert_allclose(out.float().cpu().numpy(), want, rtol=0, atol=2e-2)
         np.testing.assert_allclose(lse.cpu().numpy(), want_lse, rtol=0, atol=1e-3)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [
+    # B, T, N, Hq, H, D, S, causal, per-batch offsets
+    (3, 1, 3000, 32, 8, 128, 32, True, False),   # decode step, 4 query heads per KV head
+    (2, 5, 1337, 16, 2, 64, 12, True, True),     # 8 query heads per KV head, ragged tail
+    (2, 3, 900, 2, 2, 128, 7, True, False),      # one query head per KV head
+    (1, 40, 700, 4, 2, 64, 9, False, False),     # non-causal, two query heads per KV head
+])
+def test_ring_gather_attention_matches_oracle(cuda_device, dtype, shape):
+    """The ring-staged gather (short query runs, block size 64, D in {64, 128},
+    1/2/4/8 query heads per KV head) on arbitrary indices: -1, duplicates,
+    blocks past the causal edge or past N, per-batch query positions; output
+    and log-sum-exp against the oracle."""
+    from nlogn_pisa_b200.attention import attention_forward
+
+    B, T, N, Hq, H, D, S, causal, per_batch = shape
+    C = 64
+    g = torch.Generator().manual_seed(sum(shape[:7]))
+    q = torch.randn(B, T, Hq, D, generator=g).to(dtype)
+    k = torch.randn(B, N, H, D, generator=g).to(dtype)
+    v = torch.randn(B, N, H, D, generator=g).to(dtype)
+    blocks = -(-N // C)
+    ids = torch.randint(-1, blocks + 1, (B, T, H, S), generator=g)
+    ids[..., 1] = ids[..., 0]                     # duplicates count twice
+    ids[..., 2] = blocks - 1                      # the ragged last block
+    if per_batch:
+        offsets = [N - T - 200 * b for b in range(B)]
+        pos = O.query_positions(B, T, N, offsets)
+        positions = torch.from_numpy(np.ascontiguousarray(pos)).cuda()
+    else:
+        pos = O.query_positions(B, T, N, N - T)
+        positions = None
+    out, lse = attention_forward(q.cuda(), k.cuda(), v.cuda(), ids.cuda(), C, D ** -0.5, positions, N - T, causal)
+    want, want_lse = O.sparse_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), ids.numpy(), C,
+                                        positions=pos, causal=causal)
+    np.testing.assert_allclose(out.float().cpu().numpy(), want, rtol=0, atol=2e-2)
+    np.testing.assert_allclose(lse.cpu().numpy(), want_lse, rtol=0, atol=1e-3)
