@@ -507,7 +507,10 @@ def stage_report(m, hbm, tensor):
     return out
 
 
-def e2e_prefill(w, tensors, device, world, steps):
+E2E_CUTS = (1 / 16, 1 / 4, 1 / 2, 3 / 4, 15 / 16)
+
+
+def e2e_prefill(w, tensors, device, world, steps, cuts=E2E_CUTS):
     """The same step end to end through the public API with pinned host buffers,
     as an incremental prefill: token chunks of the sequence are copied in on
     one stream while earlier chunks are selected and attended on the compute
@@ -527,7 +530,7 @@ def e2e_prefill(w, tensors, device, world, steps):
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     # short first and last chunks (the copy in of the first and the copy out
     # of the last are not overlapped with compute), long chunks between
-    cuts = sorted({0, N} | {min(N, int(N * f) // C * C) for f in (1 / 16, 1 / 4, 1 / 2, 3 / 4, 15 / 16)})
+    cuts = sorted({0, N} | {min(N, int(N * f) // C * C) for f in cuts})
     bounds = [(a, b) for a, b in zip(cuts[:-1], cuts[1:]) if b > a]
     ev_in = [torch.cuda.Event() for _ in bounds]
     ev_out = [torch.cuda.Event() for _ in bounds]

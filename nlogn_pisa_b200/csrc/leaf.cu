@@ -304,8 +304,11 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
       const int dst = r < g.RT ? s_dst[it & 7][r] : -1;
       (void)tile;
       const uint32_t acc = tmem + lane_base + a * NK;
-      int j_first = j_begin;
-      if (kEpiGroups < 4 && g.C == 64 && g.method == PISA_METHOD_PISA && j_end - j_begin >= 2 &&
+      // a warp whose 32 rows hold no request (the tail of a bucket's last
+      // tile; decode tiles carry only G rows) has no scores to compute
+      const bool live = __any_sync(kFull, dst >= 0);
+      int j_first = live ? j_begin : j_end;
+      if (live && kEpiGroups < 4 && g.C == 64 && g.method == PISA_METHOD_PISA && j_end - j_begin >= 2 &&
           (int64_t(p) * g.br + j_begin + 2) * 64 <= g.N) {
         // two full 64-key children at once: both TMEM loads in flight, then the
         // two max / exponential chains interleaved
