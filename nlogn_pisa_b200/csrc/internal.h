@@ -138,6 +138,7 @@ struct GroupArgs {
   int64_t* out_ids;
   int* status;
   int skip_final;     // 1: stop after the tile kernel (scores only, no top-K)
+  int kbufs;          // key buffers of the tile kernel (set by grouped_leaf): 2 pairs with 2 query stages
 };
 
 int grouped_leaf(const GroupArgs& g, int dtype, cudaStream_t stream);

@@ -110,7 +110,7 @@ constexpr int kPipeThreads = (kMmaWarp + 1) * 32;
 #endif
 constexpr int kPolyPairs = PISA_LEAF_POLY_PAIRS;
 
-template <typename T>
+template <typename T, int KB>
 __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_constant__ GroupArgs g) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -118,7 +118,13 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
   const int chunks = Dp / 64;                // 128-byte K chunks per row
   const int NK = g.br * g.C;                 // keys per family = MMA N
   const int q_stage_bytes = chunks * 128 * 128;
-  uint8_t* Ks = smem + kStages * q_stage_bytes;    // [chunks][NK][128 B]
+  // query stages: 3, or 2 with two key buffers (decode-like runs of one tile
+  // per family, whose next keys then load while the current tile is scored)
+  constexpr int nst = KB == 2 ? 2 : kStages;
+  auto stage_of = [](int i) { return i % nst; };
+  auto round_of = [](int i) { return i / nst; };
+  uint8_t* Ks = smem + nst * q_stage_bytes;        // kbufs x [chunks][NK][128 B]
+  const uint32_t kbuf_bytes = uint32_t(chunks) * NK * 128;
   __shared__ uint64_t full_q[kStages], empty_q[kStages], full_acc[2], empty_acc[2];
   __shared__ uint32_t tmem_slot;
   __shared__ int s_fail;
@@ -126,7 +132,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
   // most kStages tiles ahead of the MMAs and they at most two ahead of the
   // epilogue, so slot it%8 is free again when tile it is produced
   __shared__ uint64_t meta_full[8];
-  __shared__ int s_dst[8][128], s_fam[8];
+  __shared__ int s_dst[8][128], s_fam[8], s_kb[8];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int total = *g.total_tiles;
@@ -142,7 +148,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
   const int first = tile_of(0);
 
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < nst; ++i) {
       // one cp.async arrival per producer thread + the key arrival of the first producer warp
       tc::mbar_init(&full_q[i], kLoadWarps * 32 + 1);
       tc::mbar_init(&empty_q[i], 1);
@@ -179,7 +185,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
     const int lgS = 31 - __clz(Dp / 8);
     const int nseg = 1 << lgS, dsegs = g.D / 8;
     const T* qbase = static_cast<const T*>(g.q);
-    int cur_key = -1;
+    int cur_key = -1, kb = 0;
+    int last_use0 = -1, last_use1 = -1;   // last tile that reads each key buffer
     // request of this lane's row in tile `it` (family coordinates, source
     // row, score slot), decoded one tile ahead while the previous tile's
     // copies drain
@@ -208,7 +215,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
       req_n = g.tile_req[int64_t(tile_of(1)) * g.RT + j];
     }
     for (int it = 0; it < ntiles; ++it) {
-      const int s = it % kStages, rnd = it / kStages;
+      const int s = stage_of(it), rnd = round_of(it);
       if (!tc::mbar_wait(&empty_q[s], (rnd & 1) ^ 1)) { s_fail = 1; break; }
       // rows of empty request slots are left as they are (their scores are
       // never written); dimensions past D are zero-filled
@@ -231,18 +238,27 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
       if (pw == 0) {
         const int kkey = (b * g.H + h) * g.NP + p;
         if (kkey != cur_key) {
-          // the previous tile's MMA must be done before its keys are replaced
-          if (it > 0 && !tc::mbar_wait(&empty_q[(it - 1) % kStages], ((it - 1) / kStages) & 1)) { s_fail = 1; break; }
+          // the last tile that read the buffer being refilled must have
+          // finished its MMAs; tiles up to it - nst are (the stage wait
+          // above), and a later one is at most one phase ahead on its stage
+          const int nb = KB == 2 ? kb ^ 1 : 0;
+          const int lu = nb ? last_use1 : last_use0;
+          if (lu >= 0 && lu > it - nst &&
+              !tc::mbar_wait(&empty_q[stage_of(lu)], round_of(lu) & 1)) { s_fail = 1; break; }
           if (lane < chunks)
-            tc::tma_load_4d(ks_addr + lane * NK * 128, &g.tm_k, lane * 64, h, p * NK, b, &full_q[s]);
-          bytes = uint32_t(chunks) * NK * 128;
+            tc::tma_load_4d(ks_addr + nb * kbuf_bytes + lane * NK * 128, &g.tm_k, lane * 64, h, p * NK, b,
+                            &full_q[s]);
+          bytes = kbuf_bytes;
           cur_key = kkey;
+          kb = nb;
         }
+        if (kb) last_use1 = it; else last_use0 = it;
       }
       __syncwarp();
       if (lane == 0) {
         if (pw == 0) {
           s_fam[slot] = p;
+          s_kb[slot] = kb;
           tc::mbar_arrive_expect_tx(&full_q[s], bytes);
         }
         tc::mbar_arrive(&meta_full[slot]);
@@ -261,21 +277,22 @@ __global__ void __launch_bounds__(kPipeThreads, 1) leaf_tc_kernel(const __grid_c
     // ---------------- MMA issue ----------------
     if (lane == 0) {
       for (int it = 0; it < ntiles; ++it) {
-        const int s = it % kStages, a = nacc == 2 ? (it & 1) : 0;
+        const int s = stage_of(it), a = nacc == 2 ? (it & 1) : 0;
         const int ra = nacc == 2 ? (it >> 1) : it;
-        if (!tc::mbar_wait(&full_q[s], (it / kStages) & 1)) { s_fail = 1; break; }
+        if (!tc::mbar_wait(&full_q[s], round_of(it) & 1)) { s_fail = 1; break; }
         if (!tc::mbar_wait(&empty_acc[a], (ra & 1) ^ 1)) { s_fail = 1; break; }
         tc::fence_async_smem();
         tc::fence_after_sync();
         const uint32_t acc = tmem + a * NK;
         const uint32_t qa = qs_addr + s * q_stage_bytes;
+        const uint32_t kbase = KB == 2 ? ks_addr + uint32_t(s_kb[it & 7]) * kbuf_bytes : ks_addr;
         for (int n0 = 0; n0 < NK; n0 += 256) {
           const int n = min(256, NK - n0);
           const uint32_t idesc = tc::idesc_f16(128, n, g.bf16);
           for (int ks = 0; ks < Dp / 16; ++ks) {
             const int ch = ks >> 2, off = (ks & 3) * 32;
             tc::mma_f16(acc + n0, tc::desc_sw128(qa + ch * 128 * 128 + off),
-                        tc::desc_sw128(ks_addr + ch * NK * 128 + n0 * 128 + off), idesc, ks > 0);
+                        tc::desc_sw128(kbase + ch * NK * 128 + n0 * 128 + off), idesc, ks > 0);
           }
         }
         tc::mma_commit(&full_acc[a]);
@@ -519,8 +536,15 @@ int grouped_leaf(const GroupArgs& args, int dtype, cudaStream_t stream) {
   PISA_CHECK_LAUNCH();
 
   const int chunks = g.Dp / 64;
-  const size_t smem = size_t(chunks) * 128 * (kStages * 128 + g.br * g.C) + 1024;
-  auto kernel = dtype == PISA_BF16 ? leaf_tc_kernel<__nv_bfloat16> : leaf_tc_kernel<__half>;
+  // Two key buffers (and two query stages) when a query run is too short to
+  // give a family more than about one tile (decode and short chunks): the
+  // next family's keys then load while the current tile is scored.  Prefill
+  // keeps one key buffer behind three query stages.
+  const size_t smem2 = size_t(chunks) * 128 * (2 * 128 + 2 * g.br * g.C) + 1024;
+  g.kbufs = (g.T < 64 && smem2 <= size_t(200) * 1024) ? 2 : 1;
+  const size_t smem = g.kbufs == 2 ? smem2 : size_t(chunks) * 128 * (kStages * 128 + g.br * g.C) + 1024;
+  auto kernel = dtype == PISA_BF16 ? (g.kbufs == 2 ? leaf_tc_kernel<__nv_bfloat16, 2> : leaf_tc_kernel<__nv_bfloat16, 1>)
+                                   : (g.kbufs == 2 ? leaf_tc_kernel<__half, 2> : leaf_tc_kernel<__half, 1>);
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return fail_cuda(e, "leaf smem attribute");
   {
