@@ -209,8 +209,11 @@ __device__ void item_coarse_mma(const RouteArgs& a, const int* ids, const unsign
   }
 }
 
+// Without the fused attention and with G <= 4 the kernel is held to four CTAs
+// per SM (128 registers): the 512 items of a 64-sequence decode step then run
+// in one wave (104 -> 66 us for their coarse levels).
 template <typename T, int GMAX, bool ATTEND, int NT>
-__global__ void __launch_bounds__(NT, ATTEND ? kAttendThreads / NT : 1) route_kernel(const RouteArgs a) {
+__global__ void __launch_bounds__(NT, ATTEND ? kAttendThreads / NT : (GMAX <= 4 ? 4 : 1)) route_kernel(const RouteArgs a) {
   extern __shared__ __align__(16) float smem[];
   float* qs = smem;                                    // [G][D]
   int* ids = reinterpret_cast<int*>(qs + a.G * a.D);   // [kMaxWidth]
